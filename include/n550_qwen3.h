@@ -1,0 +1,217 @@
+/* n550 Qwen3-0.6B hot path on NVIDIA B200 (sm_100a) -- the C ABI.
+ *
+ * libn550_qwen3.so exports two layers:
+ *
+ * 1. The reference's operator plug points, same names and meaning, taking
+ *    HOST pointers (drop-in for the KERNEL=ame / OPS=rvv backends): each call
+ *    copies its operands to the current CUDA device, runs the CUDA kernel and
+ *    copies the result back before returning, so on return the output is
+ *    globally visible, as kernels_ame.c:438-444 guarantees. Like the
+ *    reference these functions return nothing; a failed call leaves the output
+ *    untouched (the reference's silent-return contract, kernels_ame.c:221) and
+ *    records a status readable with n550_last_status().
+ *
+ * 2. A device-pointer, stream-ordered API (n550_*) with the same math that
+ *    returns a status code, plus the model runtime that keeps the weights, the
+ *    KV cache and all activations in HBM.
+ *
+ * No torch types, no C++ types: plain pointers and sizes. Streams are passed
+ * as `void *` holding a cudaStream_t (NULL = legacy default stream).
+ */
+#ifndef N550_QWEN3_H
+#define N550_QWEN3_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The library is built with hidden visibility; everything declared here is
+ * exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ---------------------------------------------------------------------------
+ * Status codes. Model-loader codes equal the reference's QWEN3_ERR_* values
+ * (qwen3.h:190-201); the n550 codes are below -100.
+ * ------------------------------------------------------------------------- */
+enum {
+    N550_OK               = 0,
+    N550_ERR_MAGIC        = -1,   /* QWEN3_ERR_MAGIC   */
+    N550_ERR_VERSION      = -2,   /* QWEN3_ERR_VERSION */
+    N550_ERR_DTYPE        = -3,   /* QWEN3_ERR_DTYPE   */
+    N550_ERR_SHAPE        = -4,   /* QWEN3_ERR_SHAPE   */
+    N550_ERR_SIZE         = -5,   /* QWEN3_ERR_SIZE    */
+    N550_ERR_OOM          = -6,   /* QWEN3_ERR_OOM     */
+    N550_ERR_LAYOUT       = -7,   /* QWEN3_ERR_LAYOUT  */
+    N550_ERR_ARG          = -101, /* argument outside the documented contract */
+    N550_ERR_CUDA         = -102, /* a CUDA runtime call failed               */
+    N550_ERR_UNSUPPORTED  = -103, /* shape/alignment this build does not take */
+    N550_ERR_TIMEOUT      = -104  /* a bounded device-side wait expired       */
+};
+
+/* GEMM numerics. */
+enum {
+    N550_MODE_EXACT = 0,  /* AME golden numerics, bit-exact: exact sum per
+                             K-block, binary64 then binary32 RNE per block */
+    N550_MODE_FAST  = 1   /* tcgen05 tensor cores, BF16 x BF16 -> FP32     */
+};
+
+/* Element types for the device API. */
+enum { N550_F32 = 0, N550_BF16 = 1 };
+
+/* Weight layouts (kernels.h:67-68). */
+#define N550_LAYOUT_ROW  0
+#define N550_LAYOUT_TILE 1
+
+/* ===========================================================================
+ * 1. Reference plug points, host pointers
+ * ========================================================================= */
+
+/* C[M,N] = bf16_rne(A[M,K]) . B[N,K]^T; A FP32, B BF16 [out,in], C FP32,
+ * all row-major. Replaces kernels.h:56-57 (qwen3_gemm) as implemented by
+ * kernels_ame.c:448-451. Numerics follow n550_set_gemm_mode (default: exact
+ * AME numerics, K-block 16). */
+void qwen3_gemm(float *c, const float *a, const uint16_t *b, int M, int K, int N);
+
+/* Same contract with B always row-major (kernels.h:79-80, kernels_ame.c:456-459). */
+void qwen3_gemm_row(float *c, const float *a, const uint16_t *b, int M, int K, int N);
+
+/* Accepts QW3M_LAYOUT_ROW (0) and QW3M_LAYOUT_TILE (1) with tile 128x32;
+ * returns 0 when accepted, -1 otherwise (kernels.h:89, kernels_ame.c:188-207). */
+int qwen3_set_weight_layout(int layout, int tile_n, int tile_k);
+
+/* Name of this backend (kernels.h:92). */
+const char *qwen3_kernel_name(void);
+
+/* Non-GEMM ops (ops.h:21-49), host pointers, FP32. */
+void  qwen3_op_rmsnorm(float *out, const float *x, const uint16_t *w, int n);
+void  qwen3_op_rope(float *v, int n_heads, int pos);
+void  qwen3_op_softmax(float *x, int n);
+void  qwen3_op_silu_mul(float *gate, const float *up, int n);
+void  qwen3_op_residual_add(float *x, const float *y, int n);
+int   qwen3_op_argmax(const float *v, int n);       /* lowest index on ties */
+void  qwen3_op_bf16_to_f32(float *out, const uint16_t *in, int n);
+float qwen3_op_dot(const float *a, const float *b, int n);
+void  qwen3_op_axpy(float *y, float a, const float *x, int n);
+const char *qwen3_ops_name(void);
+
+/* Numerics of qwen3_gemm / qwen3_gemm_row: mode N550_MODE_EXACT with kblock
+ * 16 or 32, or N550_MODE_FAST (kblock ignored). No counterpart in the
+ * reference, where numerics are chosen at link time (Makefile:14-21). */
+int n550_set_gemm_mode(int mode, int kblock);
+
+/* Status of the last host-pointer call on this thread (N550_OK or an error). */
+int n550_last_status(void);
+const char *n550_strerror(int status);
+
+/* ===========================================================================
+ * 2. Device-pointer, stream-ordered API
+ * ========================================================================= */
+
+/* C = A . B^T with element strides lda/ldb/ldc.
+ *   mode EXACT: a_type F32 (rounded to BF16 RNE on load, kernels_ame.c:235)
+ *               or BF16; c_type F32; kblock 16 or 32; any M, N, K >= 0.
+ *   mode FAST:  a_type BF16 (or F32, staged to BF16 RNE first); c_type F32 or
+ *               BF16. Tensor-core path needs K % 8 == 0, lda/ldb % 8 == 0 and
+ *               16-byte aligned A/B; other shapes take a CUDA-core kernel.
+ * Replaces gemm_impl (kernels_ame.c:217-445) for device-resident operands. */
+int n550_gemm(void *stream, int mode, int kblock,
+              const void *a, int a_type, int lda,
+              const uint16_t *b, int ldb,
+              void *c, int c_type, int ldc,
+              int M, int N, int K);
+
+/* Row-wise RMSNorm: out[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * w
+ * (ops_scalar.c:11-15). out_type F32 or BF16. */
+int n550_rmsnorm(void *stream, void *out, int out_type, const float *x,
+                 const uint16_t *w, int rows, int n, float eps);
+
+/* Rotate-half RoPE in place on rows of n_heads x 128 FP32, row r at position
+ * pos0 + r, theta 1e6 (ops_scalar.c:21-35). */
+int n550_rope(void *stream, float *v, int rows, int n_heads, int pos0);
+
+/* gate = silu(gate) * up over n elements (ops_scalar.c:46-51). */
+int n550_silu_mul(void *stream, float *gate, const float *up, size_t n);
+
+/* Row-wise softmax in place (ops_scalar.c:37-44). */
+int n550_softmax(void *stream, float *x, int rows, int n);
+
+/* Row-wise argmax, first index of the maximum (ops_scalar.c:57-62):
+ * idx[r] = argmax(v[r*ld .. r*ld+n)). */
+int n550_argmax(void *stream, const float *v, int rows, int n, int ld, int32_t *idx);
+
+/* x += y (ops_scalar.c:53-55); out = bf16 -> f32 (ops_scalar.c:64-66). */
+int n550_residual_add(void *stream, float *x, const float *y, size_t n);
+int n550_bf16_to_f32(void *stream, float *out, const uint16_t *in, size_t n);
+
+/* Device status word written by bounded waits inside kernels; returns it and
+ * clears it (N550_OK, or N550_ERR_TIMEOUT). Synchronises the device. */
+int n550_device_status(void);
+
+/* ===========================================================================
+ * 3. Model runtime (qwen3.h:203-257 re-designed for HBM): weights, KV cache
+ *    and activations live on one GPU; many independent sequences share it.
+ * ========================================================================= */
+typedef struct n550_model n550_model_t;
+
+typedef struct {
+    int    max_seqs;     /* sequences with their own KV cache              */
+    int    max_len;      /* positions per sequence (QWEN3_MAX_SEQ)          */
+    int    max_tokens;   /* tokens per forward call (activation capacity)   */
+    int    gemm_mode;    /* N550_MODE_FAST or N550_MODE_EXACT               */
+    int    kblock;       /* exact-mode K-block (16 or 32)                   */
+} n550_model_config;
+
+/* Parses a QW3M blob in host memory (qwen3.c:87-146: same header checks and
+ * error codes) and uploads it to the current device. */
+int n550_qwen3_init(n550_model_t **out, const void *blob, size_t blob_size,
+                    const n550_model_config *cfg);
+
+/* Random-init weights generated on the device: linear weights from the
+ * seeded integer generator (approximately N(0, sigma^2)), norms 1.0;
+ * bit-identical to the same seed written as a QW3M blob. */
+int n550_qwen3_init_random(n550_model_t **out, uint64_t seed, float sigma,
+                           const n550_model_config *cfg);
+
+void n550_qwen3_free(n550_model_t *m);
+
+/* Batched prefill: n_seqs sequences of seq_len tokens each, tokens
+ * [n_seqs][seq_len] and seq_ids [n_seqs] (KV slots) in device memory, all at
+ * positions pos0..pos0+seq_len-1. Writes last-token logits [n_seqs][151936]
+ * FP32 (may be NULL) and their argmax [n_seqs] (may be NULL).
+ * qwen3_forward_batch (qwen3.c:455-576) generalised to many sequences. */
+int n550_qwen3_prefill(n550_model_t *m, void *stream, const int32_t *tokens,
+                       const int32_t *seq_ids, int n_seqs, int seq_len, int pos0,
+                       float *logits, int32_t *next_token);
+
+/* One decode step for n_seqs sequences: token[i] at position pos[i] of
+ * sequence seq_ids[i] (device arrays). Greedy next token -> next_token[i];
+ * logits [n_seqs][151936] optional. qwen3_forward + qwen3_argmax
+ * (qwen3.c:578-584) generalised to many sequences. */
+int n550_qwen3_decode(n550_model_t *m, void *stream, const int32_t *tokens,
+                      const int32_t *seq_ids, const int32_t *pos, int n_seqs,
+                      float *logits, int32_t *next_token);
+
+/* Reference-shaped convenience on sequence slot 0 with HOST buffers:
+ * tokens[n_token] at pos0.., last-token logits copied to logits_host
+ * (151936 floats, may be NULL); returns the argmax (>= 0) or an error (< 0). */
+int n550_qwen3_forward_batch_host(n550_model_t *m, const int32_t *tokens,
+                                  int n_token, int pos0, float *logits_host);
+
+/* Device buffers of one weight tensor, for tests: which = 0 embed,
+ * 1 + 11*l + j for layer l tensor j in QW3M order, 309 final norm.
+ * Returns a device pointer to the BF16 data in QW3M [out,in] order, or NULL. */
+const uint16_t *n550_qwen3_weight(const n550_model_t *m, int which, size_t *elems);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* N550_QWEN3_H */

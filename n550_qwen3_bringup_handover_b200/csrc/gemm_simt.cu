@@ -1,0 +1,200 @@
+// CUDA-core GEMM paths of fast mode:
+//  * gemm_simt: FP32-FMA tiled GEMM for shapes the TMA tensor-core path cannot
+//    take (K % 8 != 0, unaligned strides or pointers) -- same contract.
+//  * gemv: skinny M (decode, M <= 8): one warp per output column n streams
+//    B[n, :] once with 16-byte loads; A rows come through L1. At M <= 8 the
+//    FMA work per weight byte is below the B200 FP32 rate, so this stays
+//    HBM-bound (the decode GEMV of kernels_ame.c at mtilem = 1).
+//  * f32_to_bf16: RNE staging of FP32 activations (kernels_ame.c:220-236).
+#include "common.cuh"
+#include "gemm_tc.h"
+
+namespace n550 {
+namespace {
+
+constexpr int ST = 64, SK = 16, STHREADS = 256;
+
+template <int EPI>
+__device__ __forceinline__ void epi_store(void *c, int ldc, int m, int n, float v) {
+    if (EPI == TC_EPI_F32) ((float *)c)[(size_t)m * ldc + n] = v;
+    else if (EPI == TC_EPI_BF16) ((uint16_t *)c)[(size_t)m * ldc + n] = f32_to_bf16_rne(v);
+    else ((float *)c)[(size_t)m * ldc + n] += v;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(STHREADS)
+gemm_simt_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict__ b, int ldb,
+                 void *c, int ldc, int M, int N, int K) {
+    __shared__ float As[SK][ST + 1];
+    __shared__ float Bs[SK][ST + 1];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int m0 = blockIdx.y * ST, n0 = blockIdx.x * ST;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < K; k0 += SK) {
+        for (int e = threadIdx.x; e < ST * SK; e += STHREADS) {
+            const int r = e / SK, kk = e % SK, k = k0 + kk;
+            As[kk][r] = (m0 + r < M && k < K) ? bf16_bits_to_f32(a[(size_t)(m0 + r) * lda + k]) : 0.f;
+            Bs[kk][r] = (n0 + r < N && k < K) ? bf16_bits_to_f32(b[(size_t)(n0 + r) * ldb + k]) : 0.f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < SK; kk++) {
+            float av[4], bv[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) av[i] = As[kk][ty + 16 * i];
+#pragma unroll
+            for (int j = 0; j < 4; j++) bv[j] = Bs[kk][tx + 16 * j];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int m = m0 + ty + 16 * i;
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int n = n0 + tx + 16 * j;
+            if (n < N) epi_store<EPI>(c, ldc, m, n, acc[i][j]);
+        }
+    }
+}
+
+constexpr int GV_WARPS = 8;
+constexpr int GV_MAXM = 8;
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4 q, float (&f)[8]) {
+    f[0] = __uint_as_float(q.x << 16); f[1] = __uint_as_float(q.x & 0xFFFF0000u);
+    f[2] = __uint_as_float(q.y << 16); f[3] = __uint_as_float(q.y & 0xFFFF0000u);
+    f[4] = __uint_as_float(q.z << 16); f[5] = __uint_as_float(q.z & 0xFFFF0000u);
+    f[6] = __uint_as_float(q.w << 16); f[7] = __uint_as_float(q.w & 0xFFFF0000u);
+}
+
+// One warp per output column n; requires K % 8 == 0 and 16-byte aligned rows.
+template <int MM, int EPI>
+__global__ void __launch_bounds__(GV_WARPS * 32)
+gemv_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict__ b, int ldb,
+            void *c, int ldc, int N, int K) {
+    const int lane = threadIdx.x & 31;
+    const int n = blockIdx.x * GV_WARPS + (threadIdx.x >> 5);
+    if (n >= N) return;
+    const uint16_t *brow = b + (size_t)n * ldb;
+    float acc[MM];
+#pragma unroll
+    for (int m = 0; m < MM; m++) acc[m] = 0.f;
+    // 4 independent 16-byte loads in flight per lane per step.
+    for (int k0 = lane * 8; k0 < K; k0 += 32 * 8 * 4) {
+        uint4 bq[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int k = k0 + u * 256;
+            bq[u] = (k < K) ? __ldcs((const uint4 *)(brow + k)) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int k = k0 + u * 256;
+            if (k >= K) break;
+            float bf[8];
+            bf16x8_to_f32(bq[u], bf);
+#pragma unroll
+            for (int m = 0; m < MM; m++) {
+                const uint4 aq = __ldg((const uint4 *)(a + (size_t)m * lda + k));
+                float af[8];
+                bf16x8_to_f32(aq, af);
+#pragma unroll
+                for (int j = 0; j < 8; j++) acc[m] = fmaf(af[j], bf[j], acc[m]);
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < MM; m++) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xFFFFFFFFu, acc[m], o);
+    }
+    if (lane < MM) {
+        float v = acc[0];
+#pragma unroll
+        for (int m = 1; m < MM; m++) if (lane == m) v = acc[m];
+        epi_store<EPI>(c, ldc, lane, n, v);
+    }
+}
+
+__global__ void f32_to_bf16_kernel(uint16_t *out, int ldo, const float *in, int ldi,
+                                   int rows, int cols) {
+    const size_t total = (size_t)rows * cols;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = i / cols, cc = i % cols;
+        out[r * ldo + cc] = f32_to_bf16_rne(in[r * ldi + cc]);
+    }
+}
+
+template <int MM>
+int gemv_dispatch(cudaStream_t st, int epi, const uint16_t *a, int lda, const uint16_t *b,
+                  int ldb, void *c, int ldc, int N, int K) {
+    const int grid = (N + GV_WARPS - 1) / GV_WARPS;
+    if (epi == TC_EPI_F32)
+        gemv_kernel<MM, TC_EPI_F32><<<grid, GV_WARPS * 32, 0, st>>>(a, lda, b, ldb, c, ldc, N, K);
+    else if (epi == TC_EPI_BF16)
+        gemv_kernel<MM, TC_EPI_BF16><<<grid, GV_WARPS * 32, 0, st>>>(a, lda, b, ldb, c, ldc, N, K);
+    else if (epi == TC_EPI_RESID_F32)
+        gemv_kernel<MM, TC_EPI_RESID_F32><<<grid, GV_WARPS * 32, 0, st>>>(a, lda, b, ldb, c, ldc, N, K);
+    else
+        return N550_ERR_ARG;
+    N550_LAUNCH_CHECK();
+    return N550_OK;
+}
+
+}  // namespace
+
+int launch_gemm_simt(cudaStream_t st, int epi, const uint16_t *a, int lda,
+                     const uint16_t *b, int ldb, void *c, int ldc, int M, int N, int K) {
+    if (M <= 0 || N <= 0) return N550_OK;
+    const long long gy = (M + ST - 1) / ST;
+    if (gy > 65535) return N550_ERR_UNSUPPORTED;
+    dim3 grid((N + ST - 1) / ST, (unsigned)gy);
+    if (epi == TC_EPI_F32)
+        gemm_simt_kernel<TC_EPI_F32><<<grid, STHREADS, 0, st>>>(a, lda, b, ldb, c, ldc, M, N, K);
+    else if (epi == TC_EPI_BF16)
+        gemm_simt_kernel<TC_EPI_BF16><<<grid, STHREADS, 0, st>>>(a, lda, b, ldb, c, ldc, M, N, K);
+    else if (epi == TC_EPI_RESID_F32)
+        gemm_simt_kernel<TC_EPI_RESID_F32><<<grid, STHREADS, 0, st>>>(a, lda, b, ldb, c, ldc, M, N, K);
+    else
+        return N550_ERR_ARG;
+    N550_LAUNCH_CHECK();
+    return N550_OK;
+}
+
+int launch_gemv(cudaStream_t st, int epi, const uint16_t *a, int lda,
+                const uint16_t *b, int ldb, void *c, int ldc, int M, int N, int K) {
+    if (M <= 0 || N <= 0) return N550_OK;
+    if (M > GV_MAXM || (K % 8) || (lda % 8) || (ldb % 8) || (((uintptr_t)a) & 15) ||
+        (((uintptr_t)b) & 15))
+        return N550_ERR_UNSUPPORTED;
+    switch (M) {
+    case 1: return gemv_dispatch<1>(st, epi, a, lda, b, ldb, c, ldc, N, K);
+    case 2: return gemv_dispatch<2>(st, epi, a, lda, b, ldb, c, ldc, N, K);
+    case 3: return gemv_dispatch<3>(st, epi, a, lda, b, ldb, c, ldc, N, K);
+    case 4: return gemv_dispatch<4>(st, epi, a, lda, b, ldb, c, ldc, N, K);
+    case 5: return gemv_dispatch<5>(st, epi, a, lda, b, ldb, c, ldc, N, K);
+    case 6: return gemv_dispatch<6>(st, epi, a, lda, b, ldb, c, ldc, N, K);
+    case 7: return gemv_dispatch<7>(st, epi, a, lda, b, ldb, c, ldc, N, K);
+    default: return gemv_dispatch<8>(st, epi, a, lda, b, ldb, c, ldc, N, K);
+    }
+}
+
+int launch_f32_to_bf16(cudaStream_t st, uint16_t *out, int ldo, const float *in, int ldi,
+                       int rows, int cols) {
+    if (rows <= 0 || cols <= 0) return N550_OK;
+    const size_t total = (size_t)rows * cols;
+    int grid = (int)((total + 255) / 256);
+    if (grid > 148 * 16) grid = 148 * 16;
+    f32_to_bf16_kernel<<<grid, 256, 0, st>>>(out, ldo, in, ldi, rows, cols);
+    N550_LAUNCH_CHECK();
+    return N550_OK;
+}
+
+}  // namespace n550

@@ -1,0 +1,71 @@
+"""CPU checks of the C ABI: the library loads, exports every function the
+public header declares, and its host-only logic (layout negotiation, mode
+selection, status strings) behaves like the reference interface."""
+import re
+import subprocess
+
+import pytest
+
+import n550_qwen3_bringup_handover_b200 as n5
+
+
+def declared_functions():
+    text = n5.HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", " ", text, flags=re.S)
+    names = re.findall(r"\b((?:qwen3|n550)_[A-Za-z0-9_]+)\s*\(", text)
+    return sorted(set(names))
+
+
+def test_header_declares_reference_plug_points():
+    names = set(declared_functions())
+    # kernels.h:56-92 and ops.h:21-49
+    for ref in ["qwen3_gemm", "qwen3_gemm_row", "qwen3_set_weight_layout", "qwen3_kernel_name",
+                "qwen3_op_rmsnorm", "qwen3_op_rope", "qwen3_op_softmax", "qwen3_op_silu_mul",
+                "qwen3_op_residual_add", "qwen3_op_argmax", "qwen3_op_bf16_to_f32",
+                "qwen3_op_dot", "qwen3_op_axpy", "qwen3_ops_name"]:
+        assert ref in names
+
+
+def test_library_exports_every_declared_symbol():
+    out = subprocess.run(["nm", "-D", "--defined-only", str(n5.LIB_PATH)],
+                         capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    missing = [f for f in declared_functions() if f not in exported]
+    assert not missing, missing
+
+
+def test_library_loads_and_binds():
+    L = n5.lib()
+    for f in declared_functions():
+        assert hasattr(L, f)
+
+
+def test_weight_layout_negotiation():
+    # kernels_ame.c:188-207: ROW always, TILE only with 128x32 tiles
+    assert n5.qwen3_set_weight_layout(n5.LAYOUT_ROW, 0, 0) == 0
+    assert n5.qwen3_set_weight_layout(n5.LAYOUT_TILE, 128, 32) == 0
+    assert n5.qwen3_set_weight_layout(n5.LAYOUT_TILE, 64, 32) != 0
+    assert n5.qwen3_set_weight_layout(7, 128, 32) != 0
+    assert n5.qwen3_set_weight_layout(n5.LAYOUT_ROW, 0, 0) == 0
+
+
+def test_gemm_mode_selection_and_names():
+    try:
+        n5.set_gemm_mode(n5.MODE_EXACT, 32)
+        assert "32" in n5.kernel_name()
+        n5.set_gemm_mode(n5.MODE_FAST)
+        assert "fast" in n5.kernel_name()
+        with pytest.raises(n5.N550Error):
+            n5.set_gemm_mode(n5.MODE_EXACT, 24)
+        with pytest.raises(n5.N550Error):
+            n5.set_gemm_mode(9, 16)
+    finally:
+        n5.set_gemm_mode(n5.MODE_EXACT, 16)
+    assert "16" in n5.kernel_name()
+    assert n5.lib().qwen3_ops_name().decode()
+
+
+def test_status_strings():
+    for s in (n5.OK, n5.ERR_MAGIC, n5.ERR_LAYOUT, n5.ERR_ARG, n5.ERR_CUDA, n5.ERR_TIMEOUT):
+        assert n5.strerror(s) and n5.strerror(s) != "unknown"
+    assert n5.strerror(12345) == "unknown"
