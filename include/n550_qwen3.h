@@ -174,7 +174,7 @@ int n550_qwen3_init(n550_model_t **out, const void *blob, size_t blob_size,
 /* Random-init weights generated on the device: linear weights from the
  * seeded integer generator (approximately N(0, sigma^2)), norms 1.0;
  * bit-identical to the same seed written as a QW3M blob. */
-int n550_qwen3_init_random(n550_model_t **out, uint64_t seed, float sigma,
+int n550_qwen3_init_random(n550_model_t **out, uint64_t seed, double sigma,
                            const n550_model_config *cfg);
 
 void n550_qwen3_free(n550_model_t *m);
@@ -202,10 +202,30 @@ int n550_qwen3_decode(n550_model_t *m, void *stream, const int32_t *tokens,
 int n550_qwen3_forward_batch_host(n550_model_t *m, const int32_t *tokens,
                                   int n_token, int pos0, float *logits_host);
 
+/* Seeded synthetic token ids (the benchmark's inputs), host memory:
+ * out[i] = u64(seed, stream, i) mod vocab with the generator of
+ * n550_qwen3_init_random. No counterpart in the reference (its prompts come
+ * from the tokenizer, which needs the unshipped tokenizer.bin). */
+int n550_synth_tokens(int32_t *out, size_t n, uint64_t seed, uint64_t stream, int vocab);
+
 /* Device buffers of one weight tensor, for tests: which = 0 embed,
  * 1 + 11*l + j for layer l tensor j in QW3M order, 309 final norm.
  * Returns a device pointer to the BF16 data in QW3M [out,in] order, or NULL. */
 const uint16_t *n550_qwen3_weight(const n550_model_t *m, int which, size_t *elems);
+
+/* Kernel-time accounting of one model, for benchmarks: while enabled, every
+ * kernel the runtime launches is counted and bracketed by CUDA events on its
+ * stream, accumulated per kind below. enable = 1 resets and starts, 0 stops.
+ * n550_qwen3_profile_read synchronises, then fills ms[k] (device time) and
+ * launches[k] for k < n_kinds. No counterpart in the reference (its only
+ * instrumentation is the mcycle timing of main_baremetal.c:636,733-754). */
+enum {
+    N550_PROF_GEMM_QKV = 0, N550_PROF_GEMM_O, N550_PROF_GEMM_GATEUP, N550_PROF_GEMM_DOWN,
+    N550_PROF_GEMM_LMHEAD, N550_PROF_ATTN, N550_PROF_QKNORM_ROPE, N550_PROF_RMSNORM,
+    N550_PROF_OTHER, N550_PROF_KINDS
+};
+int n550_qwen3_profile(n550_model_t *m, int enable);
+int n550_qwen3_profile_read(n550_model_t *m, double *ms, int64_t *launches, int n_kinds);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -77,12 +77,15 @@ def lib() -> C.CDLL:
     }
     optional = {
         "n550_qwen3_init": (i, [C.POINTER(vp), vp, sz, C.POINTER(ModelConfig)]),
-        "n550_qwen3_init_random": (i, [C.POINTER(vp), C.c_uint64, f, C.POINTER(ModelConfig)]),
+        "n550_qwen3_init_random": (i, [C.POINTER(vp), C.c_uint64, C.c_double, C.POINTER(ModelConfig)]),
         "n550_qwen3_free": (None, [vp]),
         "n550_qwen3_prefill": (i, [vp, vp, vp, vp, i, i, i, vp, vp]),
         "n550_qwen3_decode": (i, [vp, vp, vp, vp, vp, i, vp, vp]),
         "n550_qwen3_forward_batch_host": (i, [vp, vp, i, i, vp]),
         "n550_qwen3_weight": (vp, [vp, i, C.POINTER(sz)]),
+        "n550_qwen3_profile": (i, [vp, i]),
+        "n550_qwen3_profile_read": (i, [vp, vp, vp, i]),
+        "n550_synth_tokens": (i, [vp, sz, C.c_uint64, C.c_uint64, i]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -108,8 +111,18 @@ def kernel_name() -> str:
     return lib().qwen3_kernel_name().decode()
 
 
+def synth_tokens(n: int, seed: int, stream: int, vocab: int = 151936):
+    """Seeded synthetic token ids (numpy int32), the library's generator."""
+    import numpy as np
+    out = np.empty(n, np.int32)
+    check(lib().n550_synth_tokens(out.ctypes.data_as(C.c_void_p), n, seed, stream, vocab),
+          "n550_synth_tokens")
+    return out
+
+
 def set_gemm_mode(mode: int, kblock: int = 16) -> None:
     check(lib().n550_set_gemm_mode(mode, kblock), "n550_set_gemm_mode")
 
 
 from .api import *  # noqa: E402,F401,F403
+from .model import Model  # noqa: E402,F401

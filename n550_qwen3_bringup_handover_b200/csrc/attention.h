@@ -1,0 +1,34 @@
+// Internal launch interfaces of the attention kernels (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace n550 {
+
+// Prefill: n_seqs sequences x L queries at positions pos0..pos0+L-1; the
+// queries' own K/V are already in the cache. Q/out rows are [seq][L][2048].
+struct AttnPrefillArgs {
+    const uint16_t *q;        // BF16, row stride ldq elements
+    const uint16_t *kc, *vc;  // KV cache base pointers
+    uint16_t *out;            // BF16, row stride ldo
+    const int32_t *seq_ids;   // [n_seqs] KV slots
+    int ldq, ldo, L, pos0, layer, max_len;
+};
+
+// Decode: one query per sequence at position pos[s] (attends 0..pos[s]).
+struct AttnDecodeArgs {
+    const float *q_f32;       // FP32 queries, or NULL to read q_bf16
+    const uint16_t *q_bf16;
+    const uint16_t *kc, *vc;
+    uint16_t *out;
+    const int32_t *seq_ids, *pos;
+    int ldq, ldo, layer, max_len, splits;
+    float *part_m, *part_l, *part_o;   // split-KV partials (splits > 1)
+};
+
+int launch_attn_prefill(cudaStream_t st, const AttnPrefillArgs &a, int n_seqs);
+int launch_attn_decode(cudaStream_t st, const AttnDecodeArgs &a, int n_seqs);
+int attn_decode_splits(int n_seqs, int max_kv_len, int max_splits);
+
+}  // namespace n550

@@ -6,6 +6,7 @@
 #include "common.cuh"
 #include "gemm_tc.h"
 #include "ops.h"
+#include "synth.cuh"
 
 namespace n550 {
 namespace {
@@ -320,6 +321,13 @@ int n550_residual_add(void *stream, float *x, const float *y, size_t n) {
 
 int n550_bf16_to_f32(void *stream, float *out, const uint16_t *in, size_t n) {
     return launch_bf16_to_f32((cudaStream_t)stream, out, in, n);
+}
+
+int n550_synth_tokens(int32_t *out, size_t n, uint64_t seed, uint64_t stream, int vocab) {
+    if ((n && !out) || vocab <= 0) return N550_ERR_ARG;
+    const uint64_t key = synth_key(seed, stream);
+    for (size_t i = 0; i < n; i++) out[i] = (int32_t)(synth_u64(key, i) % (uint64_t)vocab);
+    return N550_OK;
 }
 
 int n550_device_status(void) {

@@ -1,0 +1,677 @@
+// Qwen3-0.6B runtime on one B200: qwen3_init / qwen3_forward_batch /
+// qwen3_forward / qwen3_argmax (qwen3.c:87-584) re-designed so that weights,
+// KV cache and activations stay in HBM and many independent sequences share
+// one pass.
+//
+// Per layer (prefill and decode alike):
+//   rmsnorm(x) -> xb (BF16)                    qwen3.c:471-472
+//   qkv = xb . [Wq;Wk;Wv]^T (one GEMM, N=4096)  qwen3.c:477-487
+//   per-head RMSNorm + RoPE of q and k, K/V written to the cache (BF16)
+//                                              qwen3.c:479-511
+//   attention -> attn (BF16)                   qwen3.c:513-517
+//   x += attn . Wo^T (residual fused in the GEMM epilogue)   qwen3.c:520-523
+//   rmsnorm(x) -> xb                           qwen3.c:527
+//   h = silu(xb . Wg^T) * (xb . Wu^T) (SwiGLU fused in the epilogue)
+//                                              qwen3.c:531-537
+//   x += h . Wd^T (residual fused)             qwen3.c:540-543
+// then final RMSNorm of each sequence's last token and the tied lm_head
+// (qwen3.c:547-573), followed by argmax (qwen3.c:582-584).
+//
+// BF16 activations exist only where the reference's AME GEMM rounds its FP32
+// input to BF16 anyway (kernels_ame.c:220-236), so the GEMM inputs are the
+// same values; the residual stream stays FP32. The KV cache is BF16.
+#include <stdlib.h>
+#include <string.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "attention.h"
+#include "common.cuh"
+#include "gemm_tc.h"
+#include "ops.h"
+#include "synth.cuh"
+
+namespace n550 {
+namespace {
+
+constexpr int H = 1024, INTER = 3072, NLAYER = 28, NH = 16, NKVH = 8, HDIM = 128;
+constexpr int VOCAB = 151936, QD = NH * HDIM, KVD = NKVH * HDIM, QKVD = QD + 2 * KVD;
+constexpr int N_TENSORS = 1 + NLAYER * 11 + 1;
+constexpr float EPS = 1e-6f;
+constexpr int MAX_SPLITS = 32;
+
+int32_t rd_i32(const uint8_t *p) {
+    return (int32_t)((uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) |
+                     ((uint32_t)p[3] << 24));
+}
+float rd_f32(const uint8_t *p) {
+    int32_t v = rd_i32(p);
+    float f;
+    memcpy(&f, &v, 4);
+    return f;
+}
+void wr_i32(uint8_t *p, int32_t v) {
+    for (int i = 0; i < 4; i++) p[i] = (uint8_t)((uint32_t)v >> (8 * i));
+}
+void wr_f32(uint8_t *p, float f) {
+    int32_t v;
+    memcpy(&v, &f, 4);
+    wr_i32(p, v);
+}
+
+// Elements of tensor idx in QW3M file order (qwen3_config.h:64-81).
+size_t tensor_elems(int idx, bool *is_norm) {
+    *is_norm = false;
+    if (idx == 0) return (size_t)VOCAB * H;
+    if (idx == N_TENSORS - 1) { *is_norm = true; return H; }
+    switch ((idx - 1) % 11) {
+    case 0: *is_norm = true; return H;
+    case 1: return (size_t)QD * H;
+    case 2: return (size_t)KVD * H;
+    case 3: return (size_t)KVD * H;
+    case 4: *is_norm = true; return HDIM;
+    case 5: *is_norm = true; return HDIM;
+    case 6: return (size_t)H * QD;
+    case 7: *is_norm = true; return H;
+    case 8: return (size_t)INTER * H;
+    case 9: return (size_t)INTER * H;
+    default: return (size_t)H * INTER;
+    }
+}
+
+// Header checks in the order of qwen3_init (qwen3.c:93-146), same codes.
+int parse_qw3m(const uint8_t *b, size_t size, size_t *offs) {
+    if (size < 256) return N550_ERR_SIZE;
+    if (b[0] != 'Q' || b[1] != 'W' || b[2] != '3' || b[3] != 'M') return N550_ERR_MAGIC;
+    if (rd_i32(b + 4) != 1) return N550_ERR_VERSION;
+    if (rd_i32(b + 44) != 1) return N550_ERR_DTYPE;
+    if (rd_i32(b + 8) != H || rd_i32(b + 12) != INTER || rd_i32(b + 16) != NLAYER ||
+        rd_i32(b + 20) != NH || rd_i32(b + 24) != NKVH || rd_i32(b + 28) != HDIM ||
+        rd_i32(b + 32) != VOCAB)
+        return N550_ERR_SHAPE;
+    const int align = rd_i32(b + 72);
+    if (align < 128 || (align & (align - 1)) != 0) return N550_ERR_SHAPE;
+    if (rd_i32(b + 76) != N550_LAYOUT_ROW) return N550_ERR_LAYOUT;
+    if (rd_f32(b + 48) != 1000000.0f) return N550_ERR_SHAPE;
+    if (rd_f32(b + 52) != 1e-06f) return N550_ERR_SHAPE;
+    size_t pos = (size_t)(uint32_t)rd_i32(b + 68);
+    for (int t = 0; t < N_TENSORS; t++) {
+        bool nrm;
+        const size_t n = tensor_elems(t, &nrm);
+        const size_t p = (pos + (size_t)align - 1) & ~((size_t)align - 1);
+        if (p + n * 2 > size) return N550_ERR_SIZE;
+        offs[t] = p;
+        pos = p + n * 2;
+    }
+    if (pos != size) return N550_ERR_SIZE;
+    return N550_OK;
+}
+
+// The random-init blob header: the fields a QW3M exporter writes for
+// Qwen3-0.6B (qwen3_config.h:41-62), row layout, 128-byte alignment.
+void make_header(uint8_t *h) {
+    memset(h, 0, 256);
+    memcpy(h, "QW3M", 4);
+    wr_i32(h + 4, 1);
+    wr_i32(h + 8, H); wr_i32(h + 12, INTER); wr_i32(h + 16, NLAYER);
+    wr_i32(h + 20, NH); wr_i32(h + 24, NKVH); wr_i32(h + 28, HDIM);
+    wr_i32(h + 32, VOCAB); wr_i32(h + 36, 40960); wr_i32(h + 40, 1);
+    wr_i32(h + 44, 1);
+    wr_f32(h + 48, 1000000.0f); wr_f32(h + 52, 1e-06f);
+    wr_i32(h + 56, 151643); wr_i32(h + 60, 151645); wr_i32(h + 64, 151643);
+    wr_i32(h + 68, 256); wr_i32(h + 72, 128);
+}
+
+size_t qw3m_row_size() {
+    size_t pos = 256;
+    for (int t = 0; t < N_TENSORS; t++) {
+        bool nrm;
+        pos = (pos + 127) & ~(size_t)127;
+        pos += tensor_elems(t, &nrm) * 2;
+    }
+    return pos;
+}
+
+// ---------------------------------------------------------------- kernels
+
+__global__ void synth_bf16_kernel(uint16_t *out, size_t n, uint64_t key, float scale) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x)
+        out[i] = f32_to_bf16_rne(synth_normal(synth_u64(key, i), scale));
+}
+
+__global__ void fill_u16_kernel(uint16_t *out, size_t n, uint16_t v) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x)
+        out[i] = v;
+}
+
+// Per-token (position, KV slot) of a prefill chunk: token t = i*Lc + j.
+__global__ void setup_prefill_kernel(int32_t *tok_pos, int32_t *tok_seq, const int32_t *seq_ids,
+                                     int Sc, int Lc, int p0) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= Sc * Lc) return;
+    tok_pos[t] = p0 + t % Lc;
+    tok_seq[t] = seq_ids[t / Lc];
+}
+
+// x[t] = embed[token] in FP32 (qwen3_embed, qwen3.c:276-279); the token of
+// row t = i*Lc + j is tokens[i*ld + off + j].
+__global__ void embed_kernel(float *x, const uint16_t *__restrict__ embed, const int32_t *tokens,
+                             int Lc, int ld, int off) {
+    const int t = blockIdx.x;
+    const int i = t / Lc, j = t % Lc;
+    int tok = tokens[(size_t)i * ld + off + j];
+    tok = min(max(tok, 0), VOCAB - 1);
+    const uint2 *src = (const uint2 *)(embed + (size_t)tok * H);
+    float4 *dst = (float4 *)(x + (size_t)t * H);
+    for (int c = threadIdx.x; c < H / 4; c += blockDim.x) {
+        const uint2 q = src[c];
+        dst[c] = make_float4(__uint_as_float(q.x << 16), __uint_as_float(q.x & 0xFFFF0000u),
+                             __uint_as_float(q.y << 16), __uint_as_float(q.y & 0xFFFF0000u));
+    }
+}
+
+// Per-head RMSNorm of q and k (qk_norm, qwen3.c:287-292), RoPE at the
+// token's position (ops_scalar.c:21-35), and the K/V cache write
+// (qwen3.c:498-511). One warp per head; 32 heads per token
+// ([q 16 | k 8 | v 8] x 128 is the qkv row).
+__global__ void __launch_bounds__(256)
+qknorm_rope_kv_kernel(const float *__restrict__ qkv, int ldqkv, const uint16_t *__restrict__ qn,
+                      const uint16_t *__restrict__ kn, const int32_t *__restrict__ tok_pos,
+                      const int32_t *__restrict__ tok_seq, int layer, uint16_t *kc, uint16_t *vc,
+                      int max_len, uint16_t *q_bf16, float *q_f32, int ldq) {
+    const int t = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pos = tok_pos[t], seq = tok_seq[t];
+    const float *row = qkv + (size_t)t * ldqkv;
+    for (int hd = warp; hd < 32; hd += 8) {
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) v[j] = row[hd * HDIM + lane + 32 * j];
+        if (hd < 24) {
+            const uint16_t *w = hd < 16 ? qn : kn;
+            float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+            const float sc = 1.0f / sqrtf(ss / (float)HDIM + EPS);
+#pragma unroll
+            for (int j = 0; j < 4; j++) v[j] = v[j] * sc * bf16_bits_to_f32(w[lane + 32 * j]);
+#pragma unroll
+            for (int j = 0; j < 2; j++) {          // pairs (i, i + 64), i = lane + 32 j
+                float s, c;
+                sincosf((float)pos * c_inv_freq[lane + 32 * j], &s, &c);
+                const float a = v[j], b = v[j + 2];
+                v[j] = a * c - b * s;
+                v[j + 2] = b * c + a * s;
+            }
+        }
+        if (hd < 16) {
+            const size_t o = (size_t)t * ldq + hd * HDIM + lane;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                if (q_bf16) q_bf16[o + 32 * j] = f32_to_bf16_rne(v[j]);
+                if (q_f32) q_f32[o + 32 * j] = v[j];
+            }
+        } else {
+            const int kvh = (hd - 16) & 7;
+            uint16_t *dst = (hd < 24 ? kc : vc) +
+                            (((size_t)(seq * NLAYER + layer) * NKVH + kvh) * max_len + pos) * HDIM;
+#pragma unroll
+            for (int j = 0; j < 4; j++) dst[lane + 32 * j] = f32_to_bf16_rne(v[j]);
+        }
+    }
+}
+
+// Final RMSNorm of the last token of each sequence (qwen3.c:547-573 only
+// needs row NT-1): xl[i] = rmsnorm(x[i*Lc + Lc - 1]) in BF16.
+__global__ void __launch_bounds__(256)
+final_norm_kernel(uint16_t *xl, const float *__restrict__ x, const uint16_t *__restrict__ w, int Lc) {
+    __shared__ float red[8];
+    const float *xr = x + ((size_t)blockIdx.x * Lc + Lc - 1) * H;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < H; i += 256) ss = fmaf(xr[i], xr[i], ss);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) ss += red[i];
+    const float sc = 1.0f / sqrtf(ss / (float)H + EPS);
+    for (int i = threadIdx.x; i < H; i += 256)
+        xl[(size_t)blockIdx.x * H + i] = f32_to_bf16_rne(xr[i] * sc * bf16_bits_to_f32(w[i]));
+}
+
+// h = silu(g) * u in BF16 (the unfused SwiGLU for the GEMV / exact paths).
+__global__ void silu_mul_bf16_kernel(uint16_t *h, const float *__restrict__ g,
+                                     const float *__restrict__ u, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const float gv = g[i];
+        h[i] = f32_to_bf16_rne((gv / (1.0f + expf(-gv))) * u[i]);
+    }
+}
+
+int grid1(size_t n) {
+    size_t g = (n + 255) / 256;
+    return (int)std::min<size_t>(std::max<size_t>(g, 1), 148 * 16);
+}
+
+}  // namespace
+}  // namespace n550
+
+using namespace n550;
+
+// Per-kind kernel timing (n550_qwen3_profile): event pairs recorded on the
+// launch stream around each launch while enabled.
+struct ModelProf {
+    bool on = false;
+    std::vector<cudaEvent_t> pool;
+    size_t used = 0;
+    std::vector<std::pair<int, size_t>> marks;   // (kind, index of the start event)
+    long long launches[N550_PROF_KINDS] = {};
+    cudaEvent_t next_event() {
+        if (used == pool.size()) {
+            cudaEvent_t e;
+            if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+            pool.push_back(e);
+        }
+        return pool[used++];
+    }
+};
+
+struct n550_model {
+    ModelProf prof;
+    int dev = 0;
+    n550_model_config cfg{};
+    uint8_t *blob = nullptr;
+    size_t blob_size = 0;
+    size_t off[N_TENSORS] = {};
+    const uint16_t *t[N_TENSORS] = {};
+    uint16_t *fused_qkv = nullptr;          // only if q/k/v are not contiguous
+    const uint16_t *wqkv[NLAYER] = {};
+    uint16_t *kc = nullptr, *vc = nullptr;
+    float *x = nullptr, *qkv = nullptr, *qf = nullptr, *logits = nullptr;
+    uint16_t *xb = nullptr, *qb = nullptr, *attn = nullptr, *h = nullptr, *xl = nullptr;
+    float *tmp_a = nullptr, *tmp_b = nullptr;
+    size_t tmp_rows = 0;
+    int32_t *tok_pos = nullptr, *tok_seq = nullptr, *next = nullptr, *host_tok = nullptr,
+            *zero_seq = nullptr;
+    float *part_m = nullptr, *part_l = nullptr, *part_o = nullptr;
+};
+
+namespace {
+
+const uint16_t *W(const n550_model *m, int layer, int j) { return m->t[1 + 11 * layer + j]; }
+
+// Brackets the kernels launched in its scope with an event pair of `kind`
+// (n kernels counted) while profiling is enabled.
+struct ProfScope {
+    n550_model *m;
+    cudaStream_t st;
+    int kind;
+    cudaEvent_t e1 = nullptr;
+    ProfScope(n550_model *m_, cudaStream_t st_, int kind_, int n = 1) : m(m_), st(st_), kind(kind_) {
+        if (!m->prof.on) return;
+        m->prof.launches[kind] += n;
+        const size_t idx = m->prof.used;
+        cudaEvent_t e0 = m->prof.next_event();
+        e1 = m->prof.next_event();
+        if (!e0 || !e1) { e1 = nullptr; return; }
+        cudaEventRecord(e0, st);
+        m->prof.marks.push_back({kind, idx});
+    }
+    ~ProfScope() { if (e1) cudaEventRecord(e1, st); }
+};
+
+void model_release(n550_model *m) {
+    if (!m) return;
+    for (cudaEvent_t e : m->prof.pool) cudaEventDestroy(e);
+    void *ptrs[] = {m->blob, m->fused_qkv, m->kc, m->vc, m->x, m->qkv, m->qf, m->logits, m->xb,
+                    m->qb, m->attn, m->h, m->xl, m->tmp_a, m->tmp_b, m->tok_pos, m->tok_seq,
+                    m->next, m->host_tok, m->zero_seq, m->part_m, m->part_l, m->part_o};
+    for (void *p : ptrs) if (p) cudaFree(p);
+    delete m;
+}
+
+// Allocations that depend on the config; the blob must already be on device.
+int model_setup(n550_model *m) {
+    const n550_model_config &c = m->cfg;
+    for (int i = 0; i < N_TENSORS; i++) m->t[i] = (const uint16_t *)(m->blob + m->off[i]);
+    bool contiguous = true;
+    for (int l = 0; l < NLAYER; l++)
+        contiguous = contiguous && W(m, l, 2) == W(m, l, 1) + (size_t)QD * H &&
+                     W(m, l, 3) == W(m, l, 2) + (size_t)KVD * H;
+    if (contiguous) {
+        for (int l = 0; l < NLAYER; l++) m->wqkv[l] = W(m, l, 1);
+    } else {
+        N550_CUDA_TRY(cudaMalloc(&m->fused_qkv, (size_t)NLAYER * QKVD * H * 2));
+        for (int l = 0; l < NLAYER; l++) {
+            uint16_t *d = m->fused_qkv + (size_t)l * QKVD * H;
+            N550_CUDA_TRY(cudaMemcpy(d, W(m, l, 1), (size_t)QD * H * 2, cudaMemcpyDeviceToDevice));
+            N550_CUDA_TRY(cudaMemcpy(d + (size_t)QD * H, W(m, l, 2), (size_t)KVD * H * 2,
+                                     cudaMemcpyDeviceToDevice));
+            N550_CUDA_TRY(cudaMemcpy(d + (size_t)(QD + KVD) * H, W(m, l, 3), (size_t)KVD * H * 2,
+                                     cudaMemcpyDeviceToDevice));
+            m->wqkv[l] = d;
+        }
+    }
+    const size_t T = (size_t)c.max_tokens, S = (size_t)c.max_seqs;
+    const size_t kv = (size_t)c.max_seqs * NLAYER * NKVH * (size_t)c.max_len * HDIM;
+#define ALLOC(p, bytes) N550_CUDA_TRY(cudaMalloc((void **)&(p), (bytes)))
+    ALLOC(m->kc, kv * 2);
+    ALLOC(m->vc, kv * 2);
+    ALLOC(m->x, T * H * 4);
+    ALLOC(m->xb, T * H * 2);
+    ALLOC(m->qkv, T * QKVD * 4);
+    ALLOC(m->qb, T * QD * 2);
+    ALLOC(m->qf, S * QD * 4);
+    ALLOC(m->attn, T * QD * 2);
+    ALLOC(m->h, T * INTER * 2);
+    ALLOC(m->xl, S * H * 2);
+    ALLOC(m->logits, S * (size_t)VOCAB * 4);
+    m->tmp_rows = c.gemm_mode == N550_MODE_EXACT ? T : 8;
+    ALLOC(m->tmp_a, m->tmp_rows * INTER * 4);
+    ALLOC(m->tmp_b, m->tmp_rows * INTER * 4);
+    ALLOC(m->tok_pos, T * 4);
+    ALLOC(m->tok_seq, T * 4);
+    ALLOC(m->next, S * 4);
+    ALLOC(m->host_tok, T * 4);
+    ALLOC(m->zero_seq, 4);
+    const size_t slots = S * NH * MAX_SPLITS;
+    ALLOC(m->part_m, slots * 4);
+    ALLOC(m->part_l, slots * 4);
+    ALLOC(m->part_o, slots * HDIM * 4);
+#undef ALLOC
+    N550_CUDA_TRY(cudaMemset(m->zero_seq, 0, 4));
+    N550_CUDA_TRY(cudaMemset(m->kc, 0, kv * 2));
+    N550_CUDA_TRY(cudaMemset(m->vc, 0, kv * 2));
+    int rc = ensure_rope_table();
+    if (rc) return rc;
+    N550_CUDA_TRY(cudaDeviceSynchronize());
+    return N550_OK;
+}
+
+int check_cfg(const n550_model_config *c) {
+    if (!c || c->max_seqs < 1 || c->max_len < 1 || c->max_tokens < 1) return N550_ERR_ARG;
+    if (c->gemm_mode != N550_MODE_FAST && c->gemm_mode != N550_MODE_EXACT) return N550_ERR_ARG;
+    if (c->gemm_mode == N550_MODE_EXACT && c->kblock != 16 && c->kblock != 32) return N550_ERR_ARG;
+    return N550_OK;
+}
+
+// A [M,K] BF16 . W[N,K]^T with epilogue `epi` into c (ldc). SILU takes W2.
+int mgemm(n550_model *m, cudaStream_t st, int epi, const uint16_t *a, int lda, const uint16_t *w,
+          const uint16_t *w2, void *c, int ldc, int M, int N, int K) {
+    if (m->cfg.gemm_mode == N550_MODE_EXACT) {
+        if (epi == TC_EPI_F32)
+            return launch_gemm_exact(st, a, N550_BF16, lda, w, K, (float *)c, ldc, M, N, K, m->cfg.kblock);
+        if (epi == TC_EPI_RESID_F32) {
+            int rc = launch_gemm_exact(st, a, N550_BF16, lda, w, K, m->tmp_a, N, M, N, K, m->cfg.kblock);
+            if (rc) return rc;
+            return launch_residual_add(st, (float *)c, m->tmp_a, (size_t)M * N);
+        }
+        if (epi == TC_EPI_SILU_BF16) {
+            int rc = launch_gemm_exact(st, a, N550_BF16, lda, w, K, m->tmp_a, N, M, N, K, m->cfg.kblock);
+            if (!rc) rc = launch_gemm_exact(st, a, N550_BF16, lda, w2, K, m->tmp_b, N, M, N, K, m->cfg.kblock);
+            if (rc) return rc;
+            silu_mul_bf16_kernel<<<grid1((size_t)M * N), 256, 0, st>>>((uint16_t *)c, m->tmp_a, m->tmp_b,
+                                                                    (size_t)M * N);
+            N550_LAUNCH_CHECK();
+            return N550_OK;
+        }
+        return N550_ERR_ARG;
+    }
+    if (M <= 8) {
+        if (epi != TC_EPI_SILU_BF16) return launch_gemv(st, epi, a, lda, w, K, c, ldc, M, N, K);
+        int rc = launch_gemv(st, TC_EPI_F32, a, lda, w, K, m->tmp_a, N, M, N, K);
+        if (!rc) rc = launch_gemv(st, TC_EPI_F32, a, lda, w2, K, m->tmp_b, N, M, N, K);
+        if (rc) return rc;
+        silu_mul_bf16_kernel<<<grid1((size_t)M * N), 256, 0, st>>>((uint16_t *)c, m->tmp_a, m->tmp_b,
+                                                                (size_t)M * N);
+        N550_LAUNCH_CHECK();
+        return N550_OK;
+    }
+    return launch_gemm_tc(st, epi, 128, a, lda, w, K, w2, c, ldc, M, N, K, 0);
+}
+
+int launch_qknorm_rope_kv(n550_model *m, cudaStream_t st, int T, int l, bool decode) {
+    qknorm_rope_kv_kernel<<<T, 256, 0, st>>>(m->qkv, QKVD, W(m, l, 4), W(m, l, 5), m->tok_pos,
+                                             m->tok_seq, l, m->kc, m->vc, m->cfg.max_len,
+                                             decode ? nullptr : m->qb, decode ? m->qf : nullptr, QD);
+    N550_LAUNCH_CHECK();
+    return N550_OK;
+}
+
+int launch_final_norm(cudaStream_t st, uint16_t *xl, const float *x, const uint16_t *w, int Sc, int Lc) {
+    final_norm_kernel<<<Sc, 256, 0, st>>>(xl, x, w, Lc);
+    N550_LAUNCH_CHECK();
+    return N550_OK;
+}
+
+// All 28 layers over T tokens already embedded in m->x, with tok_pos/tok_seq
+// set. decode: one token per sequence (seq_ids/pos arrays of n_seqs = T).
+int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t *seq_ids,
+               const int32_t *pos, int Sc, int Lc, int p0) {
+    const n550_model_config &c = m->cfg;
+    int rc = N550_OK;
+#define STEP(kind, nk, expr)                          \
+    do {                                              \
+        ProfScope ps_(m, st, (kind), (nk));           \
+        if ((rc = (expr))) return rc;                 \
+    } while (0)
+    const bool exact = c.gemm_mode == N550_MODE_EXACT;
+    const int gu_kernels = exact ? 3 : (T <= 8 ? 3 : 1);
+    const int res_kernels = exact ? 2 : 1;
+    for (int l = 0; l < NLAYER; l++) {
+        STEP(N550_PROF_RMSNORM, 1, launch_rmsnorm(st, m->xb, N550_BF16, m->x, W(m, l, 0), T, H, EPS));
+        STEP(N550_PROF_GEMM_QKV, 1,
+             mgemm(m, st, TC_EPI_F32, m->xb, H, m->wqkv[l], nullptr, m->qkv, QKVD, T, QKVD, H));
+        STEP(N550_PROF_QKNORM_ROPE, 1, launch_qknorm_rope_kv(m, st, T, l, decode));
+        if (decode) {
+            AttnDecodeArgs a{};
+            a.q_f32 = m->qf;
+            a.kc = m->kc; a.vc = m->vc; a.out = m->attn;
+            a.seq_ids = seq_ids; a.pos = pos;
+            a.ldq = QD; a.ldo = QD; a.layer = l; a.max_len = c.max_len;
+            a.splits = attn_decode_splits(T, c.max_len, MAX_SPLITS);
+            a.part_m = m->part_m; a.part_l = m->part_l; a.part_o = m->part_o;
+            STEP(N550_PROF_ATTN, a.splits > 1 ? 2 : 1, launch_attn_decode(st, a, T));
+        } else {
+            AttnPrefillArgs a{};
+            a.q = m->qb; a.kc = m->kc; a.vc = m->vc; a.out = m->attn; a.seq_ids = seq_ids;
+            a.ldq = QD; a.ldo = QD; a.L = Lc; a.pos0 = p0; a.layer = l; a.max_len = c.max_len;
+            STEP(N550_PROF_ATTN, 1, launch_attn_prefill(st, a, Sc));
+        }
+        STEP(N550_PROF_GEMM_O, res_kernels,
+             mgemm(m, st, TC_EPI_RESID_F32, m->attn, QD, W(m, l, 6), nullptr, m->x, H, T, H, QD));
+        STEP(N550_PROF_RMSNORM, 1, launch_rmsnorm(st, m->xb, N550_BF16, m->x, W(m, l, 7), T, H, EPS));
+        STEP(N550_PROF_GEMM_GATEUP, gu_kernels,
+             mgemm(m, st, TC_EPI_SILU_BF16, m->xb, H, W(m, l, 8), W(m, l, 9), m->h, INTER, T, INTER, H));
+        STEP(N550_PROF_GEMM_DOWN, res_kernels,
+             mgemm(m, st, TC_EPI_RESID_F32, m->h, INTER, W(m, l, 10), nullptr, m->x, H, T, H, INTER));
+    }
+    return N550_OK;
+}
+
+// Last-token logits and argmax for Sc sequences whose rows are i*Lc + Lc - 1.
+int run_head(n550_model *m, cudaStream_t st, int Sc, int Lc, float *logits, int32_t *next) {
+    int rc = N550_OK;
+    STEP(N550_PROF_RMSNORM, 1, launch_final_norm(st, m->xl, m->x, m->t[N_TENSORS - 1], Sc, Lc));
+    STEP(N550_PROF_GEMM_LMHEAD, 1,
+         mgemm(m, st, TC_EPI_F32, m->xl, H, m->t[0], nullptr, logits, VOCAB, Sc, VOCAB, H));
+    if (next) STEP(N550_PROF_OTHER, 1, launch_argmax(st, logits, Sc, VOCAB, VOCAB, next));
+    return N550_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int n550_qwen3_init(n550_model_t **out, const void *blob, size_t blob_size,
+                    const n550_model_config *cfg) {
+    if (!out || !blob) return N550_ERR_ARG;
+    *out = nullptr;
+    int rc = check_cfg(cfg);
+    if (rc) return rc;
+    n550_model *m = new n550_model();
+    m->cfg = *cfg;
+    rc = parse_qw3m((const uint8_t *)blob, blob_size, m->off);
+    if (rc) { model_release(m); return rc; }
+    cudaGetDevice(&m->dev);
+    m->blob_size = blob_size;
+    if (cudaMalloc(&m->blob, blob_size) != cudaSuccess) { model_release(m); return N550_ERR_OOM; }
+    if (cudaMemcpy(m->blob, blob, blob_size, cudaMemcpyHostToDevice) != cudaSuccess) {
+        model_release(m);
+        return N550_ERR_CUDA;
+    }
+    rc = model_setup(m);
+    if (rc) { model_release(m); return rc; }
+    *out = m;
+    return N550_OK;
+}
+
+int n550_qwen3_init_random(n550_model_t **out, uint64_t seed, double sigma,
+                           const n550_model_config *cfg) {
+    if (!out) return N550_ERR_ARG;
+    *out = nullptr;
+    int rc = check_cfg(cfg);
+    if (rc) return rc;
+    n550_model *m = new n550_model();
+    m->cfg = *cfg;
+    uint8_t hdr[256];
+    make_header(hdr);
+    m->blob_size = qw3m_row_size();
+    rc = parse_qw3m(hdr, m->blob_size, m->off);
+    if (rc) { model_release(m); return rc; }
+    cudaGetDevice(&m->dev);
+    if (cudaMalloc(&m->blob, m->blob_size) != cudaSuccess) { model_release(m); return N550_ERR_OOM; }
+    if (cudaMemset(m->blob, 0, m->blob_size) != cudaSuccess ||
+        cudaMemcpy(m->blob, hdr, 256, cudaMemcpyHostToDevice) != cudaSuccess) {
+        model_release(m);
+        return N550_ERR_CUDA;
+    }
+    const float scale = synth_normal_scale(sigma);
+    for (int t = 0; t < N_TENSORS; t++) {
+        bool nrm;
+        const size_t n = tensor_elems(t, &nrm);
+        uint16_t *dst = (uint16_t *)(m->blob + m->off[t]);
+        if (nrm) fill_u16_kernel<<<grid1(n), 256>>>(dst, n, (uint16_t)0x3F80);
+        else synth_bf16_kernel<<<148 * 16, 256>>>(dst, n, synth_key(seed, (uint64_t)t), scale);
+        if (cudaPeekAtLastError() != cudaSuccess) { model_release(m); return N550_ERR_CUDA; }
+    }
+    rc = model_setup(m);
+    if (rc) { model_release(m); return rc; }
+    *out = m;
+    return N550_OK;
+}
+
+void n550_qwen3_free(n550_model_t *m) {
+    if (m) cudaDeviceSynchronize();
+    model_release(m);
+}
+
+int n550_qwen3_prefill(n550_model_t *m, void *stream, const int32_t *tokens, const int32_t *seq_ids,
+                       int n_seqs, int seq_len, int pos0, float *logits, int32_t *next_token) {
+    if (!m || !tokens || !seq_ids || n_seqs < 1 || seq_len < 1 || pos0 < 0) return N550_ERR_ARG;
+    const n550_model_config &c = m->cfg;
+    if (pos0 + seq_len > c.max_len) return N550_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int Lmax = std::min(seq_len, c.max_tokens);
+    int rc;
+    for (int s0 = 0; s0 < n_seqs;) {
+        const int Sc = std::max(1, std::min({n_seqs - s0, c.max_tokens / Lmax, c.max_seqs}));
+        for (int j0 = 0; j0 < seq_len; j0 += Lmax) {
+            const int Lc = std::min(Lmax, seq_len - j0);
+            const int T = Sc * Lc;
+            const int p0 = pos0 + j0;
+            {
+                ProfScope ps(m, st, N550_PROF_OTHER, 2);
+                setup_prefill_kernel<<<(T + 255) / 256, 256, 0, st>>>(m->tok_pos, m->tok_seq,
+                                                                      seq_ids + s0, Sc, Lc, p0);
+                embed_kernel<<<T, 128, 0, st>>>(m->x, m->t[0], tokens + (size_t)s0 * seq_len, Lc,
+                                                seq_len, j0);
+                N550_LAUNCH_CHECK();
+            }
+            if ((rc = run_layers(m, st, T, false, seq_ids + s0, nullptr, Sc, Lc, p0))) return rc;
+            if (j0 + Lc == seq_len) {
+                float *lg = logits ? logits + (size_t)s0 * VOCAB : m->logits;
+                if ((rc = run_head(m, st, Sc, Lc, lg, next_token ? next_token + s0 : nullptr)))
+                    return rc;
+            }
+        }
+        s0 += Sc;
+    }
+    return N550_OK;
+}
+
+int n550_qwen3_decode(n550_model_t *m, void *stream, const int32_t *tokens, const int32_t *seq_ids,
+                      const int32_t *pos, int n_seqs, float *logits, int32_t *next_token) {
+    if (!m || !tokens || !seq_ids || !pos || n_seqs < 1) return N550_ERR_ARG;
+    const n550_model_config &c = m->cfg;
+    if (n_seqs > c.max_tokens || n_seqs > c.max_seqs) return N550_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    N550_CUDA_TRY(cudaMemcpyAsync(m->tok_pos, pos, (size_t)n_seqs * 4, cudaMemcpyDeviceToDevice, st));
+    N550_CUDA_TRY(cudaMemcpyAsync(m->tok_seq, seq_ids, (size_t)n_seqs * 4, cudaMemcpyDeviceToDevice, st));
+    {
+        ProfScope ps(m, st, N550_PROF_OTHER, 1);
+        embed_kernel<<<n_seqs, 128, 0, st>>>(m->x, m->t[0], tokens, 1, 1, 0);
+        N550_LAUNCH_CHECK();
+    }
+    int rc = run_layers(m, st, n_seqs, true, seq_ids, pos, n_seqs, 1, 0);
+    if (rc) return rc;
+    return run_head(m, st, n_seqs, 1, logits ? logits : m->logits, next_token);
+}
+
+int n550_qwen3_forward_batch_host(n550_model_t *m, const int32_t *tokens, int n_token, int pos0,
+                                  float *logits_host) {
+    if (!m || !tokens || n_token < 1) return N550_ERR_ARG;
+    if (n_token > m->cfg.max_tokens) return N550_ERR_ARG;
+    cudaStream_t st = 0;
+    N550_CUDA_TRY(cudaMemcpyAsync(m->host_tok, tokens, (size_t)n_token * 4, cudaMemcpyHostToDevice, st));
+    int rc = n550_qwen3_prefill(m, st, m->host_tok, m->zero_seq, 1, n_token, pos0, m->logits, m->next);
+    if (rc) return rc;
+    int32_t best = 0;
+    N550_CUDA_TRY(cudaMemcpyAsync(&best, m->next, 4, cudaMemcpyDeviceToHost, st));
+    if (logits_host)
+        N550_CUDA_TRY(cudaMemcpyAsync(logits_host, m->logits, (size_t)VOCAB * 4, cudaMemcpyDeviceToHost, st));
+    N550_CUDA_TRY(cudaStreamSynchronize(st));
+    return best;
+}
+
+int n550_qwen3_profile(n550_model_t *m, int enable) {
+    if (!m) return N550_ERR_ARG;
+    if (enable) {
+        m->prof.used = 0;
+        m->prof.marks.clear();
+        for (long long &v : m->prof.launches) v = 0;
+    }
+    m->prof.on = enable != 0;
+    return N550_OK;
+}
+
+int n550_qwen3_profile_read(n550_model_t *m, double *ms, int64_t *launches, int n_kinds) {
+    if (!m || n_kinds < 0) return N550_ERR_ARG;
+    N550_CUDA_TRY(cudaDeviceSynchronize());
+    double acc[N550_PROF_KINDS] = {};
+    for (const auto &mk : m->prof.marks) {
+        float t = 0.f;
+        N550_CUDA_TRY(cudaEventElapsedTime(&t, m->prof.pool[mk.second], m->prof.pool[mk.second + 1]));
+        acc[mk.first] += t;
+    }
+    for (int k = 0; k < n_kinds && k < N550_PROF_KINDS; k++) {
+        if (ms) ms[k] = acc[k];
+        if (launches) launches[k] = m->prof.launches[k];
+    }
+    return N550_OK;
+}
+
+const uint16_t *n550_qwen3_weight(const n550_model_t *m, int which, size_t *elems) {
+    if (!m || which < 0 || which >= N_TENSORS) return nullptr;
+    bool nrm;
+    if (elems) *elems = tensor_elems(which, &nrm);
+    return m->t[which];
+}
+
+}  // extern "C"

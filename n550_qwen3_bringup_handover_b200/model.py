@@ -1,0 +1,111 @@
+"""Model runtime binding: the reference's qwen3_init / qwen3_forward_batch /
+qwen3_forward / qwen3_argmax (qwen3.h:206-248) as one handle over
+libn550_qwen3.so, extended to many sequences per call."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import MODE_FAST, ModelConfig, check, lib
+
+VOCAB = 151936
+
+
+class Model:
+    """Weights, KV cache and activations of Qwen3-0.6B on the current CUDA device."""
+
+    def __init__(self, *, blob: np.ndarray | None = None, seed: int = 0, sigma: float = 0.02,
+                 max_seqs: int = 1, max_len: int = 2048, max_tokens: int = 512,
+                 gemm_mode: int = MODE_FAST, kblock: int = 16):
+        self.cfg = ModelConfig(max_seqs, max_len, max_tokens, gemm_mode, kblock)
+        h = C.c_void_p()
+        if blob is not None:
+            b = np.ascontiguousarray(blob, np.uint8)
+            rc = lib().n550_qwen3_init(C.byref(h), b.ctypes.data_as(C.c_void_p), b.size,
+                                       C.byref(self.cfg))
+        else:
+            rc = lib().n550_qwen3_init_random(C.byref(h), seed, sigma, C.byref(self.cfg))
+        check(rc, "n550_qwen3_init")
+        self._h = h
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().n550_qwen3_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    # ---- reference-shaped host path (sequence slot 0) ----
+    def forward_batch(self, tokens, pos0: int, want_logits: bool = True):
+        """qwen3_forward_batch on host tokens: (argmax, last-token logits or None)."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        logits = np.empty(VOCAB, np.float32) if want_logits else None
+        r = lib().n550_qwen3_forward_batch_host(
+            self._h, t.ctypes.data_as(C.c_void_p), t.size, pos0,
+            logits.ctypes.data_as(C.c_void_p) if want_logits else None)
+        if r < 0:
+            check(r, "n550_qwen3_forward_batch_host")
+        return int(r), logits
+
+    # ---- batched device path (torch CUDA tensors) ----
+    def prefill(self, tokens, seq_ids, pos0=0, logits=None, next_token=None, stream=None):
+        from .api import stream_ptr
+        S, L = tokens.shape
+        check(lib().n550_qwen3_prefill(
+            self._h, stream_ptr(stream), C.c_void_p(tokens.data_ptr()), C.c_void_p(seq_ids.data_ptr()),
+            S, L, pos0, C.c_void_p(logits.data_ptr()) if logits is not None else None,
+            C.c_void_p(next_token.data_ptr()) if next_token is not None else None), "n550_qwen3_prefill")
+
+    def decode(self, tokens, seq_ids, pos, logits=None, next_token=None, stream=None):
+        from .api import stream_ptr
+        check(lib().n550_qwen3_decode(
+            self._h, stream_ptr(stream), C.c_void_p(tokens.data_ptr()), C.c_void_p(seq_ids.data_ptr()),
+            C.c_void_p(pos.data_ptr()), tokens.shape[0],
+            C.c_void_p(logits.data_ptr()) if logits is not None else None,
+            C.c_void_p(next_token.data_ptr()) if next_token is not None else None), "n550_qwen3_decode")
+
+    def weight_bits(self, which: int) -> np.ndarray:
+        """Copy of one QW3M tensor (BF16 bits) from the device."""
+        import torch
+        n = C.c_size_t(0)
+        p = lib().n550_qwen3_weight(self._h, which, C.byref(n))
+        if not p:
+            raise IndexError(which)
+        view = torch.as_tensor(_DeviceArray(p, n.value), device="cuda")
+        return view.cpu().numpy().view(np.uint16)
+
+
+class _DeviceArray:
+    """Zero-copy CUDA array interface over a device pointer of int16."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<i2", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def smoke_forward(device) -> None:
+    """One prefill + one decode step of the random-init model, compared with
+    the oracle's restatement of qwen3_forward_batch on the same weights."""
+    import oracle
+    m = Model(seed=0, max_seqs=1, max_len=64, max_tokens=64)
+    toks = oracle.synth_tokens(8, 0, 0x544F4B)
+    nxt, lg = m.forward_batch(toks, 0)
+    blob = oracle.qw3m_blob(seed=0, sigma=0.02)
+    ref = oracle.OracleModel(blob, max_seq=64, gemm_kind=oracle.GEMM_HWSIM)
+    rl = ref.forward_batch(toks, 0)
+    err = float(np.abs(lg - rl).max() / np.abs(rl).max())
+    if not err <= 1e-2:
+        raise AssertionError(f"prefill logits rel err {err:.3e} > 1e-2")
+    nxt2, lg2 = m.forward_batch(np.array([nxt], np.int32), 8)
+    rl2 = ref.forward_batch(np.array([nxt], np.int32), 8)
+    err2 = float(np.abs(lg2 - rl2).max() / np.abs(rl2).max())
+    if not err2 <= 1e-2:
+        raise AssertionError(f"decode logits rel err {err2:.3e} > 1e-2")
+    m.close()
+    ref.close()

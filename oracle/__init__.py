@@ -278,5 +278,23 @@ class RefModel:
         return c
 
 
+_ref_libs = {}
+
+
+def ref_gemm(kernel, a_f32, b_bf16):
+    """The reference's own qwen3_gemm from kernels_<kernel>.c (oracle/_ref)."""
+    if kernel not in _ref_libs:
+        L = C.CDLL(str(REF_DIR / f"libref_{kernel}.so"), mode=os.RTLD_LOCAL)
+        L.qwen3_gemm.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int]
+        _ref_libs[kernel] = L
+    a = np.ascontiguousarray(a_f32, np.float32)
+    b = np.ascontiguousarray(b_bf16, np.uint16)
+    M, K = a.shape
+    N = b.shape[0]
+    c = np.zeros((M, N), np.float32)
+    _ref_libs[kernel].qwen3_gemm(_p(c), _p(a), _p(b), M, K, N)
+    return c
+
+
 def ref_available(kernel="scalar"):
     return (REF_DIR / f"libref_{kernel}.so").exists()

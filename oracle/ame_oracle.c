@@ -43,6 +43,21 @@ void oracle_f32_to_bf16_array(uint16_t *out, const float *in, size_t n) {
 
 static uint32_t f32_bits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
 
+/* Inline copies of the two conversions for the inner loops. */
+static inline float bf16f(uint16_t b) {
+    uint32_t u = (uint32_t)b << 16;
+    float f;
+    memcpy(&f, &u, sizeof f);
+    return f;
+}
+static inline uint16_t rne16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, sizeof u);
+    if ((u & 0x7F800000u) == 0x7F800000u) return (uint16_t)(u >> 16);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
 /* ------------------------------------------------------------------------
  * Exact superaccumulator.
  * Terms are sign * mant * 2^exp with mant < 2^24:
@@ -221,8 +236,8 @@ void oracle_gemm_hwsim(float *c, const float *a, const uint16_t *b,
                 if (k1 > K) k1 = K;
                 double blk = 0.0;
                 for (int k = k0; k < k1; k++) {
-                    float av = oracle_bf16_to_f32(oracle_f32_to_bf16_rne(arow[k]));
-                    blk += (double)av * (double)oracle_bf16_to_f32(brow[k]);
+                    float av = bf16f(rne16(arow[k]));
+                    blk += (double)av * (double)bf16f(brow[k]);
                 }
                 acc = (float)((double)acc + blk);
             }
@@ -239,7 +254,7 @@ void oracle_gemm_scalar(float *c, const float *a, const uint16_t *b,
         for (int n = 0; n < N; n++) {
             const uint16_t *brow = b + (size_t)n * K;
             float sum = 0.0f;
-            for (int k = 0; k < K; k++) sum += arow[k] * oracle_bf16_to_f32(brow[k]);
+            for (int k = 0; k < K; k++) sum += arow[k] * bf16f(brow[k]);
             crow[n] = sum;
         }
     }
@@ -252,7 +267,7 @@ void oracle_gemm_f64(float *c, const float *a, const uint16_t *b,
             double sum = 0.0;
             for (int k = 0; k < K; k++)
                 sum += (double)a[(size_t)m * K + k]
-                     * (double)oracle_bf16_to_f32(b[(size_t)n * K + k]);
+                     * (double)bf16f(b[(size_t)n * K + k]);
             c[(size_t)m * N + n] = (float)sum;
         }
 }

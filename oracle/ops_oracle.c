@@ -6,8 +6,16 @@
  * Constants from qwen3_config.h:17-28.
  */
 #include <math.h>
+#include <string.h>
 
 #include "oracle.h"
+
+static inline float bf16f(uint16_t b) {
+    uint32_t u = (uint32_t)b << 16;
+    float f;
+    memcpy(&f, &u, sizeof f);
+    return f;
+}
 
 #define HEAD_DIM   128
 #define RMS_EPS    1e-06f
@@ -17,7 +25,7 @@ void oracle_op_rmsnorm(float *out, const float *x, const uint16_t *w, int n) {
     float ss = 0.0f;
     for (int i = 0; i < n; i++) ss += x[i] * x[i];
     float scale = 1.0f / sqrtf(ss / (float)n + RMS_EPS);
-    for (int i = 0; i < n; i++) out[i] = x[i] * scale * oracle_bf16_to_f32(w[i]);
+    for (int i = 0; i < n; i++) out[i] = x[i] * scale * bf16f(w[i]);
 }
 
 /* rotate-half pairs (i, i + 64); inv_freq = theta^(-2i/128). */

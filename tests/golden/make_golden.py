@@ -7,6 +7,10 @@ Writes
   tests/golden/ame_cases.npz   the 12 shipped AME cases of
       rtl_verification/cases/*: inputs (a.bin or a_src.bin, b.bin, strides),
       expected c_ref.bin / c_peak.bin words and xor_ref (mixed cases).
+  tests/golden/greedy_ref.npz   BASELINE config 3 (seed-0 random-init model,
+      32-token seeded prompt, 64 greedy steps) run by the reference's own
+      qwen3.c + kernels_scalar.c / kernels_hwsim.c (oracle/_ref): generated
+      tokens and each step's top-8 logits (ids, values).
   tests/golden/config1_exact.npz   BASELINE config 1 (16x1024x2048, seed 0,
       this project's seeded generator) evaluated by the reference's own
       generator function ame_gemm_ref (40_gen_ame_vectors.py:121-143), imported
@@ -110,13 +114,47 @@ def config1(ref: Path):
     return res
 
 
+PROMPT = dict(seed=0, stream=0x544F4B, n=32, steps=64)
+
+
+def greedy_reference():
+    import oracle
+    blob = oracle.qw3m_blob(seed=0, sigma=0.02)
+    prompt = oracle.synth_tokens(PROMPT["n"], PROMPT["seed"], PROMPT["stream"])
+    res = {"prompt": prompt}
+    for kern in ("scalar", "hwsim"):
+        m = oracle.RefModel(blob, kern)
+        toks, top_i, top_v = [], [], []
+        logits = m.forward_batch(prompt, 0)
+        pos = PROMPT["n"]
+        for step in range(PROMPT["steps"]):
+            order = np.argsort(-logits, kind="stable")[:8]
+            top_i.append(order.astype(np.int32))
+            top_v.append(logits[order].astype(np.float32))
+            nxt = int(oracle.argmax(logits))
+            toks.append(nxt)
+            if step + 1 < PROMPT["steps"]:
+                logits = m.forward_batch(np.array([nxt], np.int32), pos)
+                pos += 1
+        res[f"{kern}_tokens"] = np.array(toks, np.int32)
+        res[f"{kern}_top_ids"] = np.stack(top_i)
+        res[f"{kern}_top_vals"] = np.stack(top_v)
+        print(kern, toks[:16])
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
     ap.add_argument("--skip-config1", action="store_true")
+    ap.add_argument("--greedy", action="store_true", help="only the greedy-decode fixture")
     args = ap.parse_args()
     ref = Path(args.reference)
     here = Path(__file__).resolve().parent
+    if args.greedy:
+        np.savez_compressed(here / "greedy_ref.npz", **greedy_reference())
+        print("wrote greedy_ref.npz")
+        return
     cases = load_cases(ref)
     np.savez_compressed(here / "ame_cases.npz", **cases)
     print("wrote ame_cases.npz:", list(cases["case_ids"]))
