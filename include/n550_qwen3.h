@@ -125,6 +125,25 @@ int n550_gemm(void *stream, int mode, int kblock,
               void *c, int c_type, int ldc,
               int M, int N, int K);
 
+/* Fast-mode C = bf16_rne(A) . B^T for callers that cannot allocate device
+ * memory: runtimes that keep the reference's no-malloc discipline (a fixed
+ * arena sized up front, qwen3.h:39-58) and hosts that must not let a call
+ * synchronise the device, as cudaMalloc/cudaFree do. It is the FP32-activation
+ * path of n550_gemm(MODE_FAST, a_type = N550_F32), with the BF16 staging copy
+ * of A held in a fixed 8 MiB array that this library places in every GPU
+ * that loads it (for as long as the process lives) instead of a per-call
+ * allocation. No counterpart in the reference.
+ *   Limit: M * round_up(K, 8) <= 4,194,304 (e.g. 4096 x 1024, 1365 x 3072);
+ *   larger calls return N550_ERR_ARG and touch nothing.
+ *   The first call on each device looks up the array's device address; make
+ *   that first call before capturing the stream into a CUDA graph.
+ *   All calls share the one array: calls that can overlap on the GPU (other
+ *   streams, other threads) race on it and must be serialised by the caller.
+ *   c_type is N550_F32 or N550_BF16; other arguments as in n550_gemm. */
+int n550_gemm_f32a_noalloc(void *stream, const float *a, int lda,
+                           const uint16_t *b, int ldb, void *c, int c_type, int ldc,
+                           int M, int N, int K);
+
 /* Row-wise RMSNorm: out[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * w
  * (ops_scalar.c:11-15). out_type F32 or BF16. */
 int n550_rmsnorm(void *stream, void *out, int out_type, const float *x,

@@ -139,6 +139,31 @@ int host_op(float *x_out, const float *x_in, size_t nx, const void *y, size_t yb
 
 inline void set_status(int s) { t_status = s; }
 
+// ---- staging area of n550_gemm_f32a_noalloc ----
+// 4 Mi BF16 elements (8 MiB) in every GPU that loads the library. Its host
+// symbol is only a stand-in: kernels get the device address looked up below.
+constexpr size_t kNoAllocStageElems = (size_t)4 << 20;
+static __device__ __align__(256) uint16_t g_noalloc_stage[kNoAllocStageElems];
+std::mutex g_noalloc_mu;
+uint16_t *g_noalloc_ptr[64];
+
+// Device address of the staging array on the current device (looked up once
+// per device, with that device current); nullptr on failure.
+uint16_t *noalloc_stage() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_stage) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return nullptr;
+        }
+        g_noalloc_ptr[dev] = (uint16_t *)p;
+    }
+    return g_noalloc_ptr[dev];
+}
+
 }  // namespace
 }  // namespace n550
 
@@ -321,6 +346,34 @@ int n550_residual_add(void *stream, float *x, const float *y, size_t n) {
 
 int n550_bf16_to_f32(void *stream, float *out, const uint16_t *in, size_t n) {
     return launch_bf16_to_f32((cudaStream_t)stream, out, in, n);
+}
+
+int n550_gemm_f32a_noalloc(void *stream, const float *a, int lda, const uint16_t *b, int ldb,
+                           void *c, int c_type, int ldc, int M, int N, int K) {
+    cudaStream_t st = (cudaStream_t)stream;
+    if (M < 0 || N < 0 || K < 0) return N550_ERR_ARG;
+    if (M == 0 || N == 0) return N550_OK;
+    if (!c || (K && (!a || !b)) || lda < K || ldb < K || ldc < N) return N550_ERR_ARG;
+    if (c_type != N550_F32 && c_type != N550_BF16) return N550_ERR_ARG;
+    const int ldab = (K + 7) & ~7;
+    if ((size_t)M * (size_t)ldab > kNoAllocStageElems) return N550_ERR_ARG;
+    const int esz = c_type == N550_F32 ? 4 : 2;
+    if (K == 0) {
+        N550_CUDA_TRY(cudaMemset2DAsync(c, (size_t)ldc * esz, 0, (size_t)N * esz, M, st));
+        return N550_OK;
+    }
+    uint16_t *stage = noalloc_stage();
+    if (!stage) return N550_ERR_CUDA;
+    // Every element the GEMM reads ([0, M) x [0, K)) is rewritten here; the
+    // padding columns [K, ldab) are never read (the TMA box and the CUDA-core
+    // paths stop at K), so the array needs no clearing between calls.
+    int rc = launch_f32_to_bf16(st, stage, ldab, a, lda, M, K);
+    if (rc) return rc;
+    const int epi = c_type == N550_F32 ? TC_EPI_F32 : TC_EPI_BF16;
+    if (M <= 8 && launch_gemv(st, epi, stage, ldab, b, ldb, c, ldc, M, N, K) == N550_OK) return N550_OK;
+    if (tc_shape_ok(stage, ldab, b, ldb, K))
+        return launch_gemm_tc(st, epi, 128, stage, ldab, b, ldb, nullptr, c, ldc, M, N, K, 0);
+    return launch_gemm_simt(st, epi, stage, ldab, b, ldb, c, ldc, M, N, K);
 }
 
 int n550_synth_tokens(int32_t *out, size_t n, uint64_t seed, uint64_t stream, int vocab) {
