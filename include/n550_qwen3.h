@@ -144,6 +144,21 @@ int n550_gemm_f32a_noalloc(void *stream, const float *a, int lda,
                            const uint16_t *b, int ldb, void *c, int c_type, int ldc,
                            int M, int N, int K);
 
+/* Tile width of the fast-mode tensor-core GEMMs: 128 or 256 output columns
+ * per CTA tile, or 0 for the automatic choice (default). A tuning knob for
+ * profiling; results do not depend on it beyond FP32 summation order. */
+int n550_gemm_tile_config(int bn);
+
+/* Fused fast-mode GEMMs of the decoder layer (A BF16, weights BF16 [N,K]):
+ *   n550_gemm_residual: x[M,N] += A . B^T in FP32 -- qwen3_gemm followed by
+ *     qwen3_op_residual_add (qwen3.c:520-523, 540-543);
+ *   n550_gemm_swiglu:  h[M,N] = bf16(silu(A . Wg^T) * (A . Wu^T)) -- the gate
+ *     and up qwen3_gemm calls followed by qwen3_op_silu_mul (qwen3.c:531-537). */
+int n550_gemm_residual(void *stream, const uint16_t *a, int lda, const uint16_t *b, int ldb,
+                       float *x, int ldx, int M, int N, int K);
+int n550_gemm_swiglu(void *stream, const uint16_t *a, int lda, const uint16_t *wg,
+                     const uint16_t *wu, int ldw, uint16_t *h, int ldh, int M, int N, int K);
+
 /* Row-wise RMSNorm: out[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * w
  * (ops_scalar.c:11-15). out_type F32 or BF16. */
 int n550_rmsnorm(void *stream, void *out, int out_type, const float *x,

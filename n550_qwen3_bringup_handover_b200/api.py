@@ -14,7 +14,7 @@ __all__ = [
     "qwen3_op_rope", "qwen3_op_softmax", "qwen3_op_silu_mul", "qwen3_op_residual_add",
     "qwen3_op_argmax", "qwen3_op_bf16_to_f32", "qwen3_op_dot", "qwen3_op_axpy",
     "last_status", "gemm", "rmsnorm", "rope", "silu_mul", "softmax", "argmax",
-    "residual_add", "bf16_to_f32", "device_status", "stream_ptr",
+    "residual_add", "bf16_to_f32", "device_status", "stream_ptr", "gemm_residual", "gemm_swiglu",
 ]
 
 
@@ -147,6 +147,27 @@ def gemm(a, b, mode=MODE_FAST, kblock=16, out=None, out_dtype=None, M=None, N=No
     check(lib().n550_gemm(stream_ptr(), mode, kblock, _dp(a), _dtype_code(a), a.stride(0),
                           _dp(b), b.stride(0), _dp(out), _dtype_code(out), out.stride(0),
                           M, N, K), "n550_gemm")
+    return out
+
+
+def gemm_residual(a, b, x):
+    """x += A . B^T (FP32 x, BF16 A and B) with the fused residual epilogue."""
+    M, K = a.shape
+    N = b.shape[0]
+    check(lib().n550_gemm_residual(stream_ptr(), _dp(a), a.stride(0), _dp(b), b.stride(0), _dp(x),
+                                   x.stride(0), M, N, K), "n550_gemm_residual")
+    return x
+
+
+def gemm_swiglu(a, wg, wu, out=None):
+    """h = silu(A . Wg^T) * (A . Wu^T) in BF16 with the fused SwiGLU epilogue."""
+    import torch
+    M, K = a.shape
+    N = wg.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    check(lib().n550_gemm_swiglu(stream_ptr(), _dp(a), a.stride(0), _dp(wg), _dp(wu), wg.stride(0),
+                                 _dp(out), out.stride(0), M, N, K), "n550_gemm_swiglu")
     return out
 
 

@@ -258,8 +258,8 @@ __device__ __forceinline__ void bf16x8(const uint4 q, float (&f)[8]) {
 
 __global__ void __launch_bounds__(DC_THREADS)
 attn_decode_kernel(AttnDecodeArgs p) {
-    __shared__ float qs[2][HD];
-    __shared__ float ps[DC_WARPS][2][32];
+    __shared__ __align__(16) float qs[2][HD];
+    __shared__ __align__(16) float ps[DC_WARPS][2][32];
     __shared__ float wm[DC_WARPS][2], wl[DC_WARPS][2];
     __shared__ float wo[DC_WARPS][2][HD];
     const int split = blockIdx.x, kvh = blockIdx.y, s = blockIdx.z;
@@ -286,17 +286,25 @@ attn_decode_kernel(AttnDecodeArgs p) {
         const int t = base + lane;
         float s0 = -INFINITY, s1 = -INFINITY;
         if (t < end) {
+            // The whole K row (256 B) in 16 independent 16-byte loads; the
+            // query (both heads) comes from shared memory as float4 broadcasts.
             const uint4 *kr = (const uint4 *)(kbase + (size_t)t * HD);
+            uint4 kq[16];
+#pragma unroll
+            for (int c = 0; c < 16; c++) kq[c] = __ldg(kr + c);
             float a0 = 0.f, a1 = 0.f;
-#pragma unroll 4
+            const float4 *q0 = (const float4 *)qs[0], *q1 = (const float4 *)qs[1];
+#pragma unroll
             for (int c = 0; c < 16; c++) {
                 float kf[8];
-                bf16x8(__ldg(kr + c), kf);
-#pragma unroll
-                for (int e = 0; e < 8; e++) {
-                    a0 = fmaf(qs[0][c * 8 + e], kf[e], a0);
-                    a1 = fmaf(qs[1][c * 8 + e], kf[e], a1);
-                }
+                bf16x8(kq[c], kf);
+                const float4 x0 = q0[2 * c], x1 = q0[2 * c + 1], y0 = q1[2 * c], y1 = q1[2 * c + 1];
+                a0 = fmaf(x0.x, kf[0], a0); a0 = fmaf(x0.y, kf[1], a0); a0 = fmaf(x0.z, kf[2], a0);
+                a0 = fmaf(x0.w, kf[3], a0); a0 = fmaf(x1.x, kf[4], a0); a0 = fmaf(x1.y, kf[5], a0);
+                a0 = fmaf(x1.z, kf[6], a0); a0 = fmaf(x1.w, kf[7], a0);
+                a1 = fmaf(y0.x, kf[0], a1); a1 = fmaf(y0.y, kf[1], a1); a1 = fmaf(y0.z, kf[2], a1);
+                a1 = fmaf(y0.w, kf[3], a1); a1 = fmaf(y1.x, kf[4], a1); a1 = fmaf(y1.y, kf[5], a1);
+                a1 = fmaf(y1.z, kf[6], a1); a1 = fmaf(y1.w, kf[7], a1);
             }
             s0 = a0;
             s1 = a1;

@@ -78,10 +78,23 @@ int device_gemm(cudaStream_t st, int mode, int kblock, const void *a, int a_type
     }
     const int epi = c_type == N550_F32 ? TC_EPI_F32 : TC_EPI_BF16;
     int rc;
+    int kt;
     if (M <= 8 && launch_gemv(st, epi, abf, ldab, b, ldb, c, ldc, M, N, K) == N550_OK) {
         rc = N550_OK;
+    } else if (M < 1024 && tc_shape_ok(abf, ldab, b, ldb, K) &&
+               tc_splitk_plan(M, N, K, epi, 128, &kt) > 1) {
+        // skinny M: split the K loop, partials in a stream-ordered workspace
+        const size_t ws_bytes = (size_t)8 * M * N * 4;
+        float *ws = nullptr;
+        if (cudaMallocAsync((void **)&ws, ws_bytes, st) != cudaSuccess) {
+            (void)cudaGetLastError();
+            if (staged) cudaFreeAsync(staged, st);
+            return N550_ERR_OOM;
+        }
+        rc = launch_gemm_tc_splitk(st, epi, abf, ldab, b, ldb, nullptr, c, ldc, M, N, K, ws, ws_bytes);
+        cudaFreeAsync(ws, st);
     } else if (tc_shape_ok(abf, ldab, b, ldb, K)) {
-        rc = launch_gemm_tc(st, epi, 128, abf, ldab, b, ldb, nullptr, c, ldc, M, N, K, 0);
+        rc = launch_gemm_tc(st, epi, n550_tile_bn(M, N), abf, ldab, b, ldb, nullptr, c, ldc, M, N, K, 0);
     } else {
         rc = launch_gemm_simt(st, epi, abf, ldab, b, ldb, c, ldc, M, N, K);
     }
@@ -138,6 +151,26 @@ int host_op(float *x_out, const float *x_in, size_t nx, const void *y, size_t yb
 }
 
 inline void set_status(int s) { t_status = s; }
+
+// Tensor-core GEMM with epilogue `epi`; skinny M (< 1024) splits the K loop
+// with its partials in a stream-ordered workspace.
+int skinny_or_full(cudaStream_t st, int epi, const uint16_t *a, int lda, const uint16_t *b, int ldb,
+                   const uint16_t *b2, void *c, int ldc, int M, int N, int K) {
+    int kt;
+    if (M < 1024 && tc_splitk_plan(M, N, K, epi, 128, &kt) > 1) {
+        const size_t ws_bytes = (size_t)8 * M * N * (epi == TC_EPI_SILU_BF16 ? 2 : 1) * 4;
+        float *ws = nullptr;
+        if (cudaMallocAsync((void **)&ws, ws_bytes, st) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return N550_ERR_OOM;
+        }
+        const int rc = launch_gemm_tc_splitk(st, epi, a, lda, b, ldb, b2, c, ldc, M, N, K, ws, ws_bytes);
+        cudaFreeAsync(ws, st);
+        return rc;
+    }
+    return launch_gemm_tc(st, epi, n550_tile_bn(M, epi == TC_EPI_SILU_BF16 ? 2 * N : N), a, lda, b, ldb,
+                          b2, c, ldc, M, N, K, 0);
+}
 
 // ---- staging area of n550_gemm_f32a_noalloc ----
 // 4 Mi BF16 elements (8 MiB) in every GPU that loads the library. Its host
@@ -319,6 +352,38 @@ int n550_gemm(void *stream, int mode, int kblock, const void *a, int a_type, int
                        ldc, M, N, K);
 }
 
+int n550_gemm_tile_config(int bn) {
+    if (bn != 0 && bn != 128 && bn != 256) return N550_ERR_ARG;
+    g_tile_bn = bn;
+    return N550_OK;
+}
+
+int n550_gemm_residual(void *stream, const uint16_t *a, int lda, const uint16_t *b, int ldb,
+                       float *x, int ldx, int M, int N, int K) {
+    cudaStream_t st = (cudaStream_t)stream;
+    if (M < 0 || N < 0 || K < 0 || (M && N && (!x || (K && (!a || !b)))) || lda < K || ldb < K ||
+        ldx < N)
+        return N550_ERR_ARG;
+    if (M == 0 || N == 0 || K == 0) return N550_OK;
+    if (M <= 8 && launch_gemv(st, TC_EPI_RESID_F32, a, lda, b, ldb, x, ldx, M, N, K) == N550_OK)
+        return N550_OK;
+    if (tc_shape_ok(a, lda, b, ldb, K))
+        return skinny_or_full(st, TC_EPI_RESID_F32, a, lda, b, ldb, nullptr, x, ldx, M, N, K);
+    return launch_gemm_simt(st, TC_EPI_RESID_F32, a, lda, b, ldb, x, ldx, M, N, K);
+}
+
+int n550_gemm_swiglu(void *stream, const uint16_t *a, int lda, const uint16_t *wg,
+                     const uint16_t *wu, int ldw, uint16_t *h, int ldh, int M, int N, int K) {
+    cudaStream_t st = (cudaStream_t)stream;
+    if (M < 0 || N < 0 || K <= 0 || (M && N && (!h || !a || !wg || !wu)) || lda < K || ldw < K ||
+        ldh < N)
+        return N550_ERR_ARG;
+    if (M == 0 || N == 0) return N550_OK;
+    if (!tc_shape_ok(a, lda, wg, ldw, K) || !tc_shape_ok(a, lda, wu, ldw, K))
+        return N550_ERR_UNSUPPORTED;
+    return skinny_or_full(st, TC_EPI_SILU_BF16, a, lda, wg, ldw, wu, h, ldh, M, N, K);
+}
+
 int n550_rmsnorm(void *stream, void *out, int out_type, const float *x, const uint16_t *w,
                  int rows, int n, float eps) {
     return launch_rmsnorm((cudaStream_t)stream, out, out_type, x, w, rows, n, eps);
@@ -372,7 +437,7 @@ int n550_gemm_f32a_noalloc(void *stream, const float *a, int lda, const uint16_t
     const int epi = c_type == N550_F32 ? TC_EPI_F32 : TC_EPI_BF16;
     if (M <= 8 && launch_gemv(st, epi, stage, ldab, b, ldb, c, ldc, M, N, K) == N550_OK) return N550_OK;
     if (tc_shape_ok(stage, ldab, b, ldb, K))
-        return launch_gemm_tc(st, epi, 128, stage, ldab, b, ldb, nullptr, c, ldc, M, N, K, 0);
+        return launch_gemm_tc(st, epi, n550_tile_bn(M, N), stage, ldab, b, ldb, nullptr, c, ldc, M, N, K, 0);
     return launch_gemm_simt(st, epi, stage, ldab, b, ldb, c, ldc, M, N, K);
 }
 

@@ -19,6 +19,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "gemm_tc.h"
 
@@ -37,53 +39,204 @@ struct TcCfg {
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr int EPI_BYTES = 4 * 32 * 32 * 4;   // one 32x32-word tile per epilogue warp
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
 };
 
+// silu(g) * u (ops_scalar.c:46-51) with the fast exponential and divide: the
+// fused SwiGLU epilogue is tolerance-checked (relative error ~1e-6).
 __device__ __forceinline__ float silu_mul_f(float g, float u) {
-    return (g / (1.0f + expf(-g))) * u;   // ops_scalar.c:46-51
+    return __fdividef(g, 1.0f + __expf(-g)) * u;
 }
 
-// Epilogue for one 32-column chunk of one row. `v` holds FP32 accumulators.
-template <int EPI>
-__device__ __forceinline__ void store_chunk(const TcEpilogue &ep, int m, int n, int ncols_valid,
-                                            const float (&v)[32]) {
-    if (EPI == TC_EPI_F32) {
-        float *dst = (float *)ep.c + (size_t)m * ep.ldc + n;
-        if (ncols_valid == 32 && ep.vec_ok) {
+// ---- epilogue staging -------------------------------------------------------
+// Each epilogue warp owns a 32 x 32-word shared tile. After tcgen05.ld, lane r
+// holds 32 consecutive columns of row r; the tile turns that into stores of
+// whole 128-byte (FP32) or 64-byte (BF16) row segments, 4 or 8 rows per
+// instruction. 16-byte chunk c of row r is placed so that the 8 lanes of a
+// quarter-warp always hit 8 different bank groups, on the write and the read.
+__device__ __forceinline__ int f32_word(int r, int c) { return r * 32 + ((c ^ (r & 7)) << 2); }
+__device__ __forceinline__ int b16_word(int r, int c) {
+    return r * 32 + (((c ^ ((r >> 1) & 3)) + 4 * (r & 1)) << 2);
+}
+
+__device__ __forceinline__ void stage_f32(uint32_t *stg, int lane, const uint32_t (&v)[32]) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-                *(float4 *)(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        } else {
-            for (int j = 0; j < ncols_valid; j++) dst[j] = v[j];
+    for (int c = 0; c < 8; c++)
+        *(uint4 *)(stg + f32_word(lane, c)) = make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+}
+
+__device__ __forceinline__ void stage_bf16(uint32_t *stg, int lane, const float (&v)[32]) {
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+        *(uint4 *)(stg + b16_word(lane, c)) =
+            make_uint4(pack_bf16x2(v[8 * c], v[8 * c + 1]), pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
+                       pack_bf16x2(v[8 * c + 4], v[8 * c + 5]), pack_bf16x2(v[8 * c + 6], v[8 * c + 7]));
+}
+
+__device__ __forceinline__ float wf(uint32_t w) { return __uint_as_float(w); }
+
+// Rows row0 + r (r < 32) of an FP32 destination; 4 columns per lane. For the
+// residual, all 8 reads of x are issued before any store so that they overlap.
+template <bool RESID>
+__device__ __forceinline__ void flush_f32(const uint32_t *stg, int lane, float *C, int ldc, int row0,
+                                          int M, int n, int N, bool vec_ok) {
+    const int c = lane & 7;
+    const int col = n + 4 * c;
+    const bool vec = vec_ok && col + 4 <= N;
+    float4 xv[8];
+    if (RESID) {
+#pragma unroll
+        for (int it = 0; it < 8; it++) {
+            const int m = row0 + it * 4 + (lane >> 3);
+            xv[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (m < M && vec) xv[it] = __ldcs((const float4 *)(C + (size_t)m * ldc + col));
         }
-    } else if (EPI == TC_EPI_BF16) {
-        uint16_t *dst = (uint16_t *)ep.c + (size_t)m * ep.ldc + n;
-        if (ncols_valid == 32 && ep.vec_ok) {
+    }
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-                uint4 q;
-                q.x = pack_bf16x2(v[j], v[j + 1]);
-                q.y = pack_bf16x2(v[j + 2], v[j + 3]);
-                q.z = pack_bf16x2(v[j + 4], v[j + 5]);
-                q.w = pack_bf16x2(v[j + 6], v[j + 7]);
-                *(uint4 *)(dst + j) = q;
-            }
+    for (int it = 0; it < 8; it++) {
+        const int r = it * 4 + (lane >> 3);
+        const uint4 q = *(const uint4 *)(stg + f32_word(r, c));
+        const int m = row0 + r;
+        if (m >= M) continue;
+        float *dst = C + (size_t)m * ldc + col;
+        if (vec) {
+            if (RESID)
+                *(float4 *)dst = make_float4(xv[it].x + wf(q.x), xv[it].y + wf(q.y),
+                                             xv[it].z + wf(q.z), xv[it].w + wf(q.w));
+            else
+                *(float4 *)dst = make_float4(wf(q.x), wf(q.y), wf(q.z), wf(q.w));
         } else {
-            for (int j = 0; j < ncols_valid; j++) dst[j] = f32_to_bf16_rne(v[j]);
+            const float v[4] = {wf(q.x), wf(q.y), wf(q.z), wf(q.w)};
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                if (col + e < N) { if (RESID) dst[e] += v[e]; else dst[e] = v[e]; }
         }
-    } else if (EPI == TC_EPI_RESID_F32) {
-        // x += y in FP32 (ops_scalar.c:53-55), y = this GEMM's output.
-        float *dst = (float *)ep.c + (size_t)m * ep.ldc + n;
-        if (ncols_valid == 32 && ep.vec_ok) {
+    }
+}
+
+// Rows of a BF16 destination; rowptr(r) gives the address of column `n` of
+// tile row r (or nullptr to skip the row); 8 columns per lane.
+template <class RowPtr>
+__device__ __forceinline__ void flush_bf16(const uint32_t *stg, int lane, RowPtr rowptr, int n,
+                                           int N, bool vec_ok) {
+    const int c = lane & 3;
+    const int col = n + 8 * c;
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-                float4 x = *(float4 *)(dst + j);
-                x.x += v[j]; x.y += v[j + 1]; x.z += v[j + 2]; x.w += v[j + 3];
-                *(float4 *)(dst + j) = x;
-            }
+    for (int it = 0; it < 4; it++) {
+        const int r = it * 8 + (lane >> 2);
+        const uint4 q = *(const uint4 *)(stg + b16_word(r, c));
+        uint16_t *dst = rowptr(r);
+        if (!dst) continue;
+        dst += 8 * c;
+        if (vec_ok && col + 8 <= N) {
+            *(uint4 *)dst = q;
         } else {
-            for (int j = 0; j < ncols_valid; j++) dst[j] += v[j];
+            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int e = 0; e < 8; e++)
+                if (col + e < N) dst[e] = (uint16_t)((e & 1) ? (w[e >> 1] >> 16) : (w[e >> 1] & 0xFFFFu));
+        }
+    }
+}
+
+__device__ __forceinline__ void load_chunk(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(taddr, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+}
+
+// Fused QKV epilogue (qwen3.c:477-511). A 128-column tile is one head of the
+// [q 16 | k 8 | v 8] x 128 qkv row. q and k heads: RMSNorm over the head
+// (qk_norm, qwen3.c:287-292, sum of squares in the order and rounding of
+// ops_scalar.c:12), RoPE pairs (i, i + 64) from the (cos, sin) table
+// (ops_scalar.c:21-35); q goes to the query buffer, k to the KV cache; v heads
+// go to the cache unchanged. The accumulator is read from TMEM twice (sum of
+// squares, then values) so no thread holds more than 64 of them.
+__device__ __forceinline__ void epilogue_qkv(const TcQkv &p, uint32_t *stg, int lane, uint32_t taddr,
+                                             int row0, int M, int head, uint64_t *tempty_bar) {
+    const int m = row0 + lane;
+    const int pos = p.tok_pos[m < M ? m : M - 1];
+    const bool normed = head < 24;
+    const uint16_t *w = head < 16 ? p.q_norm : p.k_norm;
+    float scale = 1.f;
+    if (normed) {
+        float ss = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 4; c++) {
+            float v[32];
+            load_chunk(taddr + 32 * c, v);
+#pragma unroll
+            for (int j = 0; j < 32; j++) ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
+        }
+        scale = 1.0f / sqrtf(ss / 128.0f + p.eps);
+    }
+    const int kvh = (head - 16) & 7;
+    uint16_t *cache = head < 24 ? p.kc : p.vc;
+#pragma unroll 1
+    for (int c = 0; c < 2; c++) {
+        float a[32], b[32];
+        load_chunk(taddr + 32 * c, a);
+        load_chunk(taddr + 64 + 32 * c, b);
+        if (c == 1 && tempty_bar) { tc_fence_before(); mbar_arrive(tempty_bar); }
+        if (normed) {
+            // 16-byte loads: 2 (cos, sin) pairs, 8 norm weights per load.
+            const float4 *cs4 = (const float4 *)(p.rope + (size_t)pos * 64 + 32 * c);
+            const uint4 *w_lo = (const uint4 *)(w + 32 * c);
+            const uint4 *w_hi = (const uint4 *)(w + 64 + 32 * c);
+#pragma unroll
+            for (int j8 = 0; j8 < 4; j8++) {
+                const uint4 wl = __ldg(w_lo + j8), wh = __ldg(w_hi + j8);
+                const uint32_t wlw[4] = {wl.x, wl.y, wl.z, wl.w}, whw[4] = {wh.x, wh.y, wh.z, wh.w};
+#pragma unroll
+                for (int j2 = 0; j2 < 4; j2++) {
+                    const float4 t = __ldg(cs4 + j8 * 4 + j2);
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const int j = j8 * 8 + j2 * 2 + e;
+                        const float wa = __uint_as_float(e ? (wlw[j2] & 0xFFFF0000u) : (wlw[j2] << 16));
+                        const float wb = __uint_as_float(e ? (whw[j2] & 0xFFFF0000u) : (whw[j2] << 16));
+                        const float cs = e ? t.z : t.x, sn = e ? t.w : t.y;
+                        const float x0 = a[j] * scale * wa;
+                        const float x1 = b[j] * scale * wb;
+                        a[j] = x0 * cs - x1 * sn;
+                        b[j] = x1 * cs + x0 * sn;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+            const int d0 = 32 * c + 64 * half;
+            if (head < 16 && p.q_f32) {
+                uint32_t bits[32];
+#pragma unroll
+                for (int j = 0; j < 32; j++) bits[j] = __float_as_uint(half ? b[j] : a[j]);
+                stage_f32(stg, lane, bits);
+                __syncwarp();
+                const int n = head * 128 + d0;
+                flush_f32<false>(stg, lane, p.q_f32, p.ldq, row0, M, n, n + 32, true);
+            } else {
+                if (half) stage_bf16(stg, lane, b);
+                else stage_bf16(stg, lane, a);
+                __syncwarp();
+                if (head < 16) {
+                    flush_bf16(stg, lane, [&](int r) -> uint16_t * {
+                        const int mr = row0 + r;
+                        return mr < M ? p.q_bf16 + (size_t)mr * p.ldq + head * 128 + d0 : nullptr;
+                    }, 0, 32, true);
+                } else {
+                    flush_bf16(stg, lane, [&](int r) -> uint16_t * {
+                        const int mr = row0 + r;
+                        if (mr >= M) return nullptr;
+                        const size_t slot = ((size_t)p.tok_seq[mr] * 28 + p.layer) * 8 + kvh;
+                        return cache + (slot * p.max_len + p.tok_pos[mr]) * 128 + d0;
+                    }, 0, 32, true);
+                }
+            }
+            __syncwarp();
         }
     }
 }
@@ -93,7 +246,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmB2,
-               const TcEpilogue ep, int M, int N, int K) {
+               const TcEpilogue ep, int M, int N, int K, int m_fast, int ksplit,
+               int kt_per, float *ws) {
     using Cfg = TcCfg<BN>;
     constexpr int STAGES = Cfg::STAGES;
     constexpr bool SILU = (EPI == TC_EPI_SILU_BF16);
@@ -102,7 +256,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t *full = (uint64_t *)(base + STAGES * Cfg::STAGE_BYTES);
+    // [stage ring][epilogue staging tiles][barriers]
+    uint64_t *full = (uint64_t *)(base + STAGES * Cfg::STAGE_BYTES + Cfg::EPI_BYTES);
     uint64_t *empty = full + STAGES;
     uint64_t *tfull = empty + STAGES;       // [2]
     uint64_t *tempty = tfull + 2;           // [2]
@@ -114,8 +269,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
 
     const int num_m = (M + BM - 1) / BM;
     const int num_n = (N + OUT_N - 1) / OUT_N;
-    const int total = num_m * num_n;
     const int num_k = (K + BK - 1) / BK;
+    // Work unit u = (tile u / ksplit, K slice u % ksplit); with ksplit > 1 each
+    // unit stores its FP32 partial tile into ws[slice] and a reduce kernel
+    // applies the epilogue.
+    const int total = num_m * num_n * ksplit;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -141,9 +299,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-                const int mb = t / num_n, nb = t % num_n;
-                for (int kt = 0; kt < num_k; kt++) {
+            for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+                const int t = u / ksplit, sk = u - t * ksplit;
+                const int mb = m_fast ? t % num_m : t / num_n, nb = m_fast ? t / num_m : t % num_n;
+                const int kt0 = sk * kt_per, kt1 = min(num_k, kt0 + kt_per);
+                for (int kt = kt0; kt < kt1; kt++) {
                     if (!mbar_wait(&empty[stage], phase ^ 1)) { ok = false; break; }
                     uint8_t *sA = base + stage * Cfg::STAGE_BYTES;
                     uint8_t *sB = sA + Cfg::A_BYTES;
@@ -174,11 +334,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             int ab = 0;
             uint32_t aphase = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+            for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+                const int sk = u % ksplit;
+                const int kt0 = sk * kt_per, kt1 = min(num_k, kt0 + kt_per);
                 if (!mbar_wait(&tempty[ab], aphase ^ 1)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(ab * BN);
-                for (int kt = 0; kt < num_k; kt++) {
+                for (int kt = kt0; kt < kt1; kt++) {
                     if (!mbar_wait(&full[stage], phase)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(base + stage * Cfg::STAGE_BYTES);
@@ -187,7 +349,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     for (int ks = 0; ks < BK / UMMA_K; ks++) {
                         umma_bf16(d_tmem, umma_desc_sw128(a0 + ks * UMMA_K * 2),
                                   umma_desc_sw128(b0 + ks * UMMA_K * 2), idesc,
-                                  (kt | ks) != 0);
+                                  (kt != kt0 || ks != 0) ? 1u : 0u);
                     }
                     umma_commit(&empty[stage]);
                     if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -203,30 +365,60 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
         const int q = warp & 3;                 // TMEM lane quarter of this warp
-        const int row = q * 32 + lane;
+        uint32_t *stg = (uint32_t *)(base + STAGES * Cfg::STAGE_BYTES) + (warp - 2) * 32 * 32;
         int ab = 0;
         uint32_t aphase = 0;
-        for (int t = blockIdx.x; t < total; t += gridDim.x) {
-            const int mb = t / num_n, nb = t % num_n;
+        for (int u = blockIdx.x; u < total; u += gridDim.x) {
+            const int t = u / ksplit, sk = u - t * ksplit;
+            const int mb = m_fast ? t % num_m : t / num_n, nb = m_fast ? t / num_m : t % num_n;
             if (!mbar_wait(&tfull[ab], aphase)) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
-            const int m = mb * BM + row;
-            if (SILU) {
+            const int row0 = mb * BM + q * 32;          // first row of this warp's quarter
+            if (ksplit > 1) {
+                // Partial sums of K slice sk: raw FP32 accumulators into
+                // ws[sk][M][ldw]; SwiGLU tiles put gate at column n, up at N + n.
+                const int ldw = SILU ? 2 * N : N;
+                float *slice = ws + (size_t)sk * M * ldw;
+#pragma unroll 1
+                for (int cch = 0; cch < BN; cch += 32) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(taddr + cch, r);
+                    tmem_ld_wait();
+                    if (cch + 32 == BN) { tc_fence_before(); mbar_arrive(&tempty[ab]); }
+                    const int n = SILU ? (cch < OUT_N ? nb * OUT_N + cch : N + nb * OUT_N + cch - OUT_N)
+                                       : nb * BN + cch;
+                    const int nlim = SILU ? (cch < OUT_N ? N : 2 * N) : N;
+                    stage_f32(stg, lane, r);
+                    __syncwarp();
+                    flush_f32<false>(stg, lane, slice, ldw, row0, M, n, nlim,
+                                     (ldw % 4) == 0 && (n % 4) == 0);
+                    __syncwarp();
+                }
+            } else if (EPI == TC_EPI_QKV_ROPE) {
+#pragma unroll 1
+                for (int hh = 0; hh < BN / 128; hh++)
+                    epilogue_qkv(ep.qkv, stg, lane, taddr + hh * 128, row0, M, nb * (BN / 128) + hh,
+                                 hh + 1 == BN / 128 ? &tempty[ab] : nullptr);
+            } else if (SILU) {
 #pragma unroll 1
                 for (int cch = 0; cch < OUT_N; cch += 32) {
-                    uint32_t rg[32], ru[32];
-                    tmem_ld_32x32b_x32(taddr + cch, rg);
-                    tmem_ld_32x32b_x32(taddr + OUT_N + cch, ru);
-                    tmem_ld_wait();
-                    const int n = nb * OUT_N + cch;
-                    if (m < M && n < N) {
-                        float v[32];
+                    float g[32], u[32];
+                    load_chunk(taddr + cch, g);
+                    load_chunk(taddr + OUT_N + cch, u);
+                    if (cch + 32 == OUT_N) { tc_fence_before(); mbar_arrive(&tempty[ab]); }
+                    float h[32];
 #pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            v[j] = silu_mul_f(__uint_as_float(rg[j]), __uint_as_float(ru[j]));
-                        store_chunk<TC_EPI_BF16>(ep, m, n, min(32, N - n), v);
-                    }
+                    for (int j = 0; j < 32; j++) h[j] = silu_mul_f(g[j], u[j]);
+                    stage_bf16(stg, lane, h);
+                    __syncwarp();
+                    const int n = nb * OUT_N + cch;
+                    uint16_t *C = (uint16_t *)ep.c;
+                    flush_bf16(stg, lane, [&](int r) -> uint16_t * {
+                        const int m = row0 + r;
+                        return m < M ? C + (size_t)m * ep.ldc + n : nullptr;
+                    }, n, N, ep.vec_ok);
+                    __syncwarp();
                 }
             } else {
 #pragma unroll 1
@@ -234,17 +426,28 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(taddr + cch, r);
                     tmem_ld_wait();
+                    if (cch + 32 == BN) { tc_fence_before(); mbar_arrive(&tempty[ab]); }
                     const int n = nb * BN + cch;
-                    if (m < M && n < N) {
+                    if (EPI == TC_EPI_BF16) {
                         float v[32];
 #pragma unroll
                         for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
-                        store_chunk<EPI>(ep, m, n, min(32, N - n), v);
+                        stage_bf16(stg, lane, v);
+                        __syncwarp();
+                        uint16_t *C = (uint16_t *)ep.c;
+                        flush_bf16(stg, lane, [&](int rr) -> uint16_t * {
+                            const int m = row0 + rr;
+                            return m < M ? C + (size_t)m * ep.ldc + n : nullptr;
+                        }, n, N, ep.vec_ok);
+                    } else {
+                        stage_f32(stg, lane, r);
+                        __syncwarp();
+                        flush_f32<EPI == TC_EPI_RESID_F32>(stg, lane, (float *)ep.c, ep.ldc, row0, M, n, N,
+                                                           ep.vec_ok);
                     }
+                    __syncwarp();
                 }
             }
-            tc_fence_before();
-            mbar_arrive(&tempty[ab]);
             if (++ab == 2) { ab = 0; aphase ^= 1; }
         }
     }
@@ -302,7 +505,7 @@ int num_sms() {
 template <int BN, int EPI>
 int launch_impl(cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tb,
                 const CUtensorMap &tb2, const TcEpilogue &ep, int M, int N, int K,
-                int max_ctas) {
+                int max_ctas, int ksplit = 1, int kt_per = 1 << 30, float *ws = nullptr) {
     using Cfg = TcCfg<BN>;
     static bool attr_done[64] = {};
     int dev = 0;
@@ -314,16 +517,132 @@ int launch_impl(cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tb,
         attr_done[dev] = true;
     }
     constexpr int OUT_N = (EPI == TC_EPI_SILU_BF16) ? BN / 2 : BN;
-    const long long tiles = (long long)((M + BM - 1) / BM) * ((N + OUT_N - 1) / OUT_N);
+    const long long tiles = (long long)((M + BM - 1) / BM) * ((N + OUT_N - 1) / OUT_N) * ksplit;
     int grid = num_sms();
     if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
     if (tiles < grid) grid = (int)tiles;
-    gemm_tc_kernel<BN, EPI><<<grid, THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tb2, ep, M, N, K);
+    // Resident CTAs work on consecutive tiles: walk M fastest when the weight
+    // operand is the larger one (e.g. the 311 MB lm_head), so each B tile is
+    // fetched from HBM once and reused from L2 by the CTAs of all M tiles;
+    // otherwise walk N fastest so that A rows are shared.
+    const int m_fast = (long long)N * (EPI == TC_EPI_SILU_BF16 ? 2 : 1) > (long long)M;
+    gemm_tc_kernel<BN, EPI><<<grid, THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tb2, ep, M, N, K, m_fast,
+                                                                     ksplit, kt_per, ws);
     N550_LAUNCH_CHECK();
     return N550_OK;
 }
 
+// Sum of the ksplit partial tiles in slice order, then the epilogue.
+template <int EPI>
+__global__ void splitk_reduce_kernel(const float *__restrict__ ws, int ksplit, int M, int N, void *c,
+                                     int ldc) {
+    const int ldw = EPI == TC_EPI_SILU_BF16 ? 2 * N : N;
+    const size_t slice = (size_t)M * ldw, total = (size_t)M * N;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const int m = (int)(i / N), n = (int)(i % N);
+        const float *p = ws + (size_t)m * ldw + n;
+        float acc = 0.f;
+        for (int sk = 0; sk < ksplit; sk++) acc += p[sk * slice];
+        if (EPI == TC_EPI_SILU_BF16) {
+            float up = 0.f;
+            for (int sk = 0; sk < ksplit; sk++) up += p[sk * slice + N];
+            ((uint16_t *)c)[(size_t)m * ldc + n] = f32_to_bf16_rne(silu_mul_f(acc, up));
+        } else if (EPI == TC_EPI_BF16) {
+            ((uint16_t *)c)[(size_t)m * ldc + n] = f32_to_bf16_rne(acc);
+        } else if (EPI == TC_EPI_RESID_F32) {
+            ((float *)c)[(size_t)m * ldc + n] += acc;
+        } else {
+            ((float *)c)[(size_t)m * ldc + n] = acc;
+        }
+    }
+}
+
 }  // namespace
+
+int launch_gemm_tc_qkv(cudaStream_t st, const uint16_t *a, int lda, const uint16_t *w,
+                       const TcQkv &q, int M, int K, int max_ctas) {
+    if (M <= 0) return N550_OK;
+    if (!tc_shape_ok(a, lda, w, K, K)) return N550_ERR_UNSUPPORTED;
+    if ((!q.q_bf16 && !q.q_f32) || !q.kc || !q.vc || !q.tok_pos || !q.tok_seq || !q.rope ||
+        (q.ldq % 8))
+        return N550_ERR_ARG;
+    int rc = get_encoder();
+    if (rc) return rc;
+    const int bn = n550_tile_bn(M, 4096);
+    CUtensorMap ta, tb;
+    if ((rc = make_tmap(&ta, a, M, K, lda, BM))) return rc;
+    if ((rc = make_tmap(&tb, w, 4096, K, K, bn))) return rc;
+    TcEpilogue ep{};
+    ep.qkv = q;
+    ep.vec_ok = 1;
+    if (bn == 256) return launch_impl<256, TC_EPI_QKV_ROPE>(st, ta, tb, tb, ep, M, 4096, K, max_ctas);
+    return launch_impl<128, TC_EPI_QKV_ROPE>(st, ta, tb, tb, ep, M, 4096, K, max_ctas);
+}
+
+int g_tile_bn = 0;   // 0: automatic
+
+int n550_tile_bn(int M, int N) {
+    if (g_tile_bn) return g_tile_bn;
+    // 256-wide tiles halve the operand traffic per MMA (measured on prefill
+    // shapes: 1.3 PFLOP/s vs 0.85); narrow outputs and skinny M keep 128 so
+    // that there are enough tiles to occupy the SMs.
+    return (M >= 1024 && N >= 1024) ? 256 : 128;
+}
+
+int tc_splitk_plan(int M, int N, int K, int epi, int bn, int *kt_per) {
+    const int out_n = epi == TC_EPI_SILU_BF16 ? bn / 2 : bn;
+    const long long tiles = (long long)((M + BM - 1) / BM) * ((N + out_n - 1) / out_n);
+    const int num_k = (K + BK - 1) / BK;
+    const int sms = num_sms();
+    int ks = (int)(sms / (tiles > 0 ? tiles : 1));
+    ks = std::min(ks, std::min(num_k / 2, 8));
+    if (ks < 2) { *kt_per = num_k; return 1; }
+    *kt_per = (num_k + ks - 1) / ks;
+    return (num_k + *kt_per - 1) / *kt_per;
+}
+
+int launch_gemm_tc_splitk(cudaStream_t st, int epi, const uint16_t *a, int lda, const uint16_t *b,
+                          int ldb, const uint16_t *b2, void *c, int ldc, int M, int N, int K,
+                          float *ws, size_t ws_bytes) {
+    if (M <= 0 || N <= 0) return N550_OK;
+    const int bn = 128;
+    int kt_per = 0;
+    const int ks = tc_splitk_plan(M, N, K, epi, bn, &kt_per);
+    const size_t need = (size_t)ks * M * (epi == TC_EPI_SILU_BF16 ? 2 * N : N) * 4;
+    if (ks == 1 || !ws || need > ws_bytes)
+        return launch_gemm_tc(st, epi, bn, a, lda, b, ldb, b2, c, ldc, M, N, K, 0);
+    if (!tc_shape_ok(a, lda, b, ldb, K)) return N550_ERR_UNSUPPORTED;
+    if (epi != TC_EPI_F32 && epi != TC_EPI_BF16 && epi != TC_EPI_RESID_F32 && epi != TC_EPI_SILU_BF16)
+        return N550_ERR_ARG;
+    int rc = get_encoder();
+    if (rc) return rc;
+    const int brows = (epi == TC_EPI_SILU_BF16) ? bn / 2 : bn;
+    CUtensorMap ta, tb, tb2;
+    if ((rc = make_tmap(&ta, a, M, K, lda, BM))) return rc;
+    if ((rc = make_tmap(&tb, b, N, K, ldb, brows))) return rc;
+    if (epi == TC_EPI_SILU_BF16) {
+        if ((rc = make_tmap(&tb2, b2, N, K, ldb, brows))) return rc;
+    } else {
+        tb2 = tb;
+    }
+    TcEpilogue ep{};
+    if (epi == TC_EPI_SILU_BF16)
+        rc = launch_impl<128, TC_EPI_SILU_BF16>(st, ta, tb, tb2, ep, M, N, K, 0, ks, kt_per, ws);
+    else
+        rc = launch_impl<128, TC_EPI_F32>(st, ta, tb, tb2, ep, M, N, K, 0, ks, kt_per, ws);
+    if (rc) return rc;
+    const size_t total = (size_t)M * N;
+    const int grid = (int)std::min<size_t>((total + 255) / 256, 148 * 8);
+    switch (epi) {
+    case TC_EPI_F32: splitk_reduce_kernel<TC_EPI_F32><<<grid, 256, 0, st>>>(ws, ks, M, N, c, ldc); break;
+    case TC_EPI_BF16: splitk_reduce_kernel<TC_EPI_BF16><<<grid, 256, 0, st>>>(ws, ks, M, N, c, ldc); break;
+    case TC_EPI_RESID_F32: splitk_reduce_kernel<TC_EPI_RESID_F32><<<grid, 256, 0, st>>>(ws, ks, M, N, c, ldc); break;
+    default: splitk_reduce_kernel<TC_EPI_SILU_BF16><<<grid, 256, 0, st>>>(ws, ks, M, N, c, ldc); break;
+    }
+    N550_LAUNCH_CHECK();
+    return N550_OK;
+}
 
 bool tc_shape_ok(const void *a, int lda, const void *b, int ldb, int K) {
     return K > 0 && (K % 8) == 0 && (lda % 8) == 0 && (ldb % 8) == 0 &&

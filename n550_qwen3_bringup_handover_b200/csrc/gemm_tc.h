@@ -11,14 +11,35 @@ enum {
     TC_EPI_F32 = 0,        // C (FP32) = acc
     TC_EPI_BF16 = 1,       // C (BF16) = rne(acc)
     TC_EPI_RESID_F32 = 2,  // C (FP32) += acc           (residual add fused)
-    TC_EPI_SILU_BF16 = 3   // C (BF16) = silu(acc_gate) * acc_up (SwiGLU fused)
+    TC_EPI_SILU_BF16 = 3,  // C (BF16) = silu(acc_gate) * acc_up (SwiGLU fused)
+    TC_EPI_QKV_ROPE = 4    // per-head RMSNorm + RoPE of q/k, q out, k/v into the KV cache
+};
+
+// Operands of the fused QKV epilogue (qwen3.c:477-511): a 128-column tile is
+// one head of the [q 16 | k 8 | v 8] x 128 qkv row.
+struct TcQkv {
+    uint16_t *q_bf16;          // [M, ldq] BF16 queries, or NULL
+    float *q_f32;              // [M, ldq] FP32 queries, or NULL
+    int ldq;
+    uint16_t *kc, *vc;         // KV cache [seq][layer][kv_head][pos][128]
+    int layer, max_len;
+    const int32_t *tok_pos, *tok_seq;   // per row
+    const uint16_t *q_norm, *k_norm;    // BF16 [128]
+    const float2 *rope;        // [max_len][64] (cos, sin) of pos * inv_freq[i]
+    float eps;
 };
 
 struct TcEpilogue {
     void *c;
     int ldc;
     int vec_ok;            // 16-byte vector stores allowed
+    TcQkv qkv;
 };
+
+// Tile width (BN) used by the fast GEMMs for an M x N output: 128 or 256;
+// g_tile_bn (n550_gemm_tile_config) overrides the automatic choice.
+extern int g_tile_bn;
+int n550_tile_bn(int M, int N);
 
 // True when the tensor-core path takes these operands (TMA constraints).
 bool tc_shape_ok(const void *a, int lda, const void *b, int ldb, int K);
@@ -30,6 +51,21 @@ bool tc_shape_ok(const void *a, int lda, const void *b, int ldb, int K);
 int launch_gemm_tc(cudaStream_t st, int epi, int bn, const uint16_t *a, int lda,
                    const uint16_t *b, int ldb, const uint16_t *b2, void *c, int ldc,
                    int M, int N, int K, int max_ctas);
+
+// Skinny-M variant (decode): the K loop is split over up to 8 CTAs per tile
+// when the tile count alone cannot occupy the SMs; FP32 partials go to ws
+// (ws_bytes large enough for splits x M x N floats, 2N for SwiGLU) and a
+// reduce kernel sums them in slice order and applies the epilogue. Falls back
+// to launch_gemm_tc when no split is worthwhile or ws is too small.
+int launch_gemm_tc_splitk(cudaStream_t st, int epi, const uint16_t *a, int lda, const uint16_t *b,
+                          int ldb, const uint16_t *b2, void *c, int ldc, int M, int N, int K,
+                          float *ws, size_t ws_bytes);
+// Number of K slices launch_gemm_tc_splitk uses (1 = no split).
+int tc_splitk_plan(int M, int N, int K, int epi, int bn, int *kt_per);
+
+// The QKV projection with the fused per-head epilogue (N = 4096, BN = 128).
+int launch_gemm_tc_qkv(cudaStream_t st, const uint16_t *a, int lda, const uint16_t *w,
+                       const TcQkv &q, int M, int K, int max_ctas);
 
 // Exact-mode (AME numerics) GEMM on CUDA cores.
 int launch_gemm_exact(cudaStream_t st, const void *a, int a_type, int lda,

@@ -224,6 +224,16 @@ qknorm_rope_kv_kernel(const float *__restrict__ qkv, int ldqkv, const uint16_t *
     }
 }
 
+// (cos, sin) of pos * inv_freq[i] for every position and rotation pair: the
+// RoPE factors of ops_scalar.c:21-35, computed once per model.
+__global__ void rope_table_kernel(float2 *t, int max_len) {
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= max_len * 64) return;
+    float s, c;
+    sincosf((float)(idx >> 6) * c_inv_freq[idx & 63], &s, &c);
+    t[idx] = make_float2(c, s);
+}
+
 // Final RMSNorm of the last token of each sequence (qwen3.c:547-573 only
 // needs row NT-1): xl[i] = rmsnorm(x[i*Lc + Lc - 1]) in BF16.
 __global__ void __launch_bounds__(256)
@@ -300,6 +310,9 @@ struct n550_model {
     int32_t *tok_pos = nullptr, *tok_seq = nullptr, *next = nullptr, *host_tok = nullptr,
             *zero_seq = nullptr;
     float *part_m = nullptr, *part_l = nullptr, *part_o = nullptr;
+    float2 *rope = nullptr;                 // [max_len][64] (cos, sin)
+    float *ws = nullptr;                    // split-K partials of skinny GEMMs
+    size_t ws_bytes = 0;
 };
 
 namespace {
@@ -331,7 +344,7 @@ void model_release(n550_model *m) {
     for (cudaEvent_t e : m->prof.pool) cudaEventDestroy(e);
     void *ptrs[] = {m->blob, m->fused_qkv, m->kc, m->vc, m->x, m->qkv, m->qf, m->logits, m->xb,
                     m->qb, m->attn, m->h, m->xl, m->tmp_a, m->tmp_b, m->tok_pos, m->tok_seq,
-                    m->next, m->host_tok, m->zero_seq, m->part_m, m->part_l, m->part_o};
+                    m->next, m->host_tok, m->zero_seq, m->part_m, m->part_l, m->part_o, m->rope, m->ws};
     for (void *p : ptrs) if (p) cudaFree(p);
     delete m;
 }
@@ -384,12 +397,18 @@ int model_setup(n550_model *m) {
     ALLOC(m->part_m, slots * 4);
     ALLOC(m->part_l, slots * 4);
     ALLOC(m->part_o, slots * HDIM * 4);
+    ALLOC(m->rope, (size_t)c.max_len * 64 * sizeof(float2));
+    // split-K workspace: up to 8 slices of [rows < 1024][2 x 3072] FP32
+    m->ws_bytes = (size_t)8 * std::min<size_t>(T, 1023) * 2 * INTER * 4;
+    ALLOC(m->ws, m->ws_bytes);
 #undef ALLOC
     N550_CUDA_TRY(cudaMemset(m->zero_seq, 0, 4));
     N550_CUDA_TRY(cudaMemset(m->kc, 0, kv * 2));
     N550_CUDA_TRY(cudaMemset(m->vc, 0, kv * 2));
     int rc = ensure_rope_table();
     if (rc) return rc;
+    rope_table_kernel<<<(c.max_len * 64 + 255) / 256, 256>>>(m->rope, c.max_len);
+    N550_LAUNCH_CHECK();
     N550_CUDA_TRY(cudaDeviceSynchronize());
     return N550_OK;
 }
@@ -433,7 +452,10 @@ int mgemm(n550_model *m, cudaStream_t st, int epi, const uint16_t *a, int lda, c
         N550_LAUNCH_CHECK();
         return N550_OK;
     }
-    return launch_gemm_tc(st, epi, 128, a, lda, w, K, w2, c, ldc, M, N, K, 0);
+    if (M < 1024)   // skinny (decode, short prompts): split the K loop over more SMs
+        return launch_gemm_tc_splitk(st, epi, a, lda, w, K, w2, c, ldc, M, N, K, m->ws, m->ws_bytes);
+    return launch_gemm_tc(st, epi, n550_tile_bn(M, epi == TC_EPI_SILU_BF16 ? 2 * N : N), a, lda, w, K, w2, c,
+                          ldc, M, N, K, 0);
 }
 
 int launch_qknorm_rope_kv(n550_model *m, cudaStream_t st, int T, int l, bool decode) {
@@ -462,13 +484,30 @@ int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t
         if ((rc = (expr))) return rc;                 \
     } while (0)
     const bool exact = c.gemm_mode == N550_MODE_EXACT;
-    const int gu_kernels = exact ? 3 : (T <= 8 ? 3 : 1);
-    const int res_kernels = exact ? 2 : 1;
+    int kt;
+    const bool split = !exact && T > 8 && T < 1024;
+    const int gu_kernels = exact ? 3 : (T <= 8 ? 3 : (split && tc_splitk_plan(T, INTER, H, TC_EPI_SILU_BF16, 128, &kt) > 1 ? 2 : 1));
+    const int o_kernels = exact ? 2 : (split && tc_splitk_plan(T, H, QD, TC_EPI_RESID_F32, 128, &kt) > 1 ? 2 : 1);
+    const int d_kernels = exact ? 2 : (split && tc_splitk_plan(T, H, INTER, TC_EPI_RESID_F32, 128, &kt) > 1 ? 2 : 1);
+    const int qkv_kernels = (split && tc_splitk_plan(T, QKVD, H, TC_EPI_F32, 128, &kt) > 1) ? 2 : 1;
     for (int l = 0; l < NLAYER; l++) {
         STEP(N550_PROF_RMSNORM, 1, launch_rmsnorm(st, m->xb, N550_BF16, m->x, W(m, l, 0), T, H, EPS));
-        STEP(N550_PROF_GEMM_QKV, 1,
-             mgemm(m, st, TC_EPI_F32, m->xb, H, m->wqkv[l], nullptr, m->qkv, QKVD, T, QKVD, H));
-        STEP(N550_PROF_QKNORM_ROPE, 1, launch_qknorm_rope_kv(m, st, T, l, decode));
+        if (!exact && T >= 1024) {
+            // One tcgen05 GEMM with QK-norm, RoPE and the K/V cache write in its epilogue.
+            TcQkv q{};
+            q.q_bf16 = decode ? nullptr : m->qb;
+            q.q_f32 = decode ? m->qf : nullptr;
+            q.ldq = QD;
+            q.kc = m->kc; q.vc = m->vc; q.layer = l; q.max_len = c.max_len;
+            q.tok_pos = m->tok_pos; q.tok_seq = m->tok_seq;
+            q.q_norm = W(m, l, 4); q.k_norm = W(m, l, 5);
+            q.rope = m->rope; q.eps = EPS;
+            STEP(N550_PROF_GEMM_QKV, 1, launch_gemm_tc_qkv(st, m->xb, H, m->wqkv[l], q, T, H, 0));
+        } else {
+            STEP(N550_PROF_GEMM_QKV, qkv_kernels,
+                 mgemm(m, st, TC_EPI_F32, m->xb, H, m->wqkv[l], nullptr, m->qkv, QKVD, T, QKVD, H));
+            STEP(N550_PROF_QKNORM_ROPE, 1, launch_qknorm_rope_kv(m, st, T, l, decode));
+        }
         if (decode) {
             AttnDecodeArgs a{};
             a.q_f32 = m->qf;
@@ -484,12 +523,12 @@ int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t
             a.ldq = QD; a.ldo = QD; a.L = Lc; a.pos0 = p0; a.layer = l; a.max_len = c.max_len;
             STEP(N550_PROF_ATTN, 1, launch_attn_prefill(st, a, Sc));
         }
-        STEP(N550_PROF_GEMM_O, res_kernels,
+        STEP(N550_PROF_GEMM_O, o_kernels,
              mgemm(m, st, TC_EPI_RESID_F32, m->attn, QD, W(m, l, 6), nullptr, m->x, H, T, H, QD));
         STEP(N550_PROF_RMSNORM, 1, launch_rmsnorm(st, m->xb, N550_BF16, m->x, W(m, l, 7), T, H, EPS));
         STEP(N550_PROF_GEMM_GATEUP, gu_kernels,
              mgemm(m, st, TC_EPI_SILU_BF16, m->xb, H, W(m, l, 8), W(m, l, 9), m->h, INTER, T, INTER, H));
-        STEP(N550_PROF_GEMM_DOWN, res_kernels,
+        STEP(N550_PROF_GEMM_DOWN, d_kernels,
              mgemm(m, st, TC_EPI_RESID_F32, m->h, INTER, W(m, l, 10), nullptr, m->x, H, T, H, INTER));
     }
     return N550_OK;

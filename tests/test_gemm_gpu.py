@@ -196,3 +196,29 @@ def test_fast_host_shim(cuda):
     finally:
         n5.set_gemm_mode(n5.MODE_EXACT, 16)
     assert rel_err(c, f64_ref(oracle.f32_to_bf16(a), b)) <= FAST_TOL
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 2048, 1024), (300, 2048, 1024), (129, 3072, 1000), (64, 1024, 1024)])
+def test_fused_residual_gemm(cuda, M, K, N):
+    """x += A . B^T (qwen3_gemm then qwen3_op_residual_add)."""
+    import torch
+    A = oracle.synth_normal_bf16((M, K), 31, 0x41, 1.0)
+    B = oracle.synth_normal_bf16((N, K), 31, 0x42, 0.02)
+    x0 = oracle.synth_normal_f32((M, N), 31, 0x58, 1.0)
+    x = torch.from_numpy(x0.copy()).to(cuda)
+    n5.gemm_residual(to_dev_bf16(A, cuda), to_dev_bf16(B, cuda), x)
+    ref = x0.astype(np.float64) + f64_ref(A, B)
+    assert rel_err(x.cpu().numpy(), ref) <= FAST_TOL
+
+
+@pytest.mark.parametrize("M,K,N", [(300, 1024, 3072), (128, 1024, 200), (17, 1024, 64)])
+def test_fused_swiglu_gemm(cuda, M, K, N):
+    """h = silu(A . Wg^T) * (A . Wu^T) in BF16 (gate/up qwen3_gemm then qwen3_op_silu_mul)."""
+    A = oracle.synth_normal_bf16((M, K), 41, 0x41, 1.0)
+    G = oracle.synth_normal_bf16((N, K), 41, 0x47, 0.02)
+    U = oracle.synth_normal_bf16((N, K), 41, 0x55, 0.02)
+    h = n5.gemm_swiglu(to_dev_bf16(A, cuda), to_dev_bf16(G, cuda), to_dev_bf16(U, cuda))
+    g, u = f64_ref(A, G), f64_ref(A, U)
+    ref = g / (1.0 + np.exp(-g)) * u
+    got = oracle.bf16_to_f32(bf16_bits(h)).astype(np.float64)
+    assert rel_err(got, ref) <= BF16_OUT_TOL

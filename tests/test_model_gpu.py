@@ -193,3 +193,65 @@ def test_exact_gemm_mode_model(cuda, blob):
     ref.close()
     assert rel(lg, rl) <= LOGIT_TOL
     assert nxt == oracle.argmax(rl)
+
+
+def test_decode_batch_tensor_core_path_matches_prefill(cuda):
+    """12 sequences decode together (tensor-core GEMMs with the fused QKV
+    epilogue writing FP32 queries); each sequence's logits equal the
+    last-token logits of prefilling its prompt plus that token."""
+    import torch
+    S = 12
+    lens = [4 + s for s in range(S)]
+    m = n5.Model(seed=0, max_seqs=S, max_len=64, max_tokens=64)
+    prompts = [oracle.synth_tokens(n, 70 + i, 0x544F4B) for i, n in enumerate(lens)]
+    firsts = []
+    for s in range(S):
+        t = torch.from_numpy(prompts[s]).reshape(1, -1).cuda()
+        nxt = torch.empty(1, dtype=torch.int32, device="cuda")
+        m.prefill(t, torch.tensor([s], dtype=torch.int32, device="cuda"), 0, None, nxt)
+        firsts.append(int(nxt.item()))
+    logits = torch.empty((S, 151936), dtype=torch.float32, device="cuda")
+    nxt = torch.empty(S, dtype=torch.int32, device="cuda")
+    m.decode(torch.tensor(firsts, dtype=torch.int32, device="cuda"),
+             torch.arange(S, dtype=torch.int32, device="cuda"),
+             torch.tensor(lens, dtype=torch.int32, device="cuda"), logits, nxt)
+    torch.cuda.synchronize()
+    got = logits.cpu().numpy()
+    m.close()
+    for s in range(S):
+        r = n5.Model(seed=0, max_seqs=1, max_len=64, max_tokens=64)
+        _, want = r.forward_batch(np.append(prompts[s], firsts[s]).astype(np.int32), 0)
+        r.close()
+        assert rel(got[s], want) <= LOGIT_TOL
+        assert same_choice(int(nxt[s]), want)
+
+
+def test_fused_qkv_prefill_matches_split_path(cuda):
+    """>= 1024 tokens per call take the 256-wide GEMMs with QK-norm, RoPE and
+    the KV write fused into the QKV epilogue; the same sequences prefilled one
+    by one take the split-K path and the separate QK-norm kernel. Logits and
+    the following decode step agree within the logit tolerance."""
+    import torch
+    S, L = 4, 256
+    toks = oracle.synth_tokens(S * L, 9, 0x544F4B).reshape(S, L)
+    m = n5.Model(seed=0, max_seqs=S, max_len=L + 8, max_tokens=S * L)
+    t = torch.from_numpy(toks).cuda()
+    seq = torch.arange(S, dtype=torch.int32, device="cuda")
+    logits = torch.empty((S, 151936), dtype=torch.float32, device="cuda")
+    nxt = torch.empty(S, dtype=torch.int32, device="cuda")
+    m.prefill(t, seq, 0, logits, nxt)
+    dl = torch.empty((S, 151936), dtype=torch.float32, device="cuda")
+    dn = torch.empty(S, dtype=torch.int32, device="cuda")
+    m.decode(nxt.clone(), seq, torch.full((S,), L, dtype=torch.int32, device="cuda"), dl, dn)
+    torch.cuda.synchronize()
+    fused, fused_dec = logits.cpu().numpy(), dl.cpu().numpy()
+    nx = nxt.cpu().numpy()
+    m.close()
+    for s in range(S):
+        single = n5.Model(seed=0, max_seqs=1, max_len=L + 8, max_tokens=L)
+        a, lg = single.forward_batch(toks[s], 0)
+        _, lg2 = single.forward_batch(np.array([nx[s]], np.int32), L)
+        single.close()
+        assert rel(fused[s], lg) <= LOGIT_TOL
+        assert same_choice(int(nx[s]), lg)
+        assert rel(fused_dec[s], lg2) <= LOGIT_TOL
