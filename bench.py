@@ -299,32 +299,35 @@ def run_decode(args, m, world, rank, dev, stream, ds, pk, timed):
     pos = torch.full((ds,), DECODE_CTX, dtype=torch.int32, device=dev)
     ids = torch.empty((DECODE_STEPS, ds), dtype=torch.int32, device=dev)
 
-    def job():
+    def job(use_graph=True):
         tok = first.clone()
         p = pos.clone()
-        for i in range(DECODE_STEPS):
-            m.decode(tok, seq, p, None, ids[i])
-            tok = ids[i]
-            p += 1
+        # each step is one replay of the captured decode step (all its kernels)
+        m.decode_steps(tok, seq, p, DECODE_STEPS, ids, use_graph=use_graph)
 
-    # one warm-up job, then time whole jobs (each = 128 steps)
+    # one warm-up job (captures the graph), then time whole jobs (128 steps each)
     saved = args.warmup
     args.warmup = 1
+    n_jobs = max(1, min(args.steps, 3))
     with ClockSampler(torch.cuda.current_device()) as clk:
-        ms = timed(job, max(1, min(args.steps, 3)), prof=True)
+        ms = timed(job, n_jobs)
     args.warmup = saved
+    # per-kernel breakdown: one extra job launched eagerly with event timing
+    torch.cuda.synchronize(dev)
+    n5.check(n5.lib().n550_qwen3_profile(m.handle, 1))
+    job(use_graph=False)
     kind_ms = (C.c_double * 9)()
     kind_n = (C.c_int64 * 9)()
     n5.check(n5.lib().n550_qwen3_profile_read(m.handle, kind_ms, kind_n, 9))
     n5.check(n5.lib().n550_qwen3_profile(m.handle, 0))
+    launches_per_step = sum(kind_n) / DECODE_STEPS + 1          # + the advance kernel
     tokens = DECODE_SEQS * DECODE_STEPS
     # algorithmic HBM bytes per decode step on one rank: weights + KV read + KV write
     avg_ctx = DECODE_CTX + (DECODE_STEPS + 1) / 2.0
     bytes_step = WEIGHT_BYTES + ds * KV_BYTES_PER_POS * avg_ctx + ds * KV_BYTES_PER_POS
     step_ms = ms / DECODE_STEPS
     gbs = bytes_step / (step_ms / 1000.0) / 1e9
-    n_jobs = max(1, min(args.steps, 3))
-    attn_ms = kind_ms[5] / n_jobs / DECODE_STEPS
+    attn_ms = kind_ms[5] / DECODE_STEPS
     kv_bytes = ds * KV_BYTES_PER_POS * avg_ctx
     return {"workload": "configs[4] batched decode DP: 256 seqs, 1024-token BF16 KV context, 128 greedy steps",
             "value": round(tokens / (ms / 1000.0), 1), "unit": "tok/s",
@@ -333,7 +336,8 @@ def run_decode(args, m, world, rank, dev, stream, ds, pk, timed):
                          "unit": "GB/s", "frac": round(gbs / pk["hbm_gbs"], 4),
                          "attention_kernel_gbs": round(kv_bytes / (attn_ms / 1000.0) / 1e9, 1)
                          if attn_ms > 0 else None},
-            "kernel_ms_per_step": {k: round(kind_ms[i] / n_jobs / DECODE_STEPS, 4) for i, k in enumerate(
+            "launches_per_step": round(launches_per_step, 1), "cuda_graph": True,
+            "kernel_ms_per_step_eager": {k: round(kind_ms[i] / DECODE_STEPS, 4) for i, k in enumerate(
                 ["gemm_qkv", "gemm_o", "gemm_gateup", "gemm_down", "gemm_lmhead", "attention",
                  "qknorm_rope_kv", "rmsnorm", "other"])},
             "clocks": clk.summary()}

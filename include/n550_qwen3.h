@@ -230,6 +230,17 @@ int n550_qwen3_decode(n550_model_t *m, void *stream, const int32_t *tokens,
                       const int32_t *seq_ids, const int32_t *pos, int n_seqs,
                       float *logits, int32_t *next_token);
 
+/* `steps` greedy decode steps (the generation loop of main.c:240-256 for many
+ * sequences): step i feeds tokens[s] at pos[s], writes the argmax to
+ * out_ids[i * n_seqs + s], then sets tokens[s] = that id and pos[s] += 1 on
+ * the device (tokens and pos are advanced in place). use_graph = 1 captures
+ * one step (all its kernels) into a CUDA graph on first use and replays it
+ * (one launch per step); the capture is rebuilt when n_seqs or a pointer
+ * changes. Do not call it while the stream is being captured. */
+int n550_qwen3_decode_steps(n550_model_t *m, void *stream, int32_t *tokens,
+                            const int32_t *seq_ids, int32_t *pos, int n_seqs, int steps,
+                            int32_t *out_ids, int use_graph);
+
 /* Reference-shaped convenience on sequence slot 0 with HOST buffers:
  * tokens[n_token] at pos0.., last-token logits copied to logits_host
  * (151936 floats, may be NULL); returns the argmax (>= 0) or an error (< 0). */

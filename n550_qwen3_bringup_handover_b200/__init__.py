@@ -85,6 +85,7 @@ def lib() -> C.CDLL:
         "n550_qwen3_prefill": (i, [vp, vp, vp, vp, i, i, i, vp, vp]),
         "n550_qwen3_decode": (i, [vp, vp, vp, vp, vp, i, vp, vp]),
         "n550_qwen3_forward_batch_host": (i, [vp, vp, i, i, vp]),
+        "n550_qwen3_decode_steps": (i, [vp, vp, vp, vp, vp, i, i, vp, i]),
         "n550_qwen3_weight": (vp, [vp, i, C.POINTER(sz)]),
         "n550_qwen3_profile": (i, [vp, i]),
         "n550_qwen3_profile_read": (i, [vp, vp, vp, i]),

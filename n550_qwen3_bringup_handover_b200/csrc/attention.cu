@@ -280,7 +280,9 @@ attn_decode_kernel(AttnDecodeArgs p) {
     const uint16_t *kbase = p.kc + kv_base(seq, p.layer, kvh, p.max_len);
     const uint16_t *vbase = p.vc + kv_base(seq, p.layer, kvh, p.max_len);
     float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-    float acc[2][4] = {};
+    // p.v: lane owns head dims d8..d8+7 of the rows with parity `half`.
+    const int half = lane >> 4, d8 = (lane & 15) * 8;
+    float acc[2][8] = {};
 
     for (int base = start + warp * 32; base < end; base += DC_WARPS * 32) {
         const int t = base + lane;
@@ -329,35 +331,46 @@ attn_decode_kernel(AttnDecodeArgs p) {
         l[0] = l[0] * c0 + sum0;
         l[1] = l[1] * c1 + sum1;
 #pragma unroll
-        for (int d = 0; d < 4; d++) { acc[0][d] *= c0; acc[1][d] *= c1; }
+        for (int d = 0; d < 8; d++) { acc[0][d] *= c0; acc[1][d] *= c1; }
         ps[warp][0][lane] = p0;
         ps[warp][1][lane] = p1;
         __syncwarp();
+        // 32 V rows: 16 lanes per 256-byte row, 2 rows per instruction, all
+        // 16 loads in flight before the first use.
         const int nvalid = min(32, end - base);
-        const uint16_t *vr = vbase + (size_t)base * HD + lane * 4;
-        for (int j0 = 0; j0 < nvalid; j0 += 8) {
-            uint2 vq[8];
+        const uint16_t *vr = vbase + (size_t)base * HD + d8;
+        uint4 vq[16];
 #pragma unroll
-            for (int u = 0; u < 8; u++)
-                vq[u] = (j0 + u < nvalid) ? __ldg((const uint2 *)(vr + (size_t)(j0 + u) * HD))
-                                          : make_uint2(0, 0);
+        for (int i = 0; i < 16; i++) {
+            const int j = 2 * i + half;
+            vq[i] = (j < nvalid) ? __ldg((const uint4 *)(vr + (size_t)j * HD)) : make_uint4(0, 0, 0, 0);
+        }
 #pragma unroll
-            for (int u = 0; u < 8; u++) {
-                const float w0 = ps[warp][0][j0 + u], w1 = ps[warp][1][j0 + u];
-                const float v0 = __uint_as_float(vq[u].x << 16), v1 = __uint_as_float(vq[u].x & 0xFFFF0000u);
-                const float v2 = __uint_as_float(vq[u].y << 16), v3 = __uint_as_float(vq[u].y & 0xFFFF0000u);
-                acc[0][0] = fmaf(w0, v0, acc[0][0]); acc[0][1] = fmaf(w0, v1, acc[0][1]);
-                acc[0][2] = fmaf(w0, v2, acc[0][2]); acc[0][3] = fmaf(w0, v3, acc[0][3]);
-                acc[1][0] = fmaf(w1, v0, acc[1][0]); acc[1][1] = fmaf(w1, v1, acc[1][1]);
-                acc[1][2] = fmaf(w1, v2, acc[1][2]); acc[1][3] = fmaf(w1, v3, acc[1][3]);
+        for (int i = 0; i < 16; i++) {
+            const int j = 2 * i + half;
+            const float w0 = ps[warp][0][j], w1 = ps[warp][1][j];
+            float vf[8];
+            bf16x8(vq[i], vf);
+#pragma unroll
+            for (int d = 0; d < 8; d++) {
+                acc[0][d] = fmaf(w0, vf[d], acc[0][d]);
+                acc[1][d] = fmaf(w1, vf[d], acc[1][d]);
             }
         }
         __syncwarp();
     }
+    // merge the two row-parity halves: lanes 0..15 then hold dims d8..d8+7
+#pragma unroll
+    for (int d = 0; d < 8; d++) {
+        acc[0][d] += __shfl_xor_sync(0xFFFFFFFFu, acc[0][d], 16);
+        acc[1][d] += __shfl_xor_sync(0xFFFFFFFFu, acc[1][d], 16);
+    }
 
     if (lane == 0) { wm[warp][0] = m[0]; wm[warp][1] = m[1]; wl[warp][0] = l[0]; wl[warp][1] = l[1]; }
+    if (lane < 16) {
 #pragma unroll
-    for (int d = 0; d < 4; d++) { wo[warp][0][lane * 4 + d] = acc[0][d]; wo[warp][1][lane * 4 + d] = acc[1][d]; }
+        for (int d = 0; d < 8; d++) { wo[warp][0][d8 + d] = acc[0][d]; wo[warp][1][d8 + d] = acc[1][d]; }
+    }
     __syncthreads();
 
     for (int i = threadIdx.x; i < 2 * HD; i += DC_THREADS) {

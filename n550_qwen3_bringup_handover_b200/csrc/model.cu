@@ -234,6 +234,21 @@ __global__ void rope_table_kernel(float2 *t, int max_len) {
     t[idx] = make_float2(c, s);
 }
 
+// After a decode step: record the chosen ids (row *counter of out) and feed
+// them back as the next step's tokens at the next positions.
+__global__ void decode_advance_kernel(const int32_t *next, int32_t *tokens, int32_t *pos,
+                                      int32_t *out, int32_t *counter, int n) {
+    const int step = *counter;
+    for (int s = threadIdx.x; s < n; s += blockDim.x) {
+        const int32_t id = next[s];
+        out[(size_t)step * n + s] = id;
+        tokens[s] = id;
+        pos[s] += 1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *counter = step + 1;
+}
+
 // Final RMSNorm of the last token of each sequence (qwen3.c:547-573 only
 // needs row NT-1): xl[i] = rmsnorm(x[i*Lc + Lc - 1]) in BF16.
 __global__ void __launch_bounds__(256)
@@ -313,6 +328,13 @@ struct n550_model {
     float2 *rope = nullptr;                 // [max_len][64] (cos, sin)
     float *ws = nullptr;                    // split-K partials of skinny GEMMs
     size_t ws_bytes = 0;
+    // captured decode step (n550_qwen3_decode_steps)
+    cudaGraphExec_t graph = nullptr;
+    int g_n = 0;
+    const void *g_key[4] = {};
+    int32_t *step_counter = nullptr;
+    cudaStream_t cap_stream = nullptr;      // capture/replay stream (the legacy
+    cudaEvent_t ev_in = nullptr, ev_out = nullptr;   // stream cannot be captured)
 };
 
 namespace {
@@ -341,6 +363,11 @@ struct ProfScope {
 
 void model_release(n550_model *m) {
     if (!m) return;
+    if (m->graph) cudaGraphExecDestroy(m->graph);
+    if (m->step_counter) cudaFree(m->step_counter);
+    if (m->cap_stream) cudaStreamDestroy(m->cap_stream);
+    if (m->ev_in) cudaEventDestroy(m->ev_in);
+    if (m->ev_out) cudaEventDestroy(m->ev_out);
     for (cudaEvent_t e : m->prof.pool) cudaEventDestroy(e);
     void *ptrs[] = {m->blob, m->fused_qkv, m->kc, m->vc, m->x, m->qkv, m->qf, m->logits, m->xb,
                     m->qb, m->attn, m->h, m->xl, m->tmp_a, m->tmp_b, m->tok_pos, m->tok_seq,
@@ -401,6 +428,10 @@ int model_setup(n550_model *m) {
     // split-K workspace: up to 8 slices of [rows < 1024][2 x 3072] FP32
     m->ws_bytes = (size_t)8 * std::min<size_t>(T, 1023) * 2 * INTER * 4;
     ALLOC(m->ws, m->ws_bytes);
+    ALLOC(m->step_counter, 4);
+    N550_CUDA_TRY(cudaStreamCreateWithFlags(&m->cap_stream, cudaStreamNonBlocking));
+    N550_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming));
+    N550_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_out, cudaEventDisableTiming));
 #undef ALLOC
     N550_CUDA_TRY(cudaMemset(m->zero_seq, 0, 4));
     N550_CUDA_TRY(cudaMemset(m->kc, 0, kv * 2));
@@ -661,6 +692,78 @@ int n550_qwen3_decode(n550_model_t *m, void *stream, const int32_t *tokens, cons
     int rc = run_layers(m, st, n_seqs, true, seq_ids, pos, n_seqs, 1, 0);
     if (rc) return rc;
     return run_head(m, st, n_seqs, 1, logits ? logits : m->logits, next_token);
+}
+
+int n550_qwen3_decode_steps(n550_model_t *m, void *stream, int32_t *tokens, const int32_t *seq_ids,
+                            int32_t *pos, int n_seqs, int steps, int32_t *out_ids, int use_graph) {
+    if (!m || !tokens || !seq_ids || !pos || !out_ids || n_seqs < 1 || steps < 0) return N550_ERR_ARG;
+    if (n_seqs > m->cfg.max_tokens || n_seqs > m->cfg.max_seqs) return N550_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    N550_CUDA_TRY(cudaMemsetAsync(m->step_counter, 0, 4, st));   // ordered before the capture stream joins
+    auto one_step = [&]() -> int {
+        int rc = n550_qwen3_decode(m, st, tokens, seq_ids, pos, n_seqs, nullptr, m->next);
+        if (rc) return rc;
+        decode_advance_kernel<<<1, 256, 0, st>>>(m->next, tokens, pos, out_ids, m->step_counter, n_seqs);
+        N550_LAUNCH_CHECK();
+        return N550_OK;
+    };
+    if (!use_graph) {
+        for (int i = 0; i < steps; i++) {
+            int rc = one_step();
+            if (rc) return rc;
+        }
+        return N550_OK;
+    }
+    // Capture and replay on the model's own stream, ordered after the
+    // caller's stream and joined back to it with events.
+    const cudaStream_t cs = m->cap_stream;
+    N550_CUDA_TRY(cudaEventRecord(m->ev_in, st));
+    N550_CUDA_TRY(cudaStreamWaitEvent(cs, m->ev_in, 0));
+    auto step_on = [&](cudaStream_t s_) -> int {
+        int rc = n550_qwen3_decode(m, s_, tokens, seq_ids, pos, n_seqs, nullptr, m->next);
+        if (rc) return rc;
+        decode_advance_kernel<<<1, 256, 0, s_>>>(m->next, tokens, pos, out_ids, m->step_counter, n_seqs);
+        N550_LAUNCH_CHECK();
+        return N550_OK;
+    };
+    int rc = N550_OK;
+    const void *key[4] = {tokens, seq_ids, pos, out_ids};
+    const bool same = m->graph && m->g_n == n_seqs && !memcmp(key, m->g_key, sizeof key);
+    if (!same && steps > 0) {
+        if (m->graph) { cudaGraphExecDestroy(m->graph); m->graph = nullptr; }
+        // Step 0 runs uncaptured: first launches set kernel attributes, and
+        // the capture below must not contain one-time work.
+        rc = step_on(cs);
+        steps--;
+        if (!rc) {
+            const bool prof = m->prof.on;
+            m->prof.on = false;
+            cudaGraph_t g = nullptr;
+            if (cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+                rc = N550_ERR_CUDA;
+            } else {
+                rc = step_on(cs);
+                const cudaError_t ce = cudaStreamEndCapture(cs, &g);
+                if (!rc && ce != cudaSuccess) rc = N550_ERR_CUDA;
+            }
+            m->prof.on = prof;
+            if (!rc && cudaGraphInstantiate(&m->graph, g, 0) != cudaSuccess) {
+                m->graph = nullptr;
+                rc = N550_ERR_CUDA;
+            }
+            if (g) cudaGraphDestroy(g);
+            (void)cudaGetLastError();
+            if (!rc) {
+                m->g_n = n_seqs;
+                memcpy(m->g_key, key, sizeof key);
+            }
+        }
+    }
+    for (int i = 0; i < steps && !rc; i++)
+        if (cudaGraphLaunch(m->graph, cs) != cudaSuccess) rc = N550_ERR_CUDA;
+    N550_CUDA_TRY(cudaEventRecord(m->ev_out, cs));
+    N550_CUDA_TRY(cudaStreamWaitEvent(st, m->ev_out, 0));
+    return rc;
 }
 
 int n550_qwen3_forward_batch_host(n550_model_t *m, const int32_t *tokens, int n_token, int pos0,

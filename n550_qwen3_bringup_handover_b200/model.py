@@ -70,6 +70,15 @@ class Model:
             C.c_void_p(logits.data_ptr()) if logits is not None else None,
             C.c_void_p(next_token.data_ptr()) if next_token is not None else None), "n550_qwen3_decode")
 
+    def decode_steps(self, tokens, seq_ids, pos, steps, out_ids, use_graph=True, stream=None):
+        """`steps` greedy steps; tokens/pos (device int32) advance in place,
+        out_ids[steps, n_seqs] receives the chosen ids."""
+        from .api import stream_ptr
+        check(lib().n550_qwen3_decode_steps(
+            self._h, stream_ptr(stream), C.c_void_p(tokens.data_ptr()), C.c_void_p(seq_ids.data_ptr()),
+            C.c_void_p(pos.data_ptr()), tokens.shape[0], steps, C.c_void_p(out_ids.data_ptr()),
+            1 if use_graph else 0), "n550_qwen3_decode_steps")
+
     def weight_bits(self, which: int) -> np.ndarray:
         """Copy of one QW3M tensor (BF16 bits) from the device."""
         import torch

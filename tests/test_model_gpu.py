@@ -255,3 +255,37 @@ def test_fused_qkv_prefill_matches_split_path(cuda):
         assert rel(fused[s], lg) <= LOGIT_TOL
         assert same_choice(int(nx[s]), lg)
         assert rel(fused_dec[s], lg2) <= LOGIT_TOL
+
+
+def test_decode_steps_graph_replay_matches_eager(cuda):
+    """n550_qwen3_decode_steps: the CUDA-graph replay of a decode step gives
+    exactly the ids, tokens and positions of the eager loop."""
+    import torch
+    S, L, steps = 10, 8, 6
+    toks = oracle.synth_tokens(S * L, 12, 0x544F4B).reshape(S, L)
+    results = []
+    for use_graph in (False, True):
+        m = n5.Model(seed=0, max_seqs=S, max_len=64, max_tokens=S * L)
+        seq = torch.arange(S, dtype=torch.int32, device="cuda")
+        nxt = torch.empty(S, dtype=torch.int32, device="cuda")
+        m.prefill(torch.from_numpy(toks).cuda(), seq, 0, None, nxt)
+        tok = nxt.clone()
+        pos = torch.full((S,), L, dtype=torch.int32, device="cuda")
+        ids = torch.zeros((steps, S), dtype=torch.int32, device="cuda")
+        m.decode_steps(tok, seq, pos, steps, ids, use_graph=use_graph)
+        torch.cuda.synchronize()
+        results.append((ids.cpu().numpy(), tok.cpu().numpy(), pos.cpu().numpy(), nxt.cpu().numpy()))
+        m.close()
+    (ie, te, pe, n0), (ig, tg, pg, _) = results
+    assert np.array_equal(ie, ig) and np.array_equal(te, tg) and np.array_equal(pe, pg)
+    assert np.array_equal(te, ie[-1]) and (pe == L + steps).all()
+    # step 0 of the loop is the single decode of the prefill's next tokens
+    m = n5.Model(seed=0, max_seqs=S, max_len=64, max_tokens=S * L)
+    seq = torch.arange(S, dtype=torch.int32, device="cuda")
+    nxt = torch.empty(S, dtype=torch.int32, device="cuda")
+    m.prefill(torch.from_numpy(toks).cuda(), seq, 0, None, nxt)
+    one = torch.empty(S, dtype=torch.int32, device="cuda")
+    m.decode(nxt, seq, torch.full((S,), L, dtype=torch.int32, device="cuda"), None, one)
+    torch.cuda.synchronize()
+    m.close()
+    assert np.array_equal(one.cpu().numpy(), ie[0])
