@@ -246,8 +246,12 @@ attn_prefill_kernel(AttnPrefillArgs p) {
 // ---------------------------------------------------------------------------
 // decode (CUDA cores, split-KV)
 // ---------------------------------------------------------------------------
-constexpr int DC_THREADS = 128;     // 4 warps, 32 positions per warp step
+constexpr int DC_THREADS = 128;     // 4 warps
 constexpr int DC_WARPS = DC_THREADS / 32;
+constexpr int DC_TP = 64;           // positions per tile (16 per warp)
+constexpr int DC_STAGES = 3;        // tiles in flight per CTA
+constexpr int DC_TILE_BYTES = DC_TP * HD * 2;   // 16 KB of K (and of V)
+constexpr int DC_SMEM = DC_STAGES * 2 * DC_TILE_BYTES + 1024;
 
 __device__ __forceinline__ void bf16x8(const uint4 q, float (&f)[8]) {
     f[0] = __uint_as_float(q.x << 16); f[1] = __uint_as_float(q.x & 0xFFFF0000u);
@@ -256,121 +260,148 @@ __device__ __forceinline__ void bf16x8(const uint4 q, float (&f)[8]) {
     f[6] = __uint_as_float(q.w << 16); f[7] = __uint_as_float(q.w & 0xFFFF0000u);
 }
 
+// One CTA per (split, kv head, sequence). K and V tiles of 64 positions
+// (16 KB each, contiguous in the cache) stream through a 3-stage shared
+// ring by bulk copies; warp w owns positions 16w..16w+15 of every tile and
+// keeps its own online-softmax state, merged with the others at the end.
 __global__ void __launch_bounds__(DC_THREADS)
 attn_decode_kernel(AttnDecodeArgs p) {
-    __shared__ __align__(16) float qs[2][HD];
-    __shared__ __align__(16) float ps[DC_WARPS][2][32];
+    extern __shared__ __align__(128) uint8_t dsm[];
+    uint8_t *ring = (uint8_t *)(((uintptr_t)dsm + 127) & ~(uintptr_t)127);
+    uint64_t *full = (uint64_t *)(ring + DC_STAGES * 2 * DC_TILE_BYTES);
+    uint64_t *empty = full + DC_STAGES;
+    __shared__ __align__(16) float ps[DC_WARPS][2][16];
     __shared__ float wm[DC_WARPS][2], wl[DC_WARPS][2];
-    __shared__ float wo[DC_WARPS][2][HD];
+    __shared__ __align__(16) float wo[DC_WARPS][2][HD];
+
     const int split = blockIdx.x, kvh = blockIdx.y, s = blockIdx.z;
     const int seq = p.seq_ids[s];
     const int kv_len = p.pos[s] + 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int chunk = (kv_len + p.splits - 1) / p.splits;
+    int chunk = (kv_len + p.splits - 1) / p.splits;
+    chunk = (chunk + DC_TP - 1) / DC_TP * DC_TP;
     const int start = split * chunk, end = min(kv_len, start + chunk);
-
-    for (int i = threadIdx.x; i < 2 * HD; i += DC_THREADS) {
-        const int h = i >> 7, d = i & 127;
-        const float v = p.q_f32 ? p.q_f32[(size_t)s * p.ldq + (kvh * 2 + h) * HD + d]
-                                : bf16_bits_to_f32(p.q_bf16[(size_t)s * p.ldq + (kvh * 2 + h) * HD + d]);
-        qs[h][d] = v * (kScale * kLog2e);
-    }
-    __syncthreads();
-
+    const int n_tiles = end > start ? (end - start + DC_TP - 1) / DC_TP : 0;
     const uint16_t *kbase = p.kc + kv_base(seq, p.layer, kvh, p.max_len);
     const uint16_t *vbase = p.vc + kv_base(seq, p.layer, kvh, p.max_len);
-    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-    // p.v: lane owns head dims d8..d8+7 of the rows with parity `half`.
-    const int half = lane >> 4, d8 = (lane & 15) * 8;
-    float acc[2][8] = {};
 
-    for (int base = start + warp * 32; base < end; base += DC_WARPS * 32) {
-        const int t = base + lane;
-        float s0 = -INFINITY, s1 = -INFINITY;
-        if (t < end) {
-            // The whole K row (256 B) in 16 independent 16-byte loads; the
-            // query (both heads) comes from shared memory as float4 broadcasts.
-            const uint4 *kr = (const uint4 *)(kbase + (size_t)t * HD);
-            uint4 kq[16];
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < DC_STAGES; i++) { mbar_init(&full[i], 1); mbar_init(&empty[i], DC_WARPS); }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    auto issue = [&](int tile) {
+        const int st = tile % DC_STAGES;
+        const int t0 = start + tile * DC_TP;
+        const uint32_t bytes = (uint32_t)min(DC_TP, end - t0) * HD * 2;
+        uint8_t *kd = ring + st * 2 * DC_TILE_BYTES;
+        mbar_arrive_expect_tx(&full[st], 2 * bytes);
+        bulk_load(kd, kbase + (size_t)t0 * HD, bytes, &full[st]);
+        bulk_load(kd + DC_TILE_BYTES, vbase + (size_t)t0 * HD, bytes, &full[st]);
+    };
+    if (threadIdx.x == 0)
+        for (int i = 0; i < min(DC_STAGES, n_tiles); i++) issue(i);
+
+    // q . k: 8 lanes per position, lane g8 = lane & 7 owns dims 16*g8 .. +15.
+    const int g8 = lane & 7;
+    float q0[16], q1[16];
+    {
+        const size_t qo = (size_t)s * p.ldq + (size_t)(kvh * 2) * HD + 16 * g8;
 #pragma unroll
-            for (int c = 0; c < 16; c++) kq[c] = __ldg(kr + c);
+        for (int j = 0; j < 16; j++) {
+            const float a = p.q_f32 ? p.q_f32[qo + j] : bf16_bits_to_f32(p.q_bf16[qo + j]);
+            const float b = p.q_f32 ? p.q_f32[qo + HD + j] : bf16_bits_to_f32(p.q_bf16[qo + HD + j]);
+            q0[j] = a * (kScale * kLog2e);
+            q1[j] = b * (kScale * kLog2e);
+        }
+    }
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+    float acc[2][4] = {};                 // p . v: lane owns dims 4*lane .. +3
+    bool ok = true;
+
+    for (int tile = 0; tile < n_tiles && ok; tile++) {
+        const int st = tile % DC_STAGES;
+        const uint32_t par = (uint32_t)((tile / DC_STAGES) & 1);
+        if (!mbar_wait(&full[st], par)) { ok = false; break; }
+        const uint8_t *kt = ring + st * 2 * DC_TILE_BYTES;
+        const uint8_t *vt = kt + DC_TILE_BYTES;
+        const int t0 = start + tile * DC_TP + warp * 16;     // this warp's first position
+        float sc[2][4];
+#pragma unroll
+        for (int pass = 0; pass < 4; pass++) {
+            const int r = warp * 16 + pass * 4 + (lane >> 3);  // row in the tile
+            const uint4 *kr = (const uint4 *)(kt + r * (HD * 2) + 32 * g8);
+            float kf[16];
+            bf16x8(kr[0], *(float(*)[8])kf);
+            bf16x8(kr[1], *(float(*)[8])(kf + 8));
             float a0 = 0.f, a1 = 0.f;
-            const float4 *q0 = (const float4 *)qs[0], *q1 = (const float4 *)qs[1];
 #pragma unroll
-            for (int c = 0; c < 16; c++) {
-                float kf[8];
-                bf16x8(kq[c], kf);
-                const float4 x0 = q0[2 * c], x1 = q0[2 * c + 1], y0 = q1[2 * c], y1 = q1[2 * c + 1];
-                a0 = fmaf(x0.x, kf[0], a0); a0 = fmaf(x0.y, kf[1], a0); a0 = fmaf(x0.z, kf[2], a0);
-                a0 = fmaf(x0.w, kf[3], a0); a0 = fmaf(x1.x, kf[4], a0); a0 = fmaf(x1.y, kf[5], a0);
-                a0 = fmaf(x1.z, kf[6], a0); a0 = fmaf(x1.w, kf[7], a0);
-                a1 = fmaf(y0.x, kf[0], a1); a1 = fmaf(y0.y, kf[1], a1); a1 = fmaf(y0.z, kf[2], a1);
-                a1 = fmaf(y0.w, kf[3], a1); a1 = fmaf(y1.x, kf[4], a1); a1 = fmaf(y1.y, kf[5], a1);
-                a1 = fmaf(y1.z, kf[6], a1); a1 = fmaf(y1.w, kf[7], a1);
+            for (int j = 0; j < 16; j++) { a0 = fmaf(q0[j], kf[j], a0); a1 = fmaf(q1[j], kf[j], a1); }
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) {
+                a0 += __shfl_xor_sync(0xFFFFFFFFu, a0, o);
+                a1 += __shfl_xor_sync(0xFFFFFFFFu, a1, o);
             }
-            s0 = a0;
-            s1 = a1;
+            const bool valid = t0 + pass * 4 + (lane >> 3) < end;
+            sc[0][pass] = valid ? a0 : -INFINITY;
+            sc[1][pass] = valid ? a1 : -INFINITY;
         }
-        float mx0 = s0, mx1 = s1;
+        // online softmax over this warp's 16 positions (4 per lane group)
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, o));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, o));
+        for (int h = 0; h < 2; h++) {
+            float mx = fmaxf(fmaxf(sc[h][0], sc[h][1]), fmaxf(sc[h][2], sc[h][3]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 16));
+            const float mn = fmaxf(m[h], mx);
+            const float c = (mn == -INFINITY) ? 1.f : exp2f(m[h] - mn);
+            float sum = 0.f;
+#pragma unroll
+            for (int pass = 0; pass < 4; pass++) {
+                const float e = (sc[h][pass] == -INFINITY) ? 0.f : exp2f(sc[h][pass] - mn);
+                sc[h][pass] = e;
+                sum += e;
+            }
+            sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 8);
+            sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 16);
+            l[h] = l[h] * c + sum;
+            m[h] = mn;
+#pragma unroll
+            for (int d = 0; d < 4; d++) acc[h][d] *= c;
         }
-        const float mn0 = fmaxf(m[0], mx0), mn1 = fmaxf(m[1], mx1);
-        const float c0 = exp2f(m[0] - mn0), c1 = exp2f(m[1] - mn1);
-        m[0] = mn0;
-        m[1] = mn1;
-        const float p0 = exp2f(s0 - mn0), p1 = exp2f(s1 - mn1);
-        float sum0 = p0, sum1 = p1;
+        if (g8 == 0) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            sum0 += __shfl_xor_sync(0xFFFFFFFFu, sum0, o);
-            sum1 += __shfl_xor_sync(0xFFFFFFFFu, sum1, o);
+            for (int pass = 0; pass < 4; pass++) {
+                ps[warp][0][pass * 4 + (lane >> 3)] = sc[0][pass];
+                ps[warp][1][pass * 4 + (lane >> 3)] = sc[1][pass];
+            }
         }
-        l[0] = l[0] * c0 + sum0;
-        l[1] = l[1] * c1 + sum1;
-#pragma unroll
-        for (int d = 0; d < 8; d++) { acc[0][d] *= c0; acc[1][d] *= c1; }
-        ps[warp][0][lane] = p0;
-        ps[warp][1][lane] = p1;
         __syncwarp();
-        // 32 V rows: 16 lanes per 256-byte row, 2 rows per instruction, all
-        // 16 loads in flight before the first use.
-        const int nvalid = min(32, end - base);
-        const uint16_t *vr = vbase + (size_t)base * HD + d8;
-        uint4 vq[16];
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-            const int j = 2 * i + half;
-            vq[i] = (j < nvalid) ? __ldg((const uint4 *)(vr + (size_t)j * HD)) : make_uint4(0, 0, 0, 0);
-        }
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-            const int j = 2 * i + half;
+        const int nvalid = min(16, end - t0);
+        for (int j = 0; j < nvalid; j++) {
+            const uint2 v2 = *(const uint2 *)(vt + (warp * 16 + j) * (HD * 2) + 8 * lane);
             const float w0 = ps[warp][0][j], w1 = ps[warp][1][j];
-            float vf[8];
-            bf16x8(vq[i], vf);
-#pragma unroll
-            for (int d = 0; d < 8; d++) {
-                acc[0][d] = fmaf(w0, vf[d], acc[0][d]);
-                acc[1][d] = fmaf(w1, vf[d], acc[1][d]);
-            }
+            const float v0 = __uint_as_float(v2.x << 16), v1 = __uint_as_float(v2.x & 0xFFFF0000u);
+            const float v2f = __uint_as_float(v2.y << 16), v3 = __uint_as_float(v2.y & 0xFFFF0000u);
+            acc[0][0] = fmaf(w0, v0, acc[0][0]); acc[0][1] = fmaf(w0, v1, acc[0][1]);
+            acc[0][2] = fmaf(w0, v2f, acc[0][2]); acc[0][3] = fmaf(w0, v3, acc[0][3]);
+            acc[1][0] = fmaf(w1, v0, acc[1][0]); acc[1][1] = fmaf(w1, v1, acc[1][1]);
+            acc[1][2] = fmaf(w1, v2f, acc[1][2]); acc[1][3] = fmaf(w1, v3, acc[1][3]);
         }
         __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        // refill this stage with tile + STAGES once every warp has released it
+        if (threadIdx.x == 0 && tile + DC_STAGES < n_tiles) {
+            if (!mbar_wait(&empty[st], par)) ok = false;
+            else issue(tile + DC_STAGES);
+        }
     }
-    // merge the two row-parity halves: lanes 0..15 then hold dims d8..d8+7
-#pragma unroll
-    for (int d = 0; d < 8; d++) {
-        acc[0][d] += __shfl_xor_sync(0xFFFFFFFFu, acc[0][d], 16);
-        acc[1][d] += __shfl_xor_sync(0xFFFFFFFFu, acc[1][d], 16);
-    }
+    // Copies issued but never consumed (only after an expired wait): let them land.
+    if (!ok && threadIdx.x == 0)
+        for (int i = 0; i < min(DC_STAGES, n_tiles); i++) mbar_wait(&full[i], 0);
 
     if (lane == 0) { wm[warp][0] = m[0]; wm[warp][1] = m[1]; wl[warp][0] = l[0]; wl[warp][1] = l[1]; }
-    if (lane < 16) {
 #pragma unroll
-        for (int d = 0; d < 8; d++) { wo[warp][0][d8 + d] = acc[0][d]; wo[warp][1][d8 + d] = acc[1][d]; }
-    }
+    for (int d = 0; d < 4; d++) { wo[warp][0][4 * lane + d] = acc[0][d]; wo[warp][1][4 * lane + d] = acc[1][d]; }
     __syncthreads();
 
     for (int i = threadIdx.x; i < 2 * HD; i += DC_THREADS) {
@@ -431,7 +462,8 @@ int launch_attn_prefill(cudaStream_t st, const AttnPrefillArgs &a, int n_seqs) {
 }
 
 int attn_decode_splits(int n_seqs, int max_kv_len, int max_splits) {
-    // Enough CTAs to cover the SMs twice; each split keeps >= 64 positions.
+    // Enough CTAs to cover the SMs twice (2 resident per SM); splits are
+    // rounded to whole 64-position tiles inside the kernel.
     int splits = (2 * 148 + n_seqs * NKV - 1) / (n_seqs * NKV);
     const int by_len = (max_kv_len + 63) / 64;
     if (splits > by_len) splits = by_len;
@@ -443,8 +475,16 @@ int launch_attn_decode(cudaStream_t st, const AttnDecodeArgs &a, int n_seqs) {
     if (n_seqs <= 0) return N550_OK;
     if (a.splits < 1) return N550_ERR_ARG;
     if (a.splits > 1 && (!a.part_m || !a.part_l || !a.part_o)) return N550_ERR_ARG;
+    static bool dc_attr[64];
+    int dev = 0;
+    N550_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev >= 0 && dev < 64 && !dc_attr[dev]) {
+        N550_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, DC_SMEM));
+        dc_attr[dev] = true;
+    }
     dim3 grid(a.splits, NKV, n_seqs);
-    attn_decode_kernel<<<grid, DC_THREADS, 0, st>>>(a);
+    attn_decode_kernel<<<grid, DC_THREADS, DC_SMEM, st>>>(a);
     N550_LAUNCH_CHECK();
     if (a.splits > 1) {
         attn_combine_kernel<<<dim3(16, n_seqs), HD, 0, st>>>(a);
