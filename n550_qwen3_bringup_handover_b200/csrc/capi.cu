@@ -82,7 +82,7 @@ int device_gemm(cudaStream_t st, int mode, int kblock, const void *a, int a_type
     if (M <= 8 && launch_gemv(st, epi, abf, ldab, b, ldb, c, ldc, M, N, K) == N550_OK) {
         rc = N550_OK;
     } else if (M < 1024 && tc_shape_ok(abf, ldab, b, ldb, K) &&
-               tc_splitk_plan(M, N, K, epi, 128, &kt) > 1) {
+               tc_splitk_plan(M, N, K, epi, 64, &kt) > 1) {
         // skinny M: split the K loop, partials in a stream-ordered workspace
         const size_t ws_bytes = (size_t)8 * M * N * 4;
         float *ws = nullptr;
@@ -157,7 +157,7 @@ inline void set_status(int s) { t_status = s; }
 int skinny_or_full(cudaStream_t st, int epi, const uint16_t *a, int lda, const uint16_t *b, int ldb,
                    const uint16_t *b2, void *c, int ldc, int M, int N, int K) {
     int kt;
-    if (M < 1024 && tc_splitk_plan(M, N, K, epi, 128, &kt) > 1) {
+    if (M < 1024 && tc_splitk_plan(M, N, K, epi, 64, &kt) > 1) {
         const size_t ws_bytes = (size_t)8 * M * N * (epi == TC_EPI_SILU_BF16 ? 2 : 1) * 4;
         float *ws = nullptr;
         if (cudaMallocAsync((void **)&ws, ws_bytes, st) != cudaSuccess) {

@@ -34,7 +34,7 @@ constexpr int THREADS = 192;
 
 template <int BN>
 struct TcCfg {
-    static constexpr int STAGES = (BN >= 256) ? 4 : 6;
+    static constexpr int STAGES = (BN >= 256) ? 4 : (BN >= 128 ? 6 : 8);
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -247,7 +247,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmB2,
                const TcEpilogue ep, int M, int N, int K, int m_fast, int ksplit,
-               int kt_per, float *ws) {
+               int kt_per, float *ws, bool partials) {
     using Cfg = TcCfg<BN>;
     constexpr int STAGES = Cfg::STAGES;
     constexpr bool SILU = (EPI == TC_EPI_SILU_BF16);
@@ -375,7 +375,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
             const int row0 = mb * BM + q * 32;          // first row of this warp's quarter
-            if (ksplit > 1) {
+            if (ksplit > 1 || partials) {
                 // Partial sums of K slice sk: raw FP32 accumulators into
                 // ws[sk][M][ldw]; SwiGLU tiles put gate at column n, up at N + n.
                 const int ldw = SILU ? 2 * N : N;
@@ -505,7 +505,8 @@ int num_sms() {
 template <int BN, int EPI>
 int launch_impl(cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tb,
                 const CUtensorMap &tb2, const TcEpilogue &ep, int M, int N, int K,
-                int max_ctas, int ksplit = 1, int kt_per = 1 << 30, float *ws = nullptr) {
+                int max_ctas, int ksplit = 1, int kt_per = 1 << 30, float *ws = nullptr,
+                bool partials = false) {
     using Cfg = TcCfg<BN>;
     static bool attr_done[64] = {};
     int dev = 0;
@@ -527,7 +528,7 @@ int launch_impl(cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tb,
     // otherwise walk N fastest so that A rows are shared.
     const int m_fast = (long long)N * (EPI == TC_EPI_SILU_BF16 ? 2 : 1) > (long long)M;
     gemm_tc_kernel<BN, EPI><<<grid, THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tb2, ep, M, N, K, m_fast,
-                                                                     ksplit, kt_per, ws);
+                                                                     ksplit, kt_per, ws, partials);
     N550_LAUNCH_CHECK();
     return N550_OK;
 }
@@ -602,19 +603,20 @@ int tc_splitk_plan(int M, int N, int K, int epi, int bn, int *kt_per) {
     return (num_k + *kt_per - 1) / *kt_per;
 }
 
-int launch_gemm_tc_splitk(cudaStream_t st, int epi, const uint16_t *a, int lda, const uint16_t *b,
-                          int ldb, const uint16_t *b2, void *c, int ldc, int M, int N, int K,
-                          float *ws, size_t ws_bytes) {
+int launch_gemm_tc_partials(cudaStream_t st, int epi, const uint16_t *a, int lda, const uint16_t *b,
+                            int ldb, const uint16_t *b2, int M, int N, int K, float *ws,
+                            size_t ws_bytes, int *ks_out) {
+    *ks_out = 0;
     if (M <= 0 || N <= 0) return N550_OK;
-    const int bn = 128;
+    if (!tc_shape_ok(a, lda, b, ldb, K)) return N550_ERR_UNSUPPORTED;
+    if (epi != TC_EPI_F32 && epi != TC_EPI_SILU_BF16) return N550_ERR_ARG;
+    // 64-wide tiles: twice the tiles of 128 for the same N, so half the K
+    // slices (and half the partial-sum traffic) reach the same SM count.
+    const int bn = 64;
     int kt_per = 0;
     const int ks = tc_splitk_plan(M, N, K, epi, bn, &kt_per);
     const size_t need = (size_t)ks * M * (epi == TC_EPI_SILU_BF16 ? 2 * N : N) * 4;
-    if (ks == 1 || !ws || need > ws_bytes)
-        return launch_gemm_tc(st, epi, bn, a, lda, b, ldb, b2, c, ldc, M, N, K, 0);
-    if (!tc_shape_ok(a, lda, b, ldb, K)) return N550_ERR_UNSUPPORTED;
-    if (epi != TC_EPI_F32 && epi != TC_EPI_BF16 && epi != TC_EPI_RESID_F32 && epi != TC_EPI_SILU_BF16)
-        return N550_ERR_ARG;
+    if (!ws || need > ws_bytes) return N550_ERR_ARG;
     int rc = get_encoder();
     if (rc) return rc;
     const int brows = (epi == TC_EPI_SILU_BF16) ? bn / 2 : bn;
@@ -627,21 +629,47 @@ int launch_gemm_tc_splitk(cudaStream_t st, int epi, const uint16_t *a, int lda, 
         tb2 = tb;
     }
     TcEpilogue ep{};
+    // The split path of the kernel stores raw partials (also for ks == 1).
     if (epi == TC_EPI_SILU_BF16)
-        rc = launch_impl<128, TC_EPI_SILU_BF16>(st, ta, tb, tb2, ep, M, N, K, 0, ks, kt_per, ws);
+        rc = launch_impl<64, TC_EPI_SILU_BF16>(st, ta, tb, tb2, ep, M, N, K, 0, ks, kt_per, ws, true);
     else
-        rc = launch_impl<128, TC_EPI_F32>(st, ta, tb, tb2, ep, M, N, K, 0, ks, kt_per, ws);
-    if (rc) return rc;
+        rc = launch_impl<64, TC_EPI_F32>(st, ta, tb, tb2, ep, M, N, K, 0, ks, kt_per, ws, true);
+    if (!rc) *ks_out = ks;
+    return rc;
+}
+
+int launch_splitk_reduce(cudaStream_t st, int epi, const float *ws, int ks, int M, int N, void *c,
+                         int ldc) {
     const size_t total = (size_t)M * N;
+    if (!total) return N550_OK;
     const int grid = (int)std::min<size_t>((total + 255) / 256, 148 * 8);
     switch (epi) {
     case TC_EPI_F32: splitk_reduce_kernel<TC_EPI_F32><<<grid, 256, 0, st>>>(ws, ks, M, N, c, ldc); break;
     case TC_EPI_BF16: splitk_reduce_kernel<TC_EPI_BF16><<<grid, 256, 0, st>>>(ws, ks, M, N, c, ldc); break;
     case TC_EPI_RESID_F32: splitk_reduce_kernel<TC_EPI_RESID_F32><<<grid, 256, 0, st>>>(ws, ks, M, N, c, ldc); break;
-    default: splitk_reduce_kernel<TC_EPI_SILU_BF16><<<grid, 256, 0, st>>>(ws, ks, M, N, c, ldc); break;
+    case TC_EPI_SILU_BF16: splitk_reduce_kernel<TC_EPI_SILU_BF16><<<grid, 256, 0, st>>>(ws, ks, M, N, c, ldc); break;
+    default: return N550_ERR_ARG;
     }
     N550_LAUNCH_CHECK();
     return N550_OK;
+}
+
+int launch_gemm_tc_splitk(cudaStream_t st, int epi, const uint16_t *a, int lda, const uint16_t *b,
+                          int ldb, const uint16_t *b2, void *c, int ldc, int M, int N, int K,
+                          float *ws, size_t ws_bytes) {
+    if (M <= 0 || N <= 0) return N550_OK;
+    int kt_per = 0;
+    const int ks = tc_splitk_plan(M, N, K, epi, 64, &kt_per);
+    const size_t need = (size_t)ks * M * (epi == TC_EPI_SILU_BF16 ? 2 * N : N) * 4;
+    if (ks == 1 || !ws || need > ws_bytes)
+        return launch_gemm_tc(st, epi, 128, a, lda, b, ldb, b2, c, ldc, M, N, K, 0);
+    if (epi != TC_EPI_F32 && epi != TC_EPI_BF16 && epi != TC_EPI_RESID_F32 && epi != TC_EPI_SILU_BF16)
+        return N550_ERR_ARG;
+    int got = 0;
+    const int pe = epi == TC_EPI_SILU_BF16 ? TC_EPI_SILU_BF16 : TC_EPI_F32;
+    int rc = launch_gemm_tc_partials(st, pe, a, lda, b, ldb, b2, M, N, K, ws, ws_bytes, &got);
+    if (rc) return rc;
+    return launch_splitk_reduce(st, epi, ws, got, M, N, c, ldc);
 }
 
 bool tc_shape_ok(const void *a, int lda, const void *b, int ldb, int K) {

@@ -60,6 +60,14 @@ int launch_gemm_tc(cudaStream_t st, int epi, int bn, const uint16_t *a, int lda,
 int launch_gemm_tc_splitk(cudaStream_t st, int epi, const uint16_t *a, int lda, const uint16_t *b,
                           int ldb, const uint16_t *b2, void *c, int ldc, int M, int N, int K,
                           float *ws, size_t ws_bytes);
+// Only the partial-sum stage: ks_out slices of raw FP32 accumulators in ws
+// ([slice][M][N], SwiGLU [slice][M][2N] with up at column N + n); epi is
+// TC_EPI_F32 or TC_EPI_SILU_BF16. Consumers sum the slices in order.
+int launch_gemm_tc_partials(cudaStream_t st, int epi, const uint16_t *a, int lda, const uint16_t *b,
+                            int ldb, const uint16_t *b2, int M, int N, int K, float *ws,
+                            size_t ws_bytes, int *ks_out);
+int launch_splitk_reduce(cudaStream_t st, int epi, const float *ws, int ks, int M, int N, void *c,
+                         int ldc);
 // Number of K slices launch_gemm_tc_splitk uses (1 = no split).
 int tc_splitk_plan(int M, int N, int K, int epi, int bn, int *kt_per);
 

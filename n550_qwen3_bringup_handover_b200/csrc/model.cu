@@ -177,50 +177,62 @@ __global__ void embed_kernel(float *x, const uint16_t *__restrict__ embed, const
 // token's position (ops_scalar.c:21-35), and the K/V cache write
 // (qwen3.c:498-511). One warp per head; 32 heads per token
 // ([q 16 | k 8 | v 8] x 128 is the qkv row).
-__global__ void __launch_bounds__(256)
-qknorm_rope_kv_kernel(const float *__restrict__ qkv, int ldqkv, const uint16_t *__restrict__ qn,
-                      const uint16_t *__restrict__ kn, const int32_t *__restrict__ tok_pos,
+// Sum of up to 8 split-K partial slices (issued together), or the plain row.
+__device__ __forceinline__ float sum_slices(const float *p, int ks, size_t slice) {
+    if (ks <= 0) return p[0];
+    float v[8];
+#pragma unroll
+    for (int sk = 0; sk < 8; sk++) v[sk] = sk < ks ? p[sk * slice] : 0.f;
+    float a = v[0];
+#pragma unroll
+    for (int sk = 1; sk < 8; sk++) a += v[sk];
+    return a;
+}
+
+__global__ void __launch_bounds__(1024)
+qknorm_rope_kv_kernel(const float *__restrict__ qkv, int ldqkv, int ks, size_t slice,
+                      const uint16_t *__restrict__ qn, const uint16_t *__restrict__ kn,
+                      const float2 *__restrict__ rope, const int32_t *__restrict__ tok_pos,
                       const int32_t *__restrict__ tok_seq, int layer, uint16_t *kc, uint16_t *vc,
                       int max_len, uint16_t *q_bf16, float *q_f32, int ldq) {
+    // One warp per head (32 per token): qkv row t, or (ks > 0) the sum of ks
+    // split-K partial slices of it; RoPE factors from the per-position table.
     const int t = blockIdx.x;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hd = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = tok_pos[t], seq = tok_seq[t];
-    const float *row = qkv + (size_t)t * ldqkv;
-    for (int hd = warp; hd < 32; hd += 8) {
-        float v[4];
+    const float *row = qkv + (size_t)t * ldqkv + hd * HDIM + lane;
+    float v[4];
 #pragma unroll
-        for (int j = 0; j < 4; j++) v[j] = row[hd * HDIM + lane + 32 * j];
-        if (hd < 24) {
-            const uint16_t *w = hd < 16 ? qn : kn;
-            float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+    for (int j = 0; j < 4; j++) v[j] = sum_slices(row + 32 * j, ks, slice);
+    if (hd < 24) {
+        const uint16_t *w = hd < 16 ? qn : kn;
+        float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-            const float sc = 1.0f / sqrtf(ss / (float)HDIM + EPS);
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+        const float sc = 1.0f / sqrtf(ss / (float)HDIM + EPS);
 #pragma unroll
-            for (int j = 0; j < 4; j++) v[j] = v[j] * sc * bf16_bits_to_f32(w[lane + 32 * j]);
+        for (int j = 0; j < 4; j++) v[j] = v[j] * sc * bf16_bits_to_f32(w[lane + 32 * j]);
 #pragma unroll
-            for (int j = 0; j < 2; j++) {          // pairs (i, i + 64), i = lane + 32 j
-                float s, c;
-                sincosf((float)pos * c_inv_freq[lane + 32 * j], &s, &c);
-                const float a = v[j], b = v[j + 2];
-                v[j] = a * c - b * s;
-                v[j + 2] = b * c + a * s;
-            }
+        for (int j = 0; j < 2; j++) {              // pairs (i, i + 64), i = lane + 32 j
+            const float2 cs = rope[(size_t)pos * 64 + lane + 32 * j];
+            const float a = v[j], b = v[j + 2];
+            v[j] = a * cs.x - b * cs.y;
+            v[j + 2] = b * cs.x + a * cs.y;
         }
-        if (hd < 16) {
-            const size_t o = (size_t)t * ldq + hd * HDIM + lane;
+    }
+    if (hd < 16) {
+        const size_t o = (size_t)t * ldq + hd * HDIM + lane;
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                if (q_bf16) q_bf16[o + 32 * j] = f32_to_bf16_rne(v[j]);
-                if (q_f32) q_f32[o + 32 * j] = v[j];
-            }
-        } else {
-            const int kvh = (hd - 16) & 7;
-            uint16_t *dst = (hd < 24 ? kc : vc) +
-                            (((size_t)(seq * NLAYER + layer) * NKVH + kvh) * max_len + pos) * HDIM;
-#pragma unroll
-            for (int j = 0; j < 4; j++) dst[lane + 32 * j] = f32_to_bf16_rne(v[j]);
+        for (int j = 0; j < 4; j++) {
+            if (q_bf16) q_bf16[o + 32 * j] = f32_to_bf16_rne(v[j]);
+            if (q_f32) q_f32[o + 32 * j] = v[j];
         }
+    } else {
+        const int kvh = (hd - 16) & 7;
+        uint16_t *dst = (hd < 24 ? kc : vc) +
+                        (((size_t)(seq * NLAYER + layer) * NKVH + kvh) * max_len + pos) * HDIM;
+#pragma unroll
+        for (int j = 0; j < 4; j++) dst[lane + 32 * j] = f32_to_bf16_rne(v[j]);
     }
 }
 
@@ -247,6 +259,42 @@ __global__ void decode_advance_kernel(const int32_t *next, int32_t *tokens, int3
     }
     __syncthreads();
     if (threadIdx.x == 0) *counter = step + 1;
+}
+
+// x[t] += sum of ks split-K partial slices (the o / down projection, the
+// residual add of qwen3.c:523/543), then, if w is given, out[t] =
+// bf16(rmsnorm(x[t]) * w) for the next GEMM (qwen3.c:471/527/547). One CTA
+// per row of 1024.
+__global__ void __launch_bounds__(256)
+resid_norm_rows_kernel(float *x, const float *__restrict__ ws, int ks, size_t slice,
+                       const uint16_t *__restrict__ w, uint16_t *out) {
+    __shared__ float red[8];
+    const int t = blockIdx.x;
+    float *xr = x + (size_t)t * H;
+    const float *pr = ws + (size_t)t * H;
+    float xv[4];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int c = threadIdx.x + 256 * j;
+        xv[j] = xr[c] + sum_slices(pr + c, ks, slice);
+        xr[c] = xv[j];
+        ss = fmaf(xv[j], xv[j], ss);
+    }
+    if (!w) return;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) ss += red[i];
+    const float sc = 1.0f / sqrtf(ss / (float)H + EPS);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int c = threadIdx.x + 256 * j;
+        out[(size_t)t * H + c] = f32_to_bf16_rne(xv[j] * sc * bf16_bits_to_f32(w[c]));
+    }
 }
 
 // Final RMSNorm of the last token of each sequence (qwen3.c:547-573 only
@@ -489,12 +537,28 @@ int mgemm(n550_model *m, cudaStream_t st, int epi, const uint16_t *a, int lda, c
                           ldc, M, N, K, 0);
 }
 
-int launch_qknorm_rope_kv(n550_model *m, cudaStream_t st, int T, int l, bool decode) {
-    qknorm_rope_kv_kernel<<<T, 256, 0, st>>>(m->qkv, QKVD, W(m, l, 4), W(m, l, 5), m->tok_pos,
-                                             m->tok_seq, l, m->kc, m->vc, m->cfg.max_len,
+int launch_qknorm_rope_kv(n550_model *m, cudaStream_t st, int T, int l, bool decode,
+                          const float *src = nullptr, int ks = 0) {
+    qknorm_rope_kv_kernel<<<T, 1024, 0, st>>>(src ? src : m->qkv, QKVD, ks, (size_t)T * QKVD,
+                                             W(m, l, 4), W(m, l, 5), m->rope, m->tok_pos, m->tok_seq, l,
+                                             m->kc, m->vc, m->cfg.max_len,
                                              decode ? nullptr : m->qb, decode ? m->qf : nullptr, QD);
     N550_LAUNCH_CHECK();
     return N550_OK;
+}
+
+int launch_resid_norm(cudaStream_t st, float *x, const float *ws, int ks, int T,
+                      const uint16_t *w, uint16_t *out) {
+    resid_norm_rows_kernel<<<T, 256, 0, st>>>(x, ws, ks, (size_t)T * H, w, out);
+    N550_LAUNCH_CHECK();
+    return N550_OK;
+}
+
+// Split-K partial sums of A . W^T into m->ws (fast mode, skinny M).
+int partials(n550_model *m, cudaStream_t st, const uint16_t *a, int lda, const uint16_t *w, int M,
+             int N, int K, int *ks) {
+    return launch_gemm_tc_partials(st, TC_EPI_F32, a, lda, w, K, nullptr, M, N, K, m->ws,
+                                   m->ws_bytes, ks);
 }
 
 int launch_final_norm(cudaStream_t st, uint16_t *xl, const float *x, const uint16_t *w, int Sc, int Lc) {
@@ -505,22 +569,74 @@ int launch_final_norm(cudaStream_t st, uint16_t *xl, const float *x, const uint1
 
 // All 28 layers over T tokens already embedded in m->x, with tok_pos/tok_seq
 // set. decode: one token per sequence (seq_ids/pos arrays of n_seqs = T).
-int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t *seq_ids,
-               const int32_t *pos, int Sc, int Lc, int p0) {
-    const n550_model_config &c = m->cfg;
-    int rc = N550_OK;
 #define STEP(kind, nk, expr)                          \
     do {                                              \
         ProfScope ps_(m, st, (kind), (nk));           \
         if ((rc = (expr))) return rc;                 \
     } while (0)
+
+int run_attention(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t *seq_ids,
+                  const int32_t *pos, int Sc, int Lc, int p0, int l) {
+    const n550_model_config &c = m->cfg;
+    int rc = N550_OK;
+    if (decode) {
+        AttnDecodeArgs a{};
+        a.q_f32 = m->qf;
+        a.kc = m->kc; a.vc = m->vc; a.out = m->attn;
+        a.seq_ids = seq_ids; a.pos = pos;
+        a.ldq = QD; a.ldo = QD; a.layer = l; a.max_len = c.max_len;
+        a.splits = attn_decode_splits(T, c.max_len, MAX_SPLITS);
+        a.part_m = m->part_m; a.part_l = m->part_l; a.part_o = m->part_o;
+        STEP(N550_PROF_ATTN, a.splits > 1 ? 2 : 1, launch_attn_decode(st, a, T));
+    } else {
+        AttnPrefillArgs a{};
+        a.q = m->qb; a.kc = m->kc; a.vc = m->vc; a.out = m->attn; a.seq_ids = seq_ids;
+        a.ldq = QD; a.ldo = QD; a.L = Lc; a.pos0 = p0; a.layer = l; a.max_len = c.max_len;
+        STEP(N550_PROF_ATTN, 1, launch_attn_prefill(st, a, Sc));
+    }
+    return N550_OK;
+}
+
+// Skinny token counts (8 < T < 1024: decode, short prompts). Every projection
+// is a split-K tensor-core GEMM whose partial sums feed a fused row kernel:
+// QKV -> sum + QK-norm + RoPE + K/V write; o and down -> sum + residual add +
+// the next RMSNorm (input_layernorm of the next layer, or the final norm for
+// decode, whose rows are all last tokens); gate/up -> sum + SwiGLU.
+// Sets *xl_ready when the final norm was applied to all T rows (into m->xl).
+int run_layers_split(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t *seq_ids,
+                     const int32_t *pos, int Sc, int Lc, int p0, bool *xl_ready) {
+    int rc = N550_OK, ks = 0, kt;
+    const int gu_kernels = tc_splitk_plan(T, INTER, H, TC_EPI_SILU_BF16, 64, &kt) > 1 ? 2 : 1;
+    STEP(N550_PROF_RMSNORM, 1, launch_rmsnorm(st, m->xb, N550_BF16, m->x, W(m, 0, 0), T, H, EPS));
+    for (int l = 0; l < NLAYER; l++) {
+        STEP(N550_PROF_GEMM_QKV, 1, partials(m, st, m->xb, H, m->wqkv[l], T, QKVD, H, &ks));
+        STEP(N550_PROF_QKNORM_ROPE, 1, launch_qknorm_rope_kv(m, st, T, l, decode, m->ws, ks));
+        if ((rc = run_attention(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, l))) return rc;
+        STEP(N550_PROF_GEMM_O, 1, partials(m, st, m->attn, QD, W(m, l, 6), T, H, QD, &ks));
+        STEP(N550_PROF_RMSNORM, 1, launch_resid_norm(st, m->x, m->ws, ks, T, W(m, l, 7), m->xb));
+        STEP(N550_PROF_GEMM_GATEUP, gu_kernels,
+             mgemm(m, st, TC_EPI_SILU_BF16, m->xb, H, W(m, l, 8), W(m, l, 9), m->h, INTER, T, INTER, H));
+        STEP(N550_PROF_GEMM_DOWN, 1, partials(m, st, m->h, INTER, W(m, l, 10), T, H, INTER, &ks));
+        const uint16_t *wn = l + 1 < NLAYER ? W(m, l + 1, 0) : (decode ? m->t[N_TENSORS - 1] : nullptr);
+        uint16_t *dst = l + 1 < NLAYER ? m->xb : m->xl;
+        STEP(N550_PROF_RMSNORM, 1, launch_resid_norm(st, m->x, m->ws, ks, T, wn, dst));
+    }
+    *xl_ready = decode;
+    return N550_OK;
+}
+
+// All 28 layers over T tokens already embedded in m->x, with tok_pos/tok_seq
+// set. decode: one token per sequence (seq_ids/pos arrays of n_seqs = T).
+int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t *seq_ids,
+               const int32_t *pos, int Sc, int Lc, int p0, bool *xl_ready) {
+    const n550_model_config &c = m->cfg;
+    int rc = N550_OK;
+    *xl_ready = false;
     const bool exact = c.gemm_mode == N550_MODE_EXACT;
-    int kt;
-    const bool split = !exact && T > 8 && T < 1024;
-    const int gu_kernels = exact ? 3 : (T <= 8 ? 3 : (split && tc_splitk_plan(T, INTER, H, TC_EPI_SILU_BF16, 128, &kt) > 1 ? 2 : 1));
-    const int o_kernels = exact ? 2 : (split && tc_splitk_plan(T, H, QD, TC_EPI_RESID_F32, 128, &kt) > 1 ? 2 : 1);
-    const int d_kernels = exact ? 2 : (split && tc_splitk_plan(T, H, INTER, TC_EPI_RESID_F32, 128, &kt) > 1 ? 2 : 1);
-    const int qkv_kernels = (split && tc_splitk_plan(T, QKVD, H, TC_EPI_F32, 128, &kt) > 1) ? 2 : 1;
+    if (!exact && T > 8 && T < 1024)
+        return run_layers_split(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, xl_ready);
+    const int gu_kernels = exact || T <= 8 ? 3 : 1;
+    const int res_kernels = exact ? 2 : 1;
     for (int l = 0; l < NLAYER; l++) {
         STEP(N550_PROF_RMSNORM, 1, launch_rmsnorm(st, m->xb, N550_BF16, m->x, W(m, l, 0), T, H, EPS));
         if (!exact && T >= 1024) {
@@ -535,40 +651,28 @@ int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t
             q.rope = m->rope; q.eps = EPS;
             STEP(N550_PROF_GEMM_QKV, 1, launch_gemm_tc_qkv(st, m->xb, H, m->wqkv[l], q, T, H, 0));
         } else {
-            STEP(N550_PROF_GEMM_QKV, qkv_kernels,
+            STEP(N550_PROF_GEMM_QKV, 1,
                  mgemm(m, st, TC_EPI_F32, m->xb, H, m->wqkv[l], nullptr, m->qkv, QKVD, T, QKVD, H));
             STEP(N550_PROF_QKNORM_ROPE, 1, launch_qknorm_rope_kv(m, st, T, l, decode));
         }
-        if (decode) {
-            AttnDecodeArgs a{};
-            a.q_f32 = m->qf;
-            a.kc = m->kc; a.vc = m->vc; a.out = m->attn;
-            a.seq_ids = seq_ids; a.pos = pos;
-            a.ldq = QD; a.ldo = QD; a.layer = l; a.max_len = c.max_len;
-            a.splits = attn_decode_splits(T, c.max_len, MAX_SPLITS);
-            a.part_m = m->part_m; a.part_l = m->part_l; a.part_o = m->part_o;
-            STEP(N550_PROF_ATTN, a.splits > 1 ? 2 : 1, launch_attn_decode(st, a, T));
-        } else {
-            AttnPrefillArgs a{};
-            a.q = m->qb; a.kc = m->kc; a.vc = m->vc; a.out = m->attn; a.seq_ids = seq_ids;
-            a.ldq = QD; a.ldo = QD; a.L = Lc; a.pos0 = p0; a.layer = l; a.max_len = c.max_len;
-            STEP(N550_PROF_ATTN, 1, launch_attn_prefill(st, a, Sc));
-        }
-        STEP(N550_PROF_GEMM_O, o_kernels,
+        if ((rc = run_attention(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, l))) return rc;
+        STEP(N550_PROF_GEMM_O, res_kernels,
              mgemm(m, st, TC_EPI_RESID_F32, m->attn, QD, W(m, l, 6), nullptr, m->x, H, T, H, QD));
         STEP(N550_PROF_RMSNORM, 1, launch_rmsnorm(st, m->xb, N550_BF16, m->x, W(m, l, 7), T, H, EPS));
         STEP(N550_PROF_GEMM_GATEUP, gu_kernels,
              mgemm(m, st, TC_EPI_SILU_BF16, m->xb, H, W(m, l, 8), W(m, l, 9), m->h, INTER, T, INTER, H));
-        STEP(N550_PROF_GEMM_DOWN, d_kernels,
+        STEP(N550_PROF_GEMM_DOWN, res_kernels,
              mgemm(m, st, TC_EPI_RESID_F32, m->h, INTER, W(m, l, 10), nullptr, m->x, H, T, H, INTER));
     }
     return N550_OK;
 }
 
 // Last-token logits and argmax for Sc sequences whose rows are i*Lc + Lc - 1.
-int run_head(n550_model *m, cudaStream_t st, int Sc, int Lc, float *logits, int32_t *next) {
+int run_head(n550_model *m, cudaStream_t st, int Sc, int Lc, float *logits, int32_t *next,
+             bool xl_ready = false) {
     int rc = N550_OK;
-    STEP(N550_PROF_RMSNORM, 1, launch_final_norm(st, m->xl, m->x, m->t[N_TENSORS - 1], Sc, Lc));
+    if (!xl_ready)
+        STEP(N550_PROF_RMSNORM, 1, launch_final_norm(st, m->xl, m->x, m->t[N_TENSORS - 1], Sc, Lc));
     STEP(N550_PROF_GEMM_LMHEAD, 1,
          mgemm(m, st, TC_EPI_F32, m->xl, H, m->t[0], nullptr, logits, VOCAB, Sc, VOCAB, H));
     if (next) STEP(N550_PROF_OTHER, 1, launch_argmax(st, logits, Sc, VOCAB, VOCAB, next));
@@ -664,7 +768,8 @@ int n550_qwen3_prefill(n550_model_t *m, void *stream, const int32_t *tokens, con
                                                 seq_len, j0);
                 N550_LAUNCH_CHECK();
             }
-            if ((rc = run_layers(m, st, T, false, seq_ids + s0, nullptr, Sc, Lc, p0))) return rc;
+            bool xl_ready = false;
+            if ((rc = run_layers(m, st, T, false, seq_ids + s0, nullptr, Sc, Lc, p0, &xl_ready))) return rc;
             if (j0 + Lc == seq_len) {
                 float *lg = logits ? logits + (size_t)s0 * VOCAB : m->logits;
                 if ((rc = run_head(m, st, Sc, Lc, lg, next_token ? next_token + s0 : nullptr)))
@@ -689,9 +794,10 @@ int n550_qwen3_decode(n550_model_t *m, void *stream, const int32_t *tokens, cons
         embed_kernel<<<n_seqs, 128, 0, st>>>(m->x, m->t[0], tokens, 1, 1, 0);
         N550_LAUNCH_CHECK();
     }
-    int rc = run_layers(m, st, n_seqs, true, seq_ids, pos, n_seqs, 1, 0);
+    bool xl_ready = false;
+    int rc = run_layers(m, st, n_seqs, true, seq_ids, pos, n_seqs, 1, 0, &xl_ready);
     if (rc) return rc;
-    return run_head(m, st, n_seqs, 1, logits ? logits : m->logits, next_token);
+    return run_head(m, st, n_seqs, 1, logits ? logits : m->logits, next_token, xl_ready);
 }
 
 int n550_qwen3_decode_steps(n550_model_t *m, void *stream, int32_t *tokens, const int32_t *seq_ids,
