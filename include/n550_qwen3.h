@@ -182,6 +182,29 @@ int n550_argmax(void *stream, const float *v, int rows, int n, int ld, int32_t *
 int n550_residual_add(void *stream, float *x, const float *y, size_t n);
 int n550_bf16_to_f32(void *stream, float *out, const uint16_t *in, size_t n);
 
+/* Causal GQA attention (qwen3.c:374-436, which the reference inlines in
+ * qwen3_forward_batch) over the BF16 KV cache, device pointers, stream-ordered.
+ * 16 query heads share 8 KV heads (head h reads KV head h/2), head_dim 128,
+ * scores scaled by 0.08838834764831845, softmax over positions 0..p.
+ *   k_cache, v_cache  [n_slots][28 layers][8 kv heads][max_len][128] BF16;
+ *                     sequence s reads slot seq_ids[s] (device int32 array)
+ * Prefill: n_seqs x L queries at positions pos0 .. pos0+L-1, whose K/V are
+ * already in the cache; q [n_seqs*L][ldq], out [n_seqs*L][ldo], head h at
+ * columns h*128 .. h*128+127. tcgen05 tensor cores (P rounded to BF16).
+ * Decode: one query per sequence at position pos[s] (device int32 array);
+ * q [n_seqs][ldq], out [n_seqs][ldo]. workspace may be NULL (one CTA per
+ * sequence and KV head) or n550_attention_decode_workspace(n_seqs, max_len)
+ * bytes of device memory for split-KV partials. */
+int n550_attention_prefill(void *stream, const uint16_t *q, int ldq, const uint16_t *k_cache,
+                           const uint16_t *v_cache, int n_slots, int max_len, int layer,
+                           const int32_t *seq_ids, int n_seqs, int L, int pos0, uint16_t *out,
+                           int ldo);
+int n550_attention_decode(void *stream, const uint16_t *q, int ldq, const uint16_t *k_cache,
+                          const uint16_t *v_cache, int n_slots, int max_len, int layer,
+                          const int32_t *seq_ids, const int32_t *pos, int n_seqs, uint16_t *out,
+                          int ldo, void *workspace, size_t workspace_bytes);
+size_t n550_attention_decode_workspace(int n_seqs, int max_len);
+
 /* Device status word written by bounded waits inside kernels; returns it and
  * clears it (N550_OK, or N550_ERR_TIMEOUT). Synchronises the device. */
 int n550_device_status(void);

@@ -77,6 +77,9 @@ def lib() -> C.CDLL:
         "n550_residual_add": (i, [vp, vp, vp, sz]),
         "n550_bf16_to_f32": (i, [vp, vp, vp, sz]),
         "n550_device_status": (i, []),
+        "n550_attention_prefill": (i, [vp, vp, i, vp, vp, i, i, i, vp, i, i, i, vp, i]),
+        "n550_attention_decode": (i, [vp, vp, i, vp, vp, i, i, i, vp, vp, i, vp, i, vp, sz]),
+        "n550_attention_decode_workspace": (sz, [i, i]),
     }
     optional = {
         "n550_qwen3_init": (i, [C.POINTER(vp), vp, sz, C.POINTER(ModelConfig)]),

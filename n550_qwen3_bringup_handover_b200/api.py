@@ -15,6 +15,7 @@ __all__ = [
     "qwen3_op_argmax", "qwen3_op_bf16_to_f32", "qwen3_op_dot", "qwen3_op_axpy",
     "last_status", "gemm", "rmsnorm", "rope", "silu_mul", "softmax", "argmax",
     "residual_add", "bf16_to_f32", "device_status", "stream_ptr", "gemm_residual", "gemm_swiglu",
+    "attention_prefill", "attention_decode",
 ]
 
 
@@ -215,6 +216,45 @@ def bf16_to_f32(b):
     import torch
     out = torch.empty(b.shape, dtype=torch.float32, device=b.device)
     check(lib().n550_bf16_to_f32(stream_ptr(), _dp(out), _dp(b), b.numel()), "n550_bf16_to_f32")
+    return out
+
+
+def _cache_dims(k_cache):
+    if k_cache.dim() != 5 or tuple(k_cache.shape[1:3]) != (28, 8) or k_cache.shape[4] != 128:
+        raise ValueError("KV cache must be [slots, 28, 8, max_len, 128]")
+    return k_cache.shape[0], k_cache.shape[3]
+
+
+def attention_prefill(q, k_cache, v_cache, seq_ids, L, pos0, layer, out=None):
+    """Causal GQA attention of len(seq_ids) sequences x L queries (rows of q,
+    BF16 [n_seqs*L, >=2048]) at positions pos0.. over the BF16 KV cache."""
+    import torch
+    n_slots, max_len = _cache_dims(k_cache)
+    n_seqs = seq_ids.numel()
+    if out is None:
+        out = torch.empty((n_seqs * L, 2048), dtype=torch.bfloat16, device=q.device)
+    check(lib().n550_attention_prefill(stream_ptr(), _dp(q), q.stride(0), _dp(k_cache), _dp(v_cache),
+                                       n_slots, max_len, layer, _dp(seq_ids), n_seqs, L, pos0,
+                                       _dp(out), out.stride(0)), "n550_attention_prefill")
+    return out
+
+
+def attention_decode(q, k_cache, v_cache, seq_ids, pos, layer, out=None, split=True):
+    """One query per sequence (rows of q, BF16) at position pos[s]; split=True
+    passes a split-KV workspace, split=False runs one CTA per (seq, KV head)."""
+    import torch
+    n_slots, max_len = _cache_dims(k_cache)
+    n_seqs = seq_ids.numel()
+    if out is None:
+        out = torch.empty((n_seqs, 2048), dtype=torch.bfloat16, device=q.device)
+    ws, nbytes = None, 0
+    if split:
+        nbytes = lib().n550_attention_decode_workspace(n_seqs, max_len)
+        ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q.device)
+    check(lib().n550_attention_decode(stream_ptr(), _dp(q), q.stride(0), _dp(k_cache), _dp(v_cache),
+                                      n_slots, max_len, layer, _dp(seq_ids), _dp(pos), n_seqs,
+                                      _dp(out), out.stride(0), _dp(ws) if ws is not None else None,
+                                      nbytes), "n550_attention_decode")
     return out
 
 

@@ -8,12 +8,10 @@
 // V -- one (seq, layer, kv_head) is a contiguous run of positions, the
 // kvh-major order of qwen3.h:62-76, so decode streams it with coalesced loads.
 //
-// prefill: flash attention (online softmax) with mma.sync m16n8k16 BF16 tensor
-//   core tiles; one CTA = 64 queries x the 2 query heads of one KV head, so
-//   every K/V tile is read once for both heads of the GQA pair.
-// decode:  one query per sequence; split-KV on CUDA cores: lanes own
-//   positions for q.k, then lanes own head dimensions for p.v; partial
-//   (max, sum, out) of each split are merged by a combine kernel.
+// This file is the decode side: one query per sequence, split-KV on CUDA
+// cores fed by a bulk-copy shared-memory ring; the partial (max, sum, out) of
+// each split are merged by a combine kernel. Prefill runs on the tcgen05
+// tensor cores (attn_prefill_tc.cu).
 #include "attention.h"
 #include "common.cuh"
 
@@ -28,219 +26,6 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ size_t kv_base(int seq, int layer, int kvh, int max_len) {
     return ((size_t)(seq * NL + layer) * NKV + kvh) * (size_t)max_len * HD;
-}
-
-// ---------------------------------------------------------------------------
-// prefill (tensor cores, mma.sync bf16)
-// ---------------------------------------------------------------------------
-constexpr int PF_Q = 64;          // queries per CTA (per head)
-constexpr int PF_KT = 64;         // keys per tile
-constexpr int PF_THREADS = 256;   // 8 warps: 2 heads x 4 x 16 query rows
-constexpr int PF_SMEM = (2 * PF_Q + 4 * PF_KT) * HD * 2;   // Q + 2xK + 2xV = 96 KB
-
-// Row r of a [rows][128] BF16 tile; 16-byte chunk c XOR-swizzled by r % 8 so
-// that ldmatrix reads of 8 rows at one chunk hit 8 different bank groups.
-__device__ __forceinline__ uint32_t swz(int r, int c) {
-    return (uint32_t)(r * HD + ((c ^ (r & 7)) << 3)) * 2u;
-}
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool valid) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
-                 ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
-                                        uint32_t &r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
-                                          uint32_t &r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
-}
-__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                         uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
-        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t pack2_bf16(float lo, float hi) {
-    return pack_bf16x2(lo, hi);
-}
-
-// Loads keys [k0, k0+64) of one (seq, layer, kvh) into a swizzled tile;
-// rows at or beyond kv_len are zero-filled.
-__device__ __forceinline__ void load_kv_tile(uint32_t dst, const uint16_t *base, int k0, int kv_len) {
-#pragma unroll
-    for (int i = 0; i < (PF_KT * 16) / PF_THREADS; i++) {
-        const int e = threadIdx.x + i * PF_THREADS;
-        const int r = e >> 4, c = e & 15;
-        const bool ok = (k0 + r) < kv_len;
-        const uint16_t *src = base + (size_t)(ok ? (k0 + r) : 0) * HD + c * 8;
-        cp_async16(dst + swz(r, c), src, ok);
-    }
-}
-
-__global__ void __launch_bounds__(PF_THREADS)
-attn_prefill_kernel(AttnPrefillArgs p) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const uint32_t sQ = smem_u32(smem);
-    const uint32_t sK0 = sQ + 2 * PF_Q * HD * 2;
-    const uint32_t sV0 = sK0 + 2 * PF_KT * HD * 2;
-    const int qb = blockIdx.x, kvh = blockIdx.y, s = blockIdx.z;
-    const int seq = p.seq_ids[s];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int hh = warp >> 2;                       // head within the GQA pair
-    const int wq = (warp & 3) * 16;                 // first query row of this warp
-    const int q_first = qb * PF_Q;
-    const int q_last = min(p.L, q_first + PF_Q) - 1;
-    const int kv_len = p.pos0 + p.L;
-    const uint16_t *kbase = p.kc + kv_base(seq, p.layer, kvh, p.max_len);
-    const uint16_t *vbase = p.vc + kv_base(seq, p.layer, kvh, p.max_len);
-
-    // Q tile: rows [head 0: 64 queries][head 1: 64 queries]
-#pragma unroll
-    for (int i = 0; i < (2 * PF_Q * 16) / PF_THREADS; i++) {
-        const int e = threadIdx.x + i * PF_THREADS;
-        const int r = e >> 4, c = e & 15;
-        const int qi = q_first + (r & 63);
-        const bool ok = qi < p.L;
-        const size_t row = (size_t)s * p.L + (ok ? qi : 0);
-        const uint16_t *src = p.q + row * p.ldq + (kvh * 2 + (r >> 6)) * HD + c * 8;
-        cp_async16(sQ + swz(r, c), src, ok);
-    }
-    cp_async_commit();
-
-    const int n_tiles = (p.pos0 + q_last + 1 + PF_KT - 1) / PF_KT;
-    load_kv_tile(sK0, kbase, 0, kv_len);
-    load_kv_tile(sV0, vbase, 0, kv_len);
-    cp_async_commit();
-
-    cp_async_wait<1>();
-    __syncthreads();
-    uint32_t qf[8][4];
-    {
-        const int r = hh * PF_Q + wq + (lane & 15);
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++)
-            ldsm_x4(sQ + swz(r, kk * 2 + (lane >> 4)), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
-    }
-
-    float o[16][4];
-#pragma unroll
-    for (int i = 0; i < 16; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-    float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
-    const int g = lane >> 2, t4 = lane & 3;
-    const int qpos0 = p.pos0 + q_first + wq + g;    // rows g and g + 8
-    const float sl2 = kScale * kLog2e;
-
-    for (int j = 0; j < n_tiles; j++) {
-        const int buf = j & 1;
-        if (j + 1 < n_tiles) {
-            load_kv_tile(sK0 + (buf ^ 1) * PF_KT * HD * 2, kbase, (j + 1) * PF_KT, kv_len);
-            load_kv_tile(sV0 + (buf ^ 1) * PF_KT * HD * 2, vbase, (j + 1) * PF_KT, kv_len);
-            cp_async_commit();
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
-        __syncthreads();
-        const uint32_t sK = sK0 + buf * PF_KT * HD * 2;
-        const uint32_t sV = sV0 + buf * PF_KT * HD * 2;
-
-        float sc[8][4];
-#pragma unroll
-        for (int nt = 0; nt < 8; nt++) {
-            sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-#pragma unroll
-            for (int k2 = 0; k2 < 4; k2++) {
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4(sK + swz(nt * 8 + (lane & 7), k2 * 4 + (lane >> 3)), b0, b1, b2, b3);
-                mma_bf16(sc[nt], qf[2 * k2], b0, b1);
-                mma_bf16(sc[nt], qf[2 * k2 + 1], b2, b3);
-            }
-        }
-        // scale (log2 domain) + causal mask
-        const int k0 = j * PF_KT;
-        const bool need_mask = (k0 + PF_KT - 1) > (p.pos0 + q_first + wq);
-        float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-        for (int nt = 0; nt < 8; nt++) {
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                float v = sc[nt][e] * sl2;
-                if (need_mask) {
-                    const int kp = k0 + nt * 8 + 2 * t4 + (e & 1);
-                    const int qp = qpos0 + (e >> 1) * 8;
-                    if (kp > qp) v = -INFINITY;
-                }
-                sc[nt][e] = v;
-                mx[e >> 1] = fmaxf(mx[e >> 1], v);
-            }
-        }
-        float corr[2];
-#pragma unroll
-        for (int r = 0; r < 2; r++) {
-            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xFFFFFFFFu, mx[r], 1));
-            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xFFFFFFFFu, mx[r], 2));
-            const float mn = fmaxf(m_r[r], mx[r]);
-            corr[r] = exp2f(m_r[r] - mn);
-            m_r[r] = mn;
-            l_r[r] *= corr[r];
-        }
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-            o[i][0] *= corr[0]; o[i][1] *= corr[0];
-            o[i][2] *= corr[1]; o[i][3] *= corr[1];
-        }
-        uint32_t pa[4][4];
-#pragma unroll
-        for (int nt = 0; nt < 8; nt++) {
-            const float p0 = exp2f(sc[nt][0] - m_r[0]), p1 = exp2f(sc[nt][1] - m_r[0]);
-            const float p2 = exp2f(sc[nt][2] - m_r[1]), p3 = exp2f(sc[nt][3] - m_r[1]);
-            l_r[0] += p0 + p1;
-            l_r[1] += p2 + p3;
-            const int kk = nt >> 1;
-            if ((nt & 1) == 0) { pa[kk][0] = pack2_bf16(p0, p1); pa[kk][1] = pack2_bf16(p2, p3); }
-            else               { pa[kk][2] = pack2_bf16(p0, p1); pa[kk][3] = pack2_bf16(p2, p3); }
-        }
-#pragma unroll
-        for (int np = 0; np < 8; np++) {
-#pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4_t(sV + swz(kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, np * 2 + (lane >> 4)),
-                          b0, b1, b2, b3);
-                mma_bf16(o[2 * np], pa[kk], b0, b1);
-                mma_bf16(o[2 * np + 1], pa[kk], b2, b3);
-            }
-        }
-        __syncthreads();
-    }
-
-#pragma unroll
-    for (int r = 0; r < 2; r++) {
-        l_r[r] += __shfl_xor_sync(0xFFFFFFFFu, l_r[r], 1);
-        l_r[r] += __shfl_xor_sync(0xFFFFFFFFu, l_r[r], 2);
-        l_r[r] = 1.0f / l_r[r];
-    }
-    const int head = kvh * 2 + hh;
-#pragma unroll
-    for (int r = 0; r < 2; r++) {
-        const int qi = q_first + wq + g + r * 8;
-        if (qi >= p.L) continue;
-        uint16_t *dst = p.out + ((size_t)s * p.L + qi) * p.ldo + head * HD + 2 * t4;
-#pragma unroll
-        for (int nt = 0; nt < 16; nt++)
-            *(uint32_t *)(dst + nt * 8) =
-                pack2_bf16(o[nt][2 * r] * l_r[r], o[nt][2 * r + 1] * l_r[r]);
-    }
 }
 
 // ---------------------------------------------------------------------------
@@ -442,24 +227,7 @@ __global__ void attn_combine_kernel(AttnDecodeArgs p) {
     p.out[(size_t)s * p.ldo + head * HD + d] = f32_to_bf16_rne(O / L);
 }
 
-bool g_pf_attr[64];
-
 }  // namespace
-
-int launch_attn_prefill(cudaStream_t st, const AttnPrefillArgs &a, int n_seqs) {
-    if (n_seqs <= 0 || a.L <= 0) return N550_OK;
-    int dev = 0;
-    N550_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev >= 0 && dev < 64 && !g_pf_attr[dev]) {
-        N550_CUDA_TRY(cudaFuncSetAttribute(attn_prefill_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM));
-        g_pf_attr[dev] = true;
-    }
-    dim3 grid((a.L + PF_Q - 1) / PF_Q, NKV, n_seqs);
-    attn_prefill_kernel<<<grid, PF_THREADS, PF_SMEM, st>>>(a);
-    N550_LAUNCH_CHECK();
-    return N550_OK;
-}
 
 int attn_decode_splits(int n_seqs, int max_kv_len, int max_splits) {
     // Enough CTAs to cover the SMs twice (2 resident per SM); splits are

@@ -14,6 +14,7 @@ struct AttnPrefillArgs {
     uint16_t *out;            // BF16, row stride ldo
     const int32_t *seq_ids;   // [n_seqs] KV slots
     int ldq, ldo, L, pos0, layer, max_len;
+    int kv_planes;            // slots x 28 layers x 8 KV heads in the cache
 };
 
 // Decode: one query per sequence at position pos[s] (attends 0..pos[s]).

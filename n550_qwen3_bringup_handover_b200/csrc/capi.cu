@@ -3,6 +3,7 @@
 #include <mutex>
 #include <string.h>
 
+#include "attention.h"
 #include "common.cuh"
 #include "gemm_tc.h"
 #include "ops.h"
@@ -446,6 +447,49 @@ int n550_synth_tokens(int32_t *out, size_t n, uint64_t seed, uint64_t stream, in
     const uint64_t key = synth_key(seed, stream);
     for (size_t i = 0; i < n; i++) out[i] = (int32_t)(synth_u64(key, i) % (uint64_t)vocab);
     return N550_OK;
+}
+
+int n550_attention_prefill(void *stream, const uint16_t *q, int ldq, const uint16_t *k_cache,
+                           const uint16_t *v_cache, int n_slots, int max_len, int layer,
+                           const int32_t *seq_ids, int n_seqs, int L, int pos0, uint16_t *out,
+                           int ldo) {
+    if (n_seqs < 0 || L < 0 || n_slots <= 0 || max_len <= 0) return N550_ERR_ARG;
+    AttnPrefillArgs a{};
+    a.q = q; a.kc = k_cache; a.vc = v_cache; a.out = out; a.seq_ids = seq_ids;
+    a.ldq = ldq; a.ldo = ldo; a.L = L; a.pos0 = pos0; a.layer = layer; a.max_len = max_len;
+    a.kv_planes = n_slots * 28 * 8;
+    return launch_attn_prefill((cudaStream_t)stream, a, n_seqs);
+}
+
+static const int kDecodeMaxSplits = 32;
+
+size_t n550_attention_decode_workspace(int n_seqs, int max_len) {
+    if (n_seqs <= 0 || max_len <= 0) return 0;
+    const int splits = attn_decode_splits(n_seqs, max_len, kDecodeMaxSplits);
+    return (size_t)n_seqs * 16 * splits * (2 + 128) * sizeof(float);
+}
+
+int n550_attention_decode(void *stream, const uint16_t *q, int ldq, const uint16_t *k_cache,
+                          const uint16_t *v_cache, int n_slots, int max_len, int layer,
+                          const int32_t *seq_ids, const int32_t *pos, int n_seqs, uint16_t *out,
+                          int ldo, void *workspace, size_t workspace_bytes) {
+    if (n_seqs == 0) return N550_OK;
+    if (n_seqs < 0 || n_slots <= 0 || max_len <= 0 || layer < 0 || layer >= 28 || !q || !k_cache ||
+        !v_cache || !seq_ids || !pos || !out || ldq < 16 * 128 || ldo < 16 * 128)
+        return N550_ERR_ARG;
+    AttnDecodeArgs a{};
+    a.q_bf16 = q; a.kc = k_cache; a.vc = v_cache; a.out = out; a.seq_ids = seq_ids; a.pos = pos;
+    a.ldq = ldq; a.ldo = ldo; a.layer = layer; a.max_len = max_len;
+    a.splits = 1;
+    const size_t need = n550_attention_decode_workspace(n_seqs, max_len);
+    if (workspace && workspace_bytes >= need && ((uintptr_t)workspace & 15) == 0) {
+        a.splits = attn_decode_splits(n_seqs, max_len, kDecodeMaxSplits);
+        const size_t slots = (size_t)n_seqs * 16 * a.splits;
+        a.part_o = (float *)workspace;
+        a.part_m = a.part_o + slots * 128;
+        a.part_l = a.part_m + slots;
+    }
+    return launch_attn_decode((cudaStream_t)stream, a, n_seqs);
 }
 
 int n550_device_status(void) {

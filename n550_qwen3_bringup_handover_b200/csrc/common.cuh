@@ -130,6 +130,16 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, uint64_
         : "memory");
 }
 
+// 3-D tiled TMA load (c0 innermost, same alignment rule as tma_load_2d).
+__device__ __forceinline__ void tma_load_3d(void *dst, const void *tmap, uint64_t *bar,
+                                            int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(tmap), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
 // Non-tensor bulk copy global -> shared (16-byte aligned addresses, size a
 // multiple of 16), completion counted on an mbarrier.
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
@@ -172,6 +182,18 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint
         : "memory");
 }
 
+// D[tmem] (+)= A[tmem] . B[smem]^T ; the A operand (M=128 rows = TMEM lanes,
+// K=16 BF16 packed two per 32-bit column, 8 columns) is read from TMEM.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive on an mbarrier once all previously issued tcgen05.mma of this thread
 // have completed.
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
@@ -199,6 +221,23 @@ __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Store counterpart of tmem_ld_32x32b_x32: thread t writes row (lane base + t).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]),
+          "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]),
+          "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]),
+          "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+          "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // UMMA shared-memory descriptor, K-major operand in the 128-byte swizzle
 // canonical layout: rows of 128 B, 8-row groups 1024 B apart (SBO = 1024),
 // descriptor version 1 (sm_100), layout type 2 = SWIZZLE_128B.
@@ -212,7 +251,22 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
     return d;
 }
 
-// Instruction descriptor, kind::f16: D FP32, A/B BF16, both K-major.
+// UMMA shared-memory descriptor, MN-major operand in the 128-byte swizzle
+// canonical layout: 64-element (128-byte) MN runs, 8 K rows 128 B apart form a
+// 1024-byte atom; atoms along K are 1024 B apart (SBO), atoms along MN are
+// `lbo` bytes apart (LBO).
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint32_t lbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// Instruction descriptor, kind::f16: D FP32, A/B BF16, both K-major
+// (bit 16 set = B MN-major).
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
     return (1u << 4)                       // D format F32
          | (1u << 7)                       // A format BF16

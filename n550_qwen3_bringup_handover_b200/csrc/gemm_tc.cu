@@ -23,6 +23,7 @@
 
 #include "common.cuh"
 #include "gemm_tc.h"
+#include "tmap.h"
 
 namespace n550 {
 namespace {
@@ -560,6 +561,41 @@ __global__ void splitk_reduce_kernel(const float *__restrict__ ws, int ksplit, i
 }
 
 }  // namespace
+
+namespace {
+int encode_sw128(CUtensorMap *tm, const void *ptr, cuuint32_t rank, const cuuint64_t *dims,
+                 const cuuint64_t *strides, int box_rows) {
+    int rc = get_encoder();
+    if (rc) return rc;
+    cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void *>(ptr), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? N550_OK : N550_ERR_UNSUPPORTED;
+}
+}  // namespace
+
+int tmap_bf16_sw128(CUtensorMap *tm, const void *ptr, uint64_t rows, uint64_t cols, uint64_t ld,
+                    int box_rows) {
+    if (!ptr || ((uintptr_t)ptr & 15) || (ld * 2) % 16 || cols < 64 || rows < 1 || box_rows < 1 ||
+        box_rows > 256)
+        return N550_ERR_ARG;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    return encode_sw128(tm, ptr, 2, dims, strides, box_rows);
+}
+
+int tmap_bf16_sw128_3d(CUtensorMap *tm, const void *ptr, uint64_t rows, uint64_t cols,
+                       uint64_t ld, int box_rows, uint64_t planes, uint64_t plane_ld) {
+    if (!ptr || ((uintptr_t)ptr & 15) || (ld * 2) % 16 || cols < 64 || rows < 1 || box_rows < 1 ||
+        box_rows > 256 || planes < 1 || (plane_ld * 2) % 16 || plane_ld < rows * ld)
+        return N550_ERR_ARG;
+    const cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)planes};
+    const cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)plane_ld * 2};
+    return encode_sw128(tm, ptr, 3, dims, strides, box_rows);
+}
 
 int launch_gemm_tc_qkv(cudaStream_t st, const uint16_t *a, int lda, const uint16_t *w,
                        const TcQkv &q, int M, int K, int max_ctas) {

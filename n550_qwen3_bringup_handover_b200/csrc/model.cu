@@ -592,6 +592,7 @@ int run_attention(n550_model *m, cudaStream_t st, int T, bool decode, const int3
         AttnPrefillArgs a{};
         a.q = m->qb; a.kc = m->kc; a.vc = m->vc; a.out = m->attn; a.seq_ids = seq_ids;
         a.ldq = QD; a.ldo = QD; a.L = Lc; a.pos0 = p0; a.layer = l; a.max_len = c.max_len;
+        a.kv_planes = c.max_seqs * NLAYER * NKVH;
         STEP(N550_PROF_ATTN, 1, launch_attn_prefill(st, a, Sc));
     }
     return N550_OK;
