@@ -31,17 +31,23 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;            // one 128-byte swizzle row of BF16
 constexpr int UMMA_K = 16;
-constexpr int THREADS = 192;
+// Epilogue warps: 4 (one per TMEM lane quarter); the two-head QKV tile gets
+// 8 (one head each), because its per-row RMSNorm + RoPE work is latency-bound.
+__host__ __device__ constexpr int tc_epi_warps(int BN, int EPI) {
+    return (EPI == TC_EPI_QKV_ROPE && BN == 256) ? 8 : 4;
+}
 
-template <int BN>
+template <int BN, int NEPI = 4>
 struct TcCfg {
     static constexpr int STAGES = (BN >= 256) ? 4 : (BN >= 128 ? 6 : 8);
+    static constexpr int THREADS = 64 + 32 * NEPI;
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int EPI_BYTES = 4 * 32 * 32 * 4;   // one 32x32-word tile per epilogue warp
+    static constexpr int EPI_BYTES = NEPI * 32 * 32 * 4;   // one 32x32-word tile per epilogue warp
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
+    static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 };
 
 // silu(g) * u (ops_scalar.c:46-51) with the fast exponential and divide: the
@@ -118,15 +124,18 @@ __device__ __forceinline__ void flush_f32(const uint32_t *stg, int lane, float *
 
 // Rows of a BF16 destination; rowptr(r) gives the address of column `n` of
 // tile row r (or nullptr to skip the row); 8 columns per lane.
+// A 32 x 32-word staging tile holds 32 rows x 32 BF16 in one half of each
+// 128-byte row; alt = 16 selects the other half, a second tile in the same
+// words (b16_word(r, c) ^ 16 keeps the bank spread of b16_word).
 template <class RowPtr>
 __device__ __forceinline__ void flush_bf16(const uint32_t *stg, int lane, RowPtr rowptr, int n,
-                                           int N, bool vec_ok) {
+                                           int N, bool vec_ok, int alt = 0) {
     const int c = lane & 3;
     const int col = n + 8 * c;
 #pragma unroll
     for (int it = 0; it < 4; it++) {
         const int r = it * 8 + (lane >> 2);
-        const uint4 q = *(const uint4 *)(stg + b16_word(r, c));
+        const uint4 q = *(const uint4 *)(stg + (b16_word(r, c) ^ alt));
         uint16_t *dst = rowptr(r);
         if (!dst) continue;
         dst += 8 * c;
@@ -149,46 +158,83 @@ __device__ __forceinline__ void load_chunk(uint32_t taddr, float (&v)[32]) {
     for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
 }
 
+// 16 values of one row (lane) as BF16 into 16-byte chunks c16 * 2, c16 * 2 + 1
+// of a 32-column staging tile (alt selects the tile, as in flush_bf16).
+__device__ __forceinline__ void stage_bf16_16(uint32_t *stg, int lane, int c16, int alt,
+                                              const float (&v)[16]) {
+#pragma unroll
+    for (int k = 0; k < 2; k++)
+        *(uint4 *)(stg + (b16_word(lane, c16 * 2 + k) ^ alt)) =
+            make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]), pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
+                       pack_bf16x2(v[8 * k + 4], v[8 * k + 5]), pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
+}
+
+__device__ __forceinline__ void load_chunk16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    tmem_ld_32x32b_x16(taddr, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; j++) v[j] = __uint_as_float(r[j]);
+}
+
 // Fused QKV epilogue (qwen3.c:477-511). A 128-column tile is one head of the
 // [q 16 | k 8 | v 8] x 128 qkv row. q and k heads: RMSNorm over the head
-// (qk_norm, qwen3.c:287-292, sum of squares in the order and rounding of
-// ops_scalar.c:12), RoPE pairs (i, i + 64) from the (cos, sin) table
-// (ops_scalar.c:21-35); q goes to the query buffer, k to the KV cache; v heads
-// go to the cache unchanged. The accumulator is read from TMEM twice (sum of
-// squares, then values) so no thread holds more than 64 of them.
+// (qk_norm, qwen3.c:287-292; four partial sums of squares), RoPE pairs
+// (i, i + 64) from the (cos, sin) table (ops_scalar.c:21-35); q goes to the
+// BF16 query buffer, k to the KV cache; v heads go to the cache unchanged. The
+// accumulator is read from TMEM twice (sum of squares, then 16 rotation pairs
+// at a time) to keep register use low. Lane r owns tile row r: it reads that
+// row's token position / slot once, and the store loops take other rows'
+// destination addresses from their owners by shuffle.
 __device__ __forceinline__ void epilogue_qkv(const TcQkv &p, uint32_t *stg, int lane, uint32_t taddr,
                                              int row0, int M, int head, uint64_t *tempty_bar) {
     const int m = row0 + lane;
-    const int pos = p.tok_pos[m < M ? m : M - 1];
+    const bool row_ok = m < M;
+    const int mc = row_ok ? m : M - 1;
+    const int pos = p.tok_pos[mc];
     const bool normed = head < 24;
     const uint16_t *w = head < 16 ? p.q_norm : p.k_norm;
+    uint16_t *dst_row;                     // column 0 of this head in the destination row
+    if (head < 16) {
+        dst_row = p.q_bf16 + (size_t)mc * p.ldq + head * 128;
+    } else {
+        const int kvh = (head - 16) & 7;
+        uint16_t *cache = head < 24 ? p.kc : p.vc;
+        const size_t slot = ((size_t)p.tok_seq[mc] * 28 + p.layer) * 8 + kvh;
+        dst_row = cache + (slot * p.max_len + pos) * 128;
+    }
+    if (!row_ok) dst_row = nullptr;
     float scale = 1.f;
     if (normed) {
-        float ss = 0.f;
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll 1
-        for (int c = 0; c < 4; c++) {
-            float v[32];
-            load_chunk(taddr + 32 * c, v);
+        for (int c = 0; c < 8; c++) {
+            float v[16];
+            load_chunk16(taddr + 16 * c, v);
 #pragma unroll
-            for (int j = 0; j < 32; j++) ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
+            for (int j = 0; j < 16; j += 4) {
+                s0 = fmaf(v[j], v[j], s0);
+                s1 = fmaf(v[j + 1], v[j + 1], s1);
+                s2 = fmaf(v[j + 2], v[j + 2], s2);
+                s3 = fmaf(v[j + 3], v[j + 3], s3);
+            }
         }
-        scale = 1.0f / sqrtf(ss / 128.0f + p.eps);
+        scale = 1.0f / sqrtf(((s0 + s1) + (s2 + s3)) / 128.0f + p.eps);
     }
-    const int kvh = (head - 16) & 7;
-    uint16_t *cache = head < 24 ? p.kc : p.vc;
 #pragma unroll 1
-    for (int c = 0; c < 2; c++) {
-        float a[32], b[32];
-        load_chunk(taddr + 32 * c, a);
-        load_chunk(taddr + 64 + 32 * c, b);
-        if (c == 1 && tempty_bar) { tc_fence_before(); mbar_arrive(tempty_bar); }
+    for (int c = 0; c < 4; c++) {
+        // rotation pairs (16c + j, 64 + 16c + j), j < 16
+        float a[16], b[16];
+        load_chunk16(taddr + 16 * c, a);
+        load_chunk16(taddr + 64 + 16 * c, b);
+        if (c == 3 && tempty_bar) { tc_fence_before(); mbar_arrive(tempty_bar); }
         if (normed) {
             // 16-byte loads: 2 (cos, sin) pairs, 8 norm weights per load.
-            const float4 *cs4 = (const float4 *)(p.rope + (size_t)pos * 64 + 32 * c);
-            const uint4 *w_lo = (const uint4 *)(w + 32 * c);
-            const uint4 *w_hi = (const uint4 *)(w + 64 + 32 * c);
+            const float4 *cs4 = (const float4 *)(p.rope + (size_t)pos * 64 + 16 * c);
+            const uint4 *w_lo = (const uint4 *)(w + 16 * c);
+            const uint4 *w_hi = (const uint4 *)(w + 64 + 16 * c);
 #pragma unroll
-            for (int j8 = 0; j8 < 4; j8++) {
+            for (int j8 = 0; j8 < 2; j8++) {
                 const uint4 wl = __ldg(w_lo + j8), wh = __ldg(w_hi + j8);
                 const uint32_t wlw[4] = {wl.x, wl.y, wl.z, wl.w}, whw[4] = {wh.x, wh.y, wh.z, wh.w};
 #pragma unroll
@@ -208,34 +254,18 @@ __device__ __forceinline__ void epilogue_qkv(const TcQkv &p, uint32_t *stg, int 
                 }
             }
         }
+        // dims 16c.. go to the first staging tile, dims 64 + 16c.. to the second
+        stage_bf16_16(stg, lane, c & 1, 0, a);
+        stage_bf16_16(stg, lane, c & 1, 16, b);
+        if (c & 1) {
+            __syncwarp();
 #pragma unroll
-        for (int half = 0; half < 2; half++) {
-            const int d0 = 32 * c + 64 * half;
-            if (head < 16 && p.q_f32) {
-                uint32_t bits[32];
-#pragma unroll
-                for (int j = 0; j < 32; j++) bits[j] = __float_as_uint(half ? b[j] : a[j]);
-                stage_f32(stg, lane, bits);
-                __syncwarp();
-                const int n = head * 128 + d0;
-                flush_f32<false>(stg, lane, p.q_f32, p.ldq, row0, M, n, n + 32, true);
-            } else {
-                if (half) stage_bf16(stg, lane, b);
-                else stage_bf16(stg, lane, a);
-                __syncwarp();
-                if (head < 16) {
-                    flush_bf16(stg, lane, [&](int r) -> uint16_t * {
-                        const int mr = row0 + r;
-                        return mr < M ? p.q_bf16 + (size_t)mr * p.ldq + head * 128 + d0 : nullptr;
-                    }, 0, 32, true);
-                } else {
-                    flush_bf16(stg, lane, [&](int r) -> uint16_t * {
-                        const int mr = row0 + r;
-                        if (mr >= M) return nullptr;
-                        const size_t slot = ((size_t)p.tok_seq[mr] * 28 + p.layer) * 8 + kvh;
-                        return cache + (slot * p.max_len + p.tok_pos[mr]) * 128 + d0;
-                    }, 0, 32, true);
-                }
+            for (int half = 0; half < 2; half++) {
+                const int d0 = 32 * (c >> 1) + 64 * half;
+                flush_bf16(stg, lane, [&](int r) -> uint16_t * {
+                    uint16_t *d = (uint16_t *)__shfl_sync(0xFFFFFFFFu, (unsigned long long)dst_row, r);
+                    return d ? d + d0 : nullptr;
+                }, 0, 32, true, half ? 16 : 0);
             }
             __syncwarp();
         }
@@ -243,13 +273,14 @@ __device__ __forceinline__ void epilogue_qkv(const TcQkv &p, uint32_t *stg, int 
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(TcCfg<BN, tc_epi_warps(BN, EPI)>::THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmB2,
                const TcEpilogue ep, int M, int N, int K, int m_fast, int ksplit,
                int kt_per, float *ws, bool partials) {
-    using Cfg = TcCfg<BN>;
+    constexpr int NEPI = tc_epi_warps(BN, EPI);
+    using Cfg = TcCfg<BN, NEPI>;
     constexpr int STAGES = Cfg::STAGES;
     constexpr bool SILU = (EPI == TC_EPI_SILU_BF16);
     // Output columns per tile: SILU tiles hold BN/2 gate + BN/2 up columns.
@@ -278,7 +309,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        for (int b = 0; b < 2; b++) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 128); }
+        for (int b = 0; b < 2; b++) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 32 * NEPI); }
         mbar_init(done, 1);
         fence_mbar_init();
     }
@@ -397,10 +428,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     __syncwarp();
                 }
             } else if (EPI == TC_EPI_QKV_ROPE) {
+                if (NEPI == 8) {
+                    // warps 2-5: first head of the tile, warps 6-9: second
+                    const int hh = (warp - 2) >> 2;
+                    epilogue_qkv(ep.qkv, stg, lane, taddr + hh * 128, row0, M, nb * 2 + hh, &tempty[ab]);
+                } else {
 #pragma unroll 1
-                for (int hh = 0; hh < BN / 128; hh++)
-                    epilogue_qkv(ep.qkv, stg, lane, taddr + hh * 128, row0, M, nb * (BN / 128) + hh,
-                                 hh + 1 == BN / 128 ? &tempty[ab] : nullptr);
+                    for (int hh = 0; hh < BN / 128; hh++)
+                        epilogue_qkv(ep.qkv, stg, lane, taddr + hh * 128, row0, M,
+                                     nb * (BN / 128) + hh, hh + 1 == BN / 128 ? &tempty[ab] : nullptr);
+                }
             } else if (SILU) {
 #pragma unroll 1
                 for (int cch = 0; cch < OUT_N; cch += 32) {
@@ -508,7 +545,7 @@ int launch_impl(cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tb,
                 const CUtensorMap &tb2, const TcEpilogue &ep, int M, int N, int K,
                 int max_ctas, int ksplit = 1, int kt_per = 1 << 30, float *ws = nullptr,
                 bool partials = false) {
-    using Cfg = TcCfg<BN>;
+    using Cfg = TcCfg<BN, tc_epi_warps(BN, EPI)>;
     static bool attr_done[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -528,7 +565,7 @@ int launch_impl(cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tb,
     // fetched from HBM once and reused from L2 by the CTAs of all M tiles;
     // otherwise walk N fastest so that A rows are shared.
     const int m_fast = (long long)N * (EPI == TC_EPI_SILU_BF16 ? 2 : 1) > (long long)M;
-    gemm_tc_kernel<BN, EPI><<<grid, THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tb2, ep, M, N, K, m_fast,
+    gemm_tc_kernel<BN, EPI><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tb2, ep, M, N, K, m_fast,
                                                                      ksplit, kt_per, ws, partials);
     N550_LAUNCH_CHECK();
     return N550_OK;
@@ -601,7 +638,7 @@ int launch_gemm_tc_qkv(cudaStream_t st, const uint16_t *a, int lda, const uint16
                        const TcQkv &q, int M, int K, int max_ctas) {
     if (M <= 0) return N550_OK;
     if (!tc_shape_ok(a, lda, w, K, K)) return N550_ERR_UNSUPPORTED;
-    if ((!q.q_bf16 && !q.q_f32) || !q.kc || !q.vc || !q.tok_pos || !q.tok_seq || !q.rope ||
+    if (!q.q_bf16 || !q.kc || !q.vc || !q.tok_pos || !q.tok_seq || !q.rope ||
         (q.ldq % 8))
         return N550_ERR_ARG;
     int rc = get_encoder();

@@ -18,8 +18,7 @@ enum {
 // Operands of the fused QKV epilogue (qwen3.c:477-511): a 128-column tile is
 // one head of the [q 16 | k 8 | v 8] x 128 qkv row.
 struct TcQkv {
-    uint16_t *q_bf16;          // [M, ldq] BF16 queries, or NULL
-    float *q_f32;              // [M, ldq] FP32 queries, or NULL
+    uint16_t *q_bf16;          // [M, ldq] BF16 queries
     int ldq;
     uint16_t *kc, *vc;         // KV cache [seq][layer][kv_head][pos][128]
     int layer, max_len;

@@ -297,6 +297,43 @@ resid_norm_rows_kernel(float *x, const float *__restrict__ ws, int ks, size_t sl
     }
 }
 
+// out[t] = bf16(rmsnorm(x[t]) * w) for rows of 1024 (qwen3.c:471/527, the
+// normalised GEMM input): one warp per row, eight 16-byte loads per lane held
+// in registers, warp-shuffle sum of squares, 8-byte stores.
+__global__ void __launch_bounds__(256)
+norm_rows_bf16_kernel(uint16_t *__restrict__ out, const float *__restrict__ x,
+                      const uint16_t *__restrict__ w, int T) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= T) return;
+    const float4 *xr = (const float4 *)(x + (size_t)row * H);
+    float4 v[8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        v[i] = __ldg(xr + lane + 32 * i);
+        ss = fmaf(v[i].x, v[i].x, ss);
+        ss = fmaf(v[i].y, v[i].y, ss);
+        ss = fmaf(v[i].z, v[i].z, ss);
+        ss = fmaf(v[i].w, v[i].w, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    const float sc = 1.0f / sqrtf(ss / (float)H + EPS);
+    const uint2 *wr = (const uint2 *)w;
+    uint2 *orow = (uint2 *)(out + (size_t)row * H);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const uint2 wv = __ldg(wr + lane + 32 * i);
+        uint2 o;
+        o.x = pack_bf16x2(v[i].x * sc * __uint_as_float(wv.x << 16),
+                          v[i].y * sc * __uint_as_float(wv.x & 0xFFFF0000u));
+        o.y = pack_bf16x2(v[i].z * sc * __uint_as_float(wv.y << 16),
+                          v[i].w * sc * __uint_as_float(wv.y & 0xFFFF0000u));
+        orow[lane + 32 * i] = o;
+    }
+}
+
 // Final RMSNorm of the last token of each sequence (qwen3.c:547-573 only
 // needs row NT-1): xl[i] = rmsnorm(x[i*Lc + Lc - 1]) in BF16.
 __global__ void __launch_bounds__(256)
@@ -561,6 +598,13 @@ int partials(n550_model *m, cudaStream_t st, const uint16_t *a, int lda, const u
                                    m->ws_bytes, ks);
 }
 
+int launch_norm_rows(cudaStream_t st, uint16_t *out, const float *x, const uint16_t *w, int T) {
+    if (T <= 0) return N550_OK;
+    norm_rows_bf16_kernel<<<(T + 7) / 8, 256, 0, st>>>(out, x, w, T);
+    N550_LAUNCH_CHECK();
+    return N550_OK;
+}
+
 int launch_final_norm(cudaStream_t st, uint16_t *xl, const float *x, const uint16_t *w, int Sc, int Lc) {
     final_norm_kernel<<<Sc, 256, 0, st>>>(xl, x, w, Lc);
     N550_LAUNCH_CHECK();
@@ -576,12 +620,13 @@ int launch_final_norm(cudaStream_t st, uint16_t *xl, const float *x, const uint1
     } while (0)
 
 int run_attention(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t *seq_ids,
-                  const int32_t *pos, int Sc, int Lc, int p0, int l) {
+                  const int32_t *pos, int Sc, int Lc, int p0, int l, bool q_in_bf16 = false) {
     const n550_model_config &c = m->cfg;
     int rc = N550_OK;
     if (decode) {
         AttnDecodeArgs a{};
-        a.q_f32 = m->qf;
+        a.q_f32 = q_in_bf16 ? nullptr : m->qf;
+        a.q_bf16 = m->qb;
         a.kc = m->kc; a.vc = m->vc; a.out = m->attn;
         a.seq_ids = seq_ids; a.pos = pos;
         a.ldq = QD; a.ldo = QD; a.layer = l; a.max_len = c.max_len;
@@ -608,7 +653,7 @@ int run_layers_split(n550_model *m, cudaStream_t st, int T, bool decode, const i
                      const int32_t *pos, int Sc, int Lc, int p0, bool *xl_ready) {
     int rc = N550_OK, ks = 0, kt;
     const int gu_kernels = tc_splitk_plan(T, INTER, H, TC_EPI_SILU_BF16, 64, &kt) > 1 ? 2 : 1;
-    STEP(N550_PROF_RMSNORM, 1, launch_rmsnorm(st, m->xb, N550_BF16, m->x, W(m, 0, 0), T, H, EPS));
+    STEP(N550_PROF_RMSNORM, 1, launch_norm_rows(st, m->xb, m->x, W(m, 0, 0), T));
     for (int l = 0; l < NLAYER; l++) {
         STEP(N550_PROF_GEMM_QKV, 1, partials(m, st, m->xb, H, m->wqkv[l], T, QKVD, H, &ks));
         STEP(N550_PROF_QKNORM_ROPE, 1, launch_qknorm_rope_kv(m, st, T, l, decode, m->ws, ks));
@@ -639,12 +684,11 @@ int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t
     const int gu_kernels = exact || T <= 8 ? 3 : 1;
     const int res_kernels = exact ? 2 : 1;
     for (int l = 0; l < NLAYER; l++) {
-        STEP(N550_PROF_RMSNORM, 1, launch_rmsnorm(st, m->xb, N550_BF16, m->x, W(m, l, 0), T, H, EPS));
+        STEP(N550_PROF_RMSNORM, 1, launch_norm_rows(st, m->xb, m->x, W(m, l, 0), T));
         if (!exact && T >= 1024) {
             // One tcgen05 GEMM with QK-norm, RoPE and the K/V cache write in its epilogue.
             TcQkv q{};
-            q.q_bf16 = decode ? nullptr : m->qb;
-            q.q_f32 = decode ? m->qf : nullptr;
+            q.q_bf16 = m->qb;
             q.ldq = QD;
             q.kc = m->kc; q.vc = m->vc; q.layer = l; q.max_len = c.max_len;
             q.tok_pos = m->tok_pos; q.tok_seq = m->tok_seq;
@@ -656,10 +700,12 @@ int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t
                  mgemm(m, st, TC_EPI_F32, m->xb, H, m->wqkv[l], nullptr, m->qkv, QKVD, T, QKVD, H));
             STEP(N550_PROF_QKNORM_ROPE, 1, launch_qknorm_rope_kv(m, st, T, l, decode));
         }
-        if ((rc = run_attention(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, l))) return rc;
+        // the fused QKV epilogue leaves BF16 queries (decode attention reads either)
+        if ((rc = run_attention(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, l, !exact && T >= 1024)))
+            return rc;
         STEP(N550_PROF_GEMM_O, res_kernels,
              mgemm(m, st, TC_EPI_RESID_F32, m->attn, QD, W(m, l, 6), nullptr, m->x, H, T, H, QD));
-        STEP(N550_PROF_RMSNORM, 1, launch_rmsnorm(st, m->xb, N550_BF16, m->x, W(m, l, 7), T, H, EPS));
+        STEP(N550_PROF_RMSNORM, 1, launch_norm_rows(st, m->xb, m->x, W(m, l, 7), T));
         STEP(N550_PROF_GEMM_GATEUP, gu_kernels,
              mgemm(m, st, TC_EPI_SILU_BF16, m->xb, H, W(m, l, 8), W(m, l, 9), m->h, INTER, T, INTER, H));
         STEP(N550_PROF_GEMM_DOWN, res_kernels,
