@@ -20,6 +20,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <string.h>
 
 #include "common.cuh"
 #include "gemm_tc.h"
@@ -37,7 +38,11 @@ __host__ __device__ constexpr int tc_epi_warps(int BN, int EPI) {
     return (EPI == TC_EPI_QKV_ROPE && BN == 256) ? 8 : 4;
 }
 
-template <int BN, int NEPI = 4>
+// Staging tiles per epilogue warp: the residual epilogue double-buffers the
+// tiles its TMA reduce-adds read.
+__host__ __device__ constexpr int tc_stg_tiles(int EPI) { return EPI == TC_EPI_RESID_F32 ? 2 : 1; }
+
+template <int BN, int NEPI = 4, int STG = 1>
 struct TcCfg {
     static constexpr int STAGES = (BN >= 256) ? 4 : (BN >= 128 ? 6 : 8);
     static constexpr int THREADS = 64 + 32 * NEPI;
@@ -45,7 +50,7 @@ struct TcCfg {
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int EPI_BYTES = NEPI * 32 * 32 * 4;   // one 32x32-word tile per epilogue warp
+    static constexpr int EPI_BYTES = NEPI * STG * 32 * 32 * 4;   // 32x32-word tiles per epilogue warp
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
     static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 };
@@ -277,10 +282,12 @@ __global__ void __launch_bounds__(TcCfg<BN, tc_epi_warps(BN, EPI)>::THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmB2,
+               const __grid_constant__ CUtensorMap tmC,
                const TcEpilogue ep, int M, int N, int K, int m_fast, int ksplit,
                int kt_per, float *ws, bool partials) {
     constexpr int NEPI = tc_epi_warps(BN, EPI);
-    using Cfg = TcCfg<BN, NEPI>;
+    constexpr int STG = tc_stg_tiles(EPI);
+    using Cfg = TcCfg<BN, NEPI, STG>;
     constexpr int STAGES = Cfg::STAGES;
     constexpr bool SILU = (EPI == TC_EPI_SILU_BF16);
     // Output columns per tile: SILU tiles hold BN/2 gate + BN/2 up columns.
@@ -397,7 +404,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
         const int q = warp & 3;                 // TMEM lane quarter of this warp
-        uint32_t *stg = (uint32_t *)(base + STAGES * Cfg::STAGE_BYTES) + (warp - 2) * 32 * 32;
+        uint32_t *stg = (uint32_t *)(base + STAGES * Cfg::STAGE_BYTES) + (warp - 2) * STG * 32 * 32;
+        int chunks = 0;                          // residual chunks handed to the TMA
         int ab = 0;
         uint32_t aphase = 0;
         for (int u = blockIdx.x; u < total; u += gridDim.x) {
@@ -458,6 +466,30 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     }, n, N, ep.vec_ok);
                     __syncwarp();
                 }
+            } else if (EPI == TC_EPI_RESID_F32 && ep.tma_resid) {
+                // x += acc: each 32 x 32 chunk is staged in the 128-byte
+                // swizzled layout of the FP32 tensor map and reduce-added into
+                // x by the TMA (L2 does the read-modify-write, one add per
+                // element), two staging tiles alternating.
+#pragma unroll 1
+                for (int cch = 0; cch < BN; cch += 32) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(taddr + cch, r);
+                    tmem_ld_wait();
+                    if (cch + 32 == BN) { tc_fence_before(); mbar_arrive(&tempty[ab]); }
+                    const int n = nb * BN + cch;
+                    uint32_t *sb = stg + (chunks & 1) * 32 * 32;
+                    if (lane == 0) bulk_wait_group_read<1>();   // the reduce that last read sb
+                    __syncwarp();
+                    stage_f32(sb, lane, r);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0 && n < N && row0 < M) {
+                        tma_reduce_add_2d(&tmC, sb, n, row0);
+                        bulk_commit_group();
+                    }
+                    chunks++;
+                }
             } else {
 #pragma unroll 1
                 for (int cch = 0; cch < BN; cch += 32) {
@@ -488,6 +520,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             }
             if (++ab == 2) { ab = 0; aphase ^= 1; }
         }
+        // Reduce-adds still in flight read this CTA's shared memory and must
+        // land before the kernel completes.
+        if (EPI == TC_EPI_RESID_F32 && lane == 0) bulk_wait_group<0>();
     }
 
     tc_fence_before();
@@ -527,6 +562,20 @@ int make_tmap(CUtensorMap *tm, const void *ptr, int rows, int K, int ld, int box
     return r == CUDA_SUCCESS ? N550_OK : N550_ERR_UNSUPPORTED;
 }
 
+// FP32 output [rows, cols] (row stride ld elements) for TMA stores/reduces of
+// 32 x 32 staging tiles (128-byte rows, 128-byte swizzle).
+int make_tmap_f32_out(CUtensorMap *tm, void *ptr, int rows, int cols, int ld) {
+    if (get_encoder()) return N550_ERR_CUDA;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ptr, dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? N550_OK : N550_ERR_UNSUPPORTED;
+}
+
 int g_num_sms[64];
 
 int num_sms() {
@@ -544,8 +593,11 @@ template <int BN, int EPI>
 int launch_impl(cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tb,
                 const CUtensorMap &tb2, const TcEpilogue &ep, int M, int N, int K,
                 int max_ctas, int ksplit = 1, int kt_per = 1 << 30, float *ws = nullptr,
-                bool partials = false) {
-    using Cfg = TcCfg<BN, tc_epi_warps(BN, EPI)>;
+                bool partials = false, const CUtensorMap *tc = nullptr) {
+    using Cfg = TcCfg<BN, tc_epi_warps(BN, EPI), tc_stg_tiles(EPI)>;
+    CUtensorMap tmc;
+    if (tc) tmc = *tc;
+    else memset(&tmc, 0, sizeof tmc);
     static bool attr_done[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -565,7 +617,7 @@ int launch_impl(cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tb,
     // fetched from HBM once and reused from L2 by the CTAs of all M tiles;
     // otherwise walk N fastest so that A rows are shared.
     const int m_fast = (long long)N * (EPI == TC_EPI_SILU_BF16 ? 2 : 1) > (long long)M;
-    gemm_tc_kernel<BN, EPI><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tb2, ep, M, N, K, m_fast,
+    gemm_tc_kernel<BN, EPI><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tb2, tmc, ep, M, N, K, m_fast,
                                                                      ksplit, kt_per, ws, partials);
     N550_LAUNCH_CHECK();
     return N550_OK;
@@ -768,13 +820,20 @@ int launch_gemm_tc(cudaStream_t st, int epi, int bn, const uint16_t *a, int lda,
     } else {
         tb2 = tb;
     }
-    TcEpilogue ep;
+    TcEpilogue ep{};
     ep.c = c;
     ep.ldc = ldc;
     const int esz = (epi == TC_EPI_BF16 || epi == TC_EPI_SILU_BF16) ? 2 : 4;
     ep.vec_ok = ((((uintptr_t)c) & 15) == 0) && ((ldc * esz) % 16 == 0);
+    CUtensorMap tc;
+    const CUtensorMap *tcp = nullptr;
+    if (epi == TC_EPI_RESID_F32 && ep.vec_ok && make_tmap_f32_out(&tc, c, M, N, ldc) == N550_OK) {
+        ep.tma_resid = 1;
+        tcp = &tc;
+    }
 #define N550_TC_CASE(BNV, EV) \
-    if (bn == BNV && epi == EV) return launch_impl<BNV, EV>(st, ta, tb, tb2, ep, M, N, K, max_ctas);
+    if (bn == BNV && epi == EV)   \
+        return launch_impl<BNV, EV>(st, ta, tb, tb2, ep, M, N, K, max_ctas, 1, 1 << 30, nullptr, false, tcp);
     N550_TC_CASE(128, TC_EPI_F32)
     N550_TC_CASE(128, TC_EPI_BF16)
     N550_TC_CASE(128, TC_EPI_RESID_F32)

@@ -32,6 +32,7 @@ struct TcEpilogue {
     void *c;
     int ldc;
     int vec_ok;            // 16-byte vector stores allowed
+    int tma_resid;         // TC_EPI_RESID_F32 through TMA reduce-adds (C map given)
     TcQkv qkv;
 };
 

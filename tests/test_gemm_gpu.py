@@ -211,6 +211,25 @@ def test_fused_residual_gemm(cuda, M, K, N):
     assert rel_err(x.cpu().numpy(), ref) <= FAST_TOL
 
 
+@pytest.mark.parametrize("M,K,N,ld", [(2048, 1024, 1024, 1024), (1100, 2048, 1000, 1000),
+                                      (1500, 3072, 1024, 1040)])
+def test_residual_gemm_tma_add_is_exact(cuda, M, K, N, ld):
+    """Large-M residual GEMMs reduce-add their tiles into x through the TMA:
+    the result must be bit-identical to the FP32-output GEMM (same tiles, same
+    accumulation order) added to x in FP32, and columns past N of a strided x
+    must stay untouched."""
+    import torch
+    A = to_dev_bf16(oracle.synth_normal_bf16((M, K), 37, 0x41, 1.0), cuda)
+    B = to_dev_bf16(oracle.synth_normal_bf16((N, K), 37, 0x42, 0.02), cuda)
+    x0 = torch.from_numpy(oracle.synth_normal_f32((M, ld), 37, 0x58, 1.0)).to(cuda)
+    c = n5.gemm(A, B, mode=n5.MODE_FAST)
+    x = x0.clone()
+    n5.gemm_residual(A, B, x[:, :N])
+    torch.cuda.synchronize()
+    assert torch.equal(x[:, :N], x0[:, :N] + c)
+    assert torch.equal(x[:, N:], x0[:, N:])
+
+
 @pytest.mark.parametrize("M,K,N", [(300, 1024, 3072), (128, 1024, 200), (17, 1024, 64)])
 def test_fused_swiglu_gemm(cuda, M, K, N):
     """h = silu(A . Wg^T) * (A . Wu^T) in BF16 (gate/up qwen3_gemm then qwen3_op_silu_mul)."""
