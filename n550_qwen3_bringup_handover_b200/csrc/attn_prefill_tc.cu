@@ -4,22 +4,26 @@
 // head h/2, qwen3.c:299), s_t = (q . k_t) * 0.08838834764831845 for
 // t = 0..p, softmax over t, out = sum_t softmax_t * v_t.
 //
-// One CTA = 128 consecutive queries of one sequence x the two query heads of
-// one KV head (the GQA pair), so each 128-key K/V block is read once for both
-// heads.
-//   warp 0     TMA producer: Q of both heads once, then K and V blocks into a
-//              2-stage ring (128-byte swizzle; V is the MN-major B operand).
-//   warp 1     allocates TMEM (512 columns); one thread issues the MMAs:
-//              S_h = Q_h K^T (A and B in shared memory) and O_h += P_h V
-//              (A = P read from TMEM, B = V from shared memory).
-//   warps 2-5  softmax and output of head 0, warps 6-9 of head 1; a thread
-//              owns one query row. Scores are taken in the log2 domain; P is
-//              written back into TMEM over its S as packed BF16. O is rescaled
-//              in TMEM only when a row's running maximum grows by more than 8
-//              (a factor 256): the exponentials use the stale maximum
-//              otherwise, which leaves O / l unchanged.
-// MMA issue order S0(0) S1(0) | PV0(j) S0(j+1) PV1(j) S1(j+1) | ... keeps the
-// tensor core on one head while the other head's softmax runs.
+// Persistent kernel: one CTA per SM walks work items (longest first); an item
+// is 128 consecutive queries of one sequence x the two query heads of one KV
+// head (the GQA pair), so every 128-key K/V block is read once for both heads.
+//   warp 0      TMA producer: Q of both heads per item, then K and V blocks
+//               into a 2-stage ring (128-byte swizzle; V is consumed as the
+//               MN-major B operand).
+//   warp 1      allocates TMEM (512 columns); one thread issues the MMAs:
+//               S_h = Q_h K^T (A and B in shared memory) and O_h += P_h V
+//               (A = P read from TMEM, B = V from shared memory), in the order
+//               S0 S1 | PV0(j) S0(j+1) PV1(j) S1(j+1) | ... so the tensor core
+//               works on one head while the other head's softmax runs.
+//   warps 2-17  softmax and output: 8 warps per head, a pair of warps per
+//               32-row TMEM lane quarter, each warp owning 64 of the 128 key
+//               columns of its rows (and 64 of the 128 output dimensions); the
+//               pair exchanges row maxima and sums through shared memory
+//               behind a 64-thread named barrier. Scores are in the log2
+//               domain; P is written back into TMEM over its S as packed BF16;
+//               O is rescaled in TMEM only when a row's running maximum grows
+//               by more than 8 (a factor 256), otherwise the stale maximum is
+//               kept, which leaves O / l unchanged.
 // TMEM columns: S0/P0 [0,128), S1/P1 [128,256), O0 [256,384), O1 [384,512).
 // Every wait is bounded and reports N550_ERR_TIMEOUT through the device status
 // word.
@@ -35,20 +39,22 @@ namespace {
 constexpr int HD = 128;
 constexpr int NKV = 8;
 constexpr int NL = 28;
-constexpr int BQ = 128;                      // queries per CTA (per head)
+constexpr int BQ = 128;                      // queries per item (per head)
 constexpr int BKV = 128;                     // keys per block
-constexpr int THREADS = 320;                 // 10 warps
+constexpr int THREADS = 576;                 // 18 warps
 constexpr int TILE_BYTES = 128 * HD * 2;     // 32 KB: 128 rows x 128 BF16
 constexpr int HALF_BYTES = TILE_BYTES / 2;   // one 64-column TMA box (16 KB)
 constexpr int STAGES = 2;
-constexpr int SMEM_BYTES = (2 + 2 * STAGES) * TILE_BYTES + 1024 + 256;
+constexpr int XCH_BYTES = (2 * 2 * 2 * 128 + 2 * 2 * 128) * 4;   // row max (x2 parity) + row sum
+constexpr int SMEM_BYTES = (2 + 2 * STAGES) * TILE_BYTES + XCH_BYTES + 1024 + 256;
+static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 constexpr float kScaleLog2 = 0.08838834764831845f * 1.4426950408889634f;   // qwen3.c:296
 constexpr float kRescale = 8.0f;
 
 struct PfParams {
     uint16_t *out;
     const int32_t *seq_ids;
-    int ldo, L, pos0, layer, max_len, n_qblocks;
+    int ldo, L, pos0, layer, max_len, n_qblocks, n_seqs, n_items;
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -71,16 +77,38 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity) {
     return __all_sync(0xFFFFFFFFu, ok);
 }
 
-__device__ __forceinline__ void tmem_ld_row128(uint32_t taddr, uint32_t (&r)[128]) {
-    uint32_t(&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[0]);
-    uint32_t(&r1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[32]);
-    uint32_t(&r2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[64]);
-    uint32_t(&r3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[96]);
-    tmem_ld_32x32b_x32(taddr, r0);
-    tmem_ld_32x32b_x32(taddr + 32, r1);
-    tmem_ld_32x32b_x32(taddr + 64, r2);
-    tmem_ld_32x32b_x32(taddr + 96, r3);
+// Named barrier over the two warps (64 threads) of a softmax pair.
+__device__ __forceinline__ void pair_sync(int id) {
+    asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
+#pragma unroll
+    for (int c = 0; c < N / 32; c++)
+        tmem_ld_32x32b_x32(taddr + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * c]));
     tmem_ld_wait();
+}
+
+// Work item k (longest first): q block n_qblocks - 1 - k / (8 n_seqs), then
+// KV head k % 8 of sequence (k % (8 n_seqs)) / 8.
+struct Item {
+    int s, kvh, q0, nblk, plane;
+};
+
+__device__ __forceinline__ Item decode_item(const PfParams &p, int k, bool with_plane = false) {
+    Item it;
+    const int per_q = NKV * p.n_seqs;
+    const int qb = p.n_qblocks - 1 - k / per_q;
+    const int rest = k % per_q;
+    it.s = rest / NKV;
+    it.kvh = rest % NKV;
+    it.q0 = qb * BQ;
+    const int q_last = min(p.L, it.q0 + BQ) - 1;
+    it.nblk = (p.pos0 + q_last) / BKV + 1;                      // key blocks 0..nblk-1
+    // (slot, layer, kv head); only the producer needs it (a global load)
+    it.plane = with_plane ? (p.seq_ids[it.s] * NL + p.layer) * NKV + it.kvh : 0;
+    return it;
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -91,35 +119,34 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *sQ = base;                              // [2 heads][TILE]
     uint8_t *sKV = base + 2 * TILE_BYTES;            // [STAGES][K TILE | V TILE]
-    uint64_t *bars = (uint64_t *)(base + (2 + 2 * STAGES) * TILE_BYTES);
+    float *xmax = (float *)(base + (2 + 2 * STAGES) * TILE_BYTES);   // [parity][head][half][row]
+    float *xsum = xmax + 2 * 2 * 2 * 128;                             // [head][half][row]
+    uint64_t *bars = (uint64_t *)((uint8_t *)xmax + XCH_BYTES);
     uint64_t *q_full = bars;          // [1]
-    uint64_t *k_full = bars + 1;      // [STAGES]
-    uint64_t *v_full = bars + 3;      // [STAGES]
-    uint64_t *kv_empty = bars + 5;    // [STAGES]
-    uint64_t *s_full = bars + 7;      // [2 heads]
-    uint64_t *p_full = bars + 9;      // [2 heads]
-    uint64_t *o_full = bars + 11;     // [2 heads]
-    uint64_t *done = bars + 13;       // [1]
-    uint32_t *tmem_slot = (uint32_t *)(bars + 14);
+    uint64_t *q_empty = bars + 1;     // [1] every S MMA of the item has read Q
+    uint64_t *k_full = bars + 2;      // [STAGES]
+    uint64_t *v_full = bars + 4;      // [STAGES]
+    uint64_t *kv_empty = bars + 6;    // [STAGES]
+    uint64_t *s_full = bars + 8;      // [2 heads]
+    uint64_t *p_full = bars + 10;     // [2 heads]
+    uint64_t *o_full = bars + 12;     // [2 heads] the item's last P.V done
+    uint64_t *o_free = bars + 14;     // [2 heads] O read out of TMEM
+    uint64_t *done = bars + 16;       // [1]
+    uint32_t *tmem_slot = (uint32_t *)(bars + 17);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qb = p.n_qblocks - 1 - (int)blockIdx.x;   // longest rows first
-    const int kvh = blockIdx.y, s = blockIdx.z;
-    const int seq = p.seq_ids[s];
-    const int q0 = qb * BQ;
-    const int q_last = min(p.L, q0 + BQ) - 1;
-    const int nblk = (p.pos0 + q_last) / BKV + 1;       // key blocks 0..nblk-1
-    const int plane = (seq * NL + p.layer) * NKV + kvh;  // (slot, layer, kv head)
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
         for (int i = 0; i < 2; i++) {
             mbar_init(&k_full[i], 1);
             mbar_init(&v_full[i], 1);
             mbar_init(&kv_empty[i], 1);
             mbar_init(&s_full[i], 1);
-            mbar_init(&p_full[i], 128);
+            mbar_init(&p_full[i], 256);
             mbar_init(&o_full[i], 1);
+            mbar_init(&o_free[i], 256);
         }
         mbar_init(done, 1);
         fence_mbar_init();
@@ -138,30 +165,45 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
-            for (int h = 0; h < 2; h++)
-                for (int half = 0; half < 2; half++)
-                    tma_load_3d(sQ + h * TILE_BYTES + half * HALF_BYTES, &tmQ, q_full,
-                                (2 * kvh + h) * HD + half * 64, q0, s);
-            int issued = 0;
-            for (int j = 0; j < nblk; j++) {
-                const int st = j & 1;
-                if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1)) break;
-                uint8_t *sK = sKV + st * 2 * TILE_BYTES;
-                uint8_t *sV = sK + TILE_BYTES;
-                // Positions at or beyond pos0 + L are outside the map: zeros.
-                const int row = j * BKV;
-                mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
-                tma_load_3d(sK, &tmK, &k_full[st], 0, row, plane);
-                tma_load_3d(sK + HALF_BYTES, &tmK, &k_full[st], 64, row, plane);
-                mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
-                tma_load_3d(sV, &tmV, &v_full[st], 0, row, plane);
-                tma_load_3d(sV + HALF_BYTES, &tmV, &v_full[st], 64, row, plane);
-                issued = j + 1;
+            int kv_iter = 0, item_i = 0, q_loads = 0;
+            bool ok = true;
+            for (int k = blockIdx.x; k < p.n_items && ok; k += gridDim.x, item_i++) {
+                const Item it = decode_item(p, k, true);
+                if (!(ok = mbar_wait(q_empty, (item_i & 1) ^ 1))) break;
+                mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+                q_loads++;
+                for (int h = 0; h < 2; h++)
+                    for (int half = 0; half < 2; half++)
+                        tma_load_3d(sQ + h * TILE_BYTES + half * HALF_BYTES, &tmQ, q_full,
+                                    (2 * it.kvh + h) * HD + half * 64, it.q0, it.s);
+                // The next item's Q can only be loaded once this item's last S
+                // MMA has read the buffer; bring it into L2 now so that load
+                // does not wait on HBM.
+                if (k + (int)gridDim.x < p.n_items) {
+                    const Item nx = decode_item(p, k + gridDim.x);
+                    for (int h = 0; h < 2; h++)
+                        for (int half = 0; half < 2; half++)
+                            tma_prefetch_3d(&tmQ, (2 * nx.kvh + h) * HD + half * 64, nx.q0, nx.s);
+                }
+                for (int j = 0; j < it.nblk; j++, kv_iter++) {
+                    const int st = kv_iter & 1;
+                    if (!(ok = mbar_wait(&kv_empty[st], ((kv_iter >> 1) & 1) ^ 1))) break;
+                    uint8_t *sK = sKV + st * 2 * TILE_BYTES;
+                    uint8_t *sV = sK + TILE_BYTES;
+                    // Positions at or beyond pos0 + L are outside the map: zeros.
+                    const int row = j * BKV;
+                    mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
+                    tma_load_3d(sK, &tmK, &k_full[st], 0, row, it.plane);
+                    tma_load_3d(sK + HALF_BYTES, &tmK, &k_full[st], 64, row, it.plane);
+                    mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
+                    tma_load_3d(sV, &tmV, &v_full[st], 0, row, it.plane);
+                    tma_load_3d(sV + HALF_BYTES, &tmV, &v_full[st], 64, row, it.plane);
+                }
             }
-            // Drain: every load issued must have landed before the CTA exits.
-            mbar_wait(q_full, 0);
-            for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; j++) {
+            // Drain: every load issued must have landed before the CTA exits
+            // (the last Q and the last two K/V stages; older ones were consumed).
+            if (q_loads > 0) mbar_wait(q_full, (q_loads - 1) & 1);
+            for (int j = kv_iter > STAGES ? kv_iter - STAGES : 0; j < kv_iter; j++) {
                 mbar_wait(&k_full[j & 1], (j >> 1) & 1);
                 mbar_wait(&v_full[j & 1], (j >> 1) & 1);
             }
@@ -183,144 +225,212 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                 }
                 umma_commit(&s_full[t]);
             };
-            bool ok = mbar_wait(q_full, 0) && mbar_wait(&k_full[0], 0);
-            if (ok) {
+            int kv_iter = 0, item_i = 0, bj = 0;
+            bool ok = true;
+            for (int k = blockIdx.x; k < p.n_items && ok; k += gridDim.x, item_i++) {
+                const Item it = decode_item(p, k);
+                // S columns are free: the previous item's P.V MMAs, which read
+                // P there, were issued earlier and execute in order.
+                if (!(ok = mbar_wait(q_full, item_i & 1) && mbar_wait(&k_full[kv_iter & 1],
+                                                                        (kv_iter >> 1) & 1)))
+                    break;
                 tc_fence_after();
-                issue_s(0, 0);
-                issue_s(1, 0);
-            }
-            for (int j = 0; j < nblk && ok; j++) {
-                const int st = j & 1;
-                const uint32_t v = aKV + st * 2 * TILE_BYTES + TILE_BYTES;
-                for (int t = 0; t < 2; t++) {
-                    if (!(ok = mbar_wait(&p_full[t], j & 1))) break;
-                    if (t == 0 && !(ok = mbar_wait(&v_full[st], (j >> 1) & 1))) break;
-                    tc_fence_after();
-                    // O_t += P_t . V over the 128 keys of the block (8 x K=16):
-                    // P columns 8 kk .. 8 kk + 7, V rows 16 kk .. 16 kk + 15.
-#pragma unroll
-                    for (int kk = 0; kk < 8; kk++)
-                        umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
-                                     umma_desc_sw128_mn(v + kk * 2048, HALF_BYTES), id_o,
-                                     (j > 0 || kk > 0) ? 1u : 0u);
-                    if (t == 1) umma_commit(&kv_empty[st]);
-                    if (j + 1 < nblk) {
-                        if (t == 0 && !(ok = mbar_wait(&k_full[st ^ 1], ((j + 1) >> 1) & 1))) break;
+                issue_s(0, kv_iter & 1);
+                issue_s(1, kv_iter & 1);
+                if (it.nblk == 1) umma_commit(q_empty);
+                for (int j = 0; j < it.nblk && ok; j++, bj++) {
+                    const int st = (kv_iter + j) & 1;
+                    const uint32_t v = aKV + st * 2 * TILE_BYTES + TILE_BYTES;
+                    for (int t = 0; t < 2; t++) {
+                        if (!(ok = mbar_wait(&p_full[t], bj & 1))) break;
+                        if (t == 0 && !(ok = mbar_wait(&v_full[st], ((kv_iter + j) >> 1) & 1))) break;
+                        // the first P.V of an item overwrites O: the previous
+                        // item's output must have been read out of TMEM
+                        if (j == 0 && !(ok = mbar_wait(&o_free[t], (item_i & 1) ^ 1))) break;
                         tc_fence_after();
-                        issue_s(t, st ^ 1);
-                    } else {
-                        umma_commit(&o_full[t]);
+                        // O_t += P_t . V over the 128 keys of the block (8 x K=16):
+                        // P columns 8 kk .. 8 kk + 7, V rows 16 kk .. 16 kk + 15.
+#pragma unroll
+                        for (int kk = 0; kk < 8; kk++)
+                            umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                                         umma_desc_sw128_mn(v + kk * 2048, HALF_BYTES), id_o,
+                                         (j > 0 || kk > 0) ? 1u : 0u);
+                        if (t == 1) umma_commit(&kv_empty[st]);
+                        if (j + 1 < it.nblk) {
+                            if (t == 0 && !(ok = mbar_wait(&k_full[st ^ 1], ((kv_iter + j + 1) >> 1) & 1)))
+                                break;
+                            tc_fence_after();
+                            issue_s(t, st ^ 1);
+                            if (t == 1 && j + 2 == it.nblk) umma_commit(q_empty);
+                        } else {
+                            umma_commit(&o_full[t]);
+                        }
                     }
                 }
+                kv_iter += it.nblk;
             }
             // Drain all MMAs of this thread before TMEM is released.
             umma_commit(done);
             mbar_wait(done, 0);
         }
     } else {
-        // ---------------- softmax + output (warps 2..9) ----------------
-        const int t = (warp - 2) >> 2;                  // head of the GQA pair
+        // ---------------- softmax + output (warps 2..17) ----------------
+        const int sw = warp - 2;
+        const int t = sw >> 3;                          // head of the GQA pair
+        const int half = (sw >> 2) & 1;                 // key columns / output dims 64*half..
         const int qw = warp & 3;                        // TMEM lane quarter
-        const int row = qw * 32 + lane;                 // query row in the block
-        const int qpos = p.pos0 + q0 + row;
+        const int row = qw * 32 + lane;                 // query row in the item
+        const int bar_id = 1 + t * 4 + qw;              // this pair's named barrier
         const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
-        const uint32_t tS = tmem + lane_off + t * 128;
-        const uint32_t tO = tmem + lane_off + 256 + t * 128;
-        float m_run = -INFINITY, l_run = 0.f;
+        const uint32_t tS = tmem + lane_off + t * 128;  // S (and P) of head t, this lane quarter
+        const uint32_t tO = tmem + lane_off + 256 + t * 128 + half * 64;
+        float *my_sum = xsum + (t * 2 + half) * 128 + row;
+        const float *other_sum = xsum + (t * 2 + (half ^ 1)) * 128 + row;
+        int bj = 0;
         bool ok = true;
-        for (int j = 0; j < nblk; j++) {
-            if (!(ok = warp_wait(&s_full[t], j & 1))) break;
-            tc_fence_after();
-            uint32_t r[128];
-            tmem_ld_row128(tS, r);
-            const int k0 = j * BKV;
-            if (k0 + BKV - 1 > p.pos0 + q0) {           // the block crosses the diagonal
+        for (int k = blockIdx.x, i = 0; k < p.n_items && ok; k += gridDim.x, i++) {
+            const Item it = decode_item(p, k);
+            const int qpos = p.pos0 + it.q0 + row;
+            float m_run = -INFINITY, l_run = 0.f;
+            for (int j = 0; j < it.nblk; j++, bj++) {
+                if (!(ok = warp_wait(&s_full[t], bj & 1))) break;
+                tc_fence_after();
+                // Causal mask: key column e of this half is valid for e <= lim.
+                // lim grows with the lane, so each 32-column chunk is, for the
+                // whole warp, all valid (state 0), all masked (1) or mixed (2).
+                const int k0 = j * BKV;
+                const bool diag = k0 + BKV - 1 > p.pos0 + it.q0;
+                const int lim = qpos - k0 - half * 64;
+                const int lim_lo = __shfl_sync(0xFFFFFFFFu, lim, 0);
+                const int lim_hi = __shfl_sync(0xFFFFFFFFu, lim, 31);
+                auto chunk_state = [&](int c) -> int {
+                    if (!diag || 32 * c + 31 <= lim_lo) return 0;
+                    return 32 * c > lim_hi ? 1 : 2;
+                };
+                // pass 1: maximum over this warp's 64 columns, 32 at a time
+                float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-                for (int i = 0; i < 128; i++)
-                    if (k0 + i > qpos) r[i] = 0xFF800000u;   // -inf
-            }
-            float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+                for (int c = 0; c < 2; c++) {
+                    const int cs = chunk_state(c);
+                    if (cs == 1) continue;
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(tS + half * 64 + 32 * c, v);
+                    tmem_ld_wait();
+                    if (cs == 2) {
 #pragma unroll
-            for (int i = 0; i < 128; i += 4) {
-                mx0 = fmaxf(mx0, __uint_as_float(r[i]));
-                mx1 = fmaxf(mx1, __uint_as_float(r[i + 1]));
-                mx2 = fmaxf(mx2, __uint_as_float(r[i + 2]));
-                mx3 = fmaxf(mx3, __uint_as_float(r[i + 3]));
-            }
-            const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * kScaleLog2;
-            float m_use = m_run;
-            bool resc = false;
-            if (j == 0) {
-                m_use = mx;
-            } else if (mx > m_run + kRescale) {
-                m_use = mx;
-                resc = true;
-            }
-            const float corr = resc ? ex2(m_run - m_use) : 1.0f;
-            float l0 = 0.f, l1 = 0.f;
-            uint32_t pk[64];
+                        for (int e = 0; e < 32; e++)
+                            if (32 * c + e > lim) v[e] = 0xFF800000u;   // -inf
+                    }
 #pragma unroll
-            for (int c = 0; c < 64; c++) {
-                const float a = ex2(fmaf(__uint_as_float(r[2 * c]), kScaleLog2, -m_use));
-                const float b = ex2(fmaf(__uint_as_float(r[2 * c + 1]), kScaleLog2, -m_use));
-                l0 += a;
-                l1 += b;
-                pk[c] = cvt_bf16x2(a, b);
-            }
-            tmem_st_32x32b_x32(tS, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-            tmem_st_32x32b_x32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
-            l_run = l_run * corr + (l0 + l1);
-            m_run = m_use;
-            if (__any_sync(0xFFFFFFFFu, resc)) {
-                // O_t holds blocks 0..j-1 (complete: s_full(j) was committed
-                // after PV_t(j-1)); PV_t(j) is not issued before p_full.
-#pragma unroll 1
-                for (int c = 0; c < 4; c++) {
-                    uint32_t o[32];
-                    tmem_ld_32x32b_x32(tO + 32 * c, o);
+                    for (int e = 0; e < 32; e += 4) {
+                        mx0 = fmaxf(mx0, __uint_as_float(v[e]));
+                        mx1 = fmaxf(mx1, __uint_as_float(v[e + 1]));
+                        mx2 = fmaxf(mx2, __uint_as_float(v[e + 2]));
+                        mx3 = fmaxf(mx3, __uint_as_float(v[e + 3]));
+                    }
+                }
+                // Row maximum over both halves. The exchange slot alternates
+                // with the block parity, so a slot is rewritten only after the
+                // partner has passed the next barrier (and so read it). After
+                // this barrier both warps have also finished reading the S
+                // columns P overwrites (P of this half lands on S columns
+                // 32*half.., read in pass 1 by half 0).
+                float *xm = xmax + (((bj & 1) * 2 + t) * 2) * 128;
+                xm[half * 128 + row] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+                pair_sync(bar_id);
+                const float mx = fmaxf(xm[row], xm[128 + row]) * kScaleLog2;
+                float m_use = m_run;
+                bool resc = false;
+                if (j == 0) {
+                    m_use = mx;
+                } else if (mx > m_run + kRescale) {
+                    m_use = mx;
+                    resc = true;
+                }
+                const float corr = resc ? ex2(m_run - m_use) : 1.0f;
+                // pass 2: P for keys 64*half + 32c .. +31 as 16 packed words at
+                // P columns 32*half + 16c. Half 1's P overwrites S columns of
+                // half 0's first chunk pair (32..63), which half 0 re-reads in
+                // its own pass 2 -- so both halves re-read S before the second
+                // barrier and write P only after it.
+                uint32_t pk[2][16];
+                float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    const int cs = chunk_state(c);
+                    if (cs == 1) {
+#pragma unroll
+                        for (int e = 0; e < 16; e++) pk[c][e] = 0u;
+                        continue;
+                    }
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(tS + half * 64 + 32 * c, v);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
-                    tmem_st_32x32b_x32(tO + 32 * c, o);
+                    for (int e = 0; e < 16; e++) {
+                        float a = ex2(fmaf(__uint_as_float(v[2 * e]), kScaleLog2, -m_use));
+                        float b = ex2(fmaf(__uint_as_float(v[2 * e + 1]), kScaleLog2, -m_use));
+                        if (cs == 2) {
+                            if (32 * c + 2 * e > lim) a = 0.f;
+                            if (32 * c + 2 * e + 1 > lim) b = 0.f;
+                        }
+                        l0 += a;
+                        l1 += b;
+                        pk[c][e] = cvt_bf16x2(a, b);
+                    }
                 }
-            }
-            tmem_st_wait();
-            tc_fence_before();
-            mbar_arrive(&p_full[t]);
-        }
-        if (ok) ok = warp_wait(&o_full[t], 0);
-        if (ok) {
-            tc_fence_after();
-            const float inv = 1.0f / l_run;
-            // Stage the BF16 row in this head's Q tile (no longer read: every
-            // S_t MMA completed before o_full), 16-byte chunk cc of row r at
-            // chunk cc ^ (r & 7), then store whole rows.
-            uint8_t *stg = sQ + t * TILE_BYTES;
+                pair_sync(bar_id);
+                tmem_st_32x32b_x16(tS + half * 32, pk[0]);
+                tmem_st_32x32b_x16(tS + half * 32 + 16, pk[1]);
+                l_run = l_run * corr + (l0 + l1);
+                m_run = m_use;
+                if (__any_sync(0xFFFFFFFFu, resc)) {
+                    // O_t holds blocks 0..j-1 (complete: s_full(j) was committed
+                    // after PV_t(j-1)); PV_t(j) is not issued before p_full.
 #pragma unroll 1
-            for (int c = 0; c < 4; c++) {
+                    for (int c = 0; c < 2; c++) {
+                        uint32_t o[32];
+                        tmem_ld_32x32b_x32(tO + 32 * c, o);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
+                        tmem_st_32x32b_x32(tO + 32 * c, o);
+                    }
+                }
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(&p_full[t]);
+            }
+            if (ok) ok = warp_wait(&o_full[t], i & 1);
+            if (!ok) break;
+            tc_fence_after();
+            // row sum over both halves; the slot is rewritten only an item later
+            *my_sum = l_run;
+            pair_sync(bar_id);
+            const float inv = 1.0f / (l_run + *other_sum);
+            const int qi = it.q0 + row;
+            uint4 *dst = (uint4 *)(p.out + ((size_t)it.s * p.L + (qi < p.L ? qi : 0)) * p.ldo +
+                                   (2 * it.kvh + t) * HD + half * 64);
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
                 uint32_t o[32];
                 tmem_ld_32x32b_x32(tO + 32 * c, o);
                 tmem_ld_wait();
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const int cc = c * 4 + k;
-                    uint4 w;
-                    w.x = cvt_bf16x2(__uint_as_float(o[8 * k]) * inv, __uint_as_float(o[8 * k + 1]) * inv);
-                    w.y = cvt_bf16x2(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv);
-                    w.z = cvt_bf16x2(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv);
-                    w.w = cvt_bf16x2(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv);
-                    *(uint4 *)(stg + row * 256 + ((cc ^ (row & 7)) << 4)) = w;
+                if (c == 1) {
+                    // O is read out: the next item's first P.V may overwrite it
+                    tc_fence_before();
+                    mbar_arrive(&o_free[t]);
                 }
-            }
-            __syncwarp();
-            const int head = 2 * kvh + t;
-#pragma unroll 4
-            for (int it = 0; it < 16; it++) {
-                const int rr = qw * 32 + it * 2 + (lane >> 4), cc = lane & 15;
-                const int qi = q0 + rr;
                 if (qi < p.L) {
-                    const uint4 w = *(const uint4 *)(stg + rr * 256 + ((cc ^ (rr & 7)) << 4));
-                    *(uint4 *)(p.out + ((size_t)s * p.L + qi) * p.ldo + head * HD + cc * 8) = w;
+#pragma unroll
+                    for (int cc = 0; cc < 4; cc++) {
+                        uint4 w;
+                        w.x = cvt_bf16x2(__uint_as_float(o[8 * cc]) * inv, __uint_as_float(o[8 * cc + 1]) * inv);
+                        w.y = cvt_bf16x2(__uint_as_float(o[8 * cc + 2]) * inv, __uint_as_float(o[8 * cc + 3]) * inv);
+                        w.z = cvt_bf16x2(__uint_as_float(o[8 * cc + 4]) * inv, __uint_as_float(o[8 * cc + 5]) * inv);
+                        w.w = cvt_bf16x2(__uint_as_float(o[8 * cc + 6]) * inv, __uint_as_float(o[8 * cc + 7]) * inv);
+                        dst[c * 4 + cc] = w;
+                    }
                 }
             }
         }
@@ -373,7 +483,12 @@ int launch_attn_prefill(cudaStream_t st, const AttnPrefillArgs &a, int n_seqs) {
     p.layer = a.layer;
     p.max_len = a.max_len;
     p.n_qblocks = (a.L + BQ - 1) / BQ;
-    dim3 grid(p.n_qblocks, NKV, n_seqs);
+    p.n_seqs = n_seqs;
+    p.n_items = p.n_qblocks * NKV * n_seqs;
+    int sms = 148;
+    N550_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    // persistent: one CTA per SM walks the items
+    const int grid = p.n_items < sms ? p.n_items : sms;
     attn_prefill_tc_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
     N550_LAUNCH_CHECK();
     return N550_OK;
