@@ -354,7 +354,7 @@ int n550_gemm(void *stream, int mode, int kblock, const void *a, int a_type, int
 }
 
 int n550_gemm_tile_config(int bn) {
-    if (bn != 0 && bn != 128 && bn != 256) return N550_ERR_ARG;
+    if (bn != 0 && bn != 128 && bn != 256 && bn != 512) return N550_ERR_ARG;
     g_tile_bn = bn;
     return N550_OK;
 }

@@ -42,12 +42,15 @@ __host__ __device__ constexpr int tc_epi_warps(int BN, int EPI) {
 // tiles its TMA reduce-adds read.
 __host__ __device__ constexpr int tc_stg_tiles(int EPI) { return EPI == TC_EPI_RESID_F32 ? 2 : 1; }
 
-template <int BN, int NEPI = 4, int STG = 1>
+// PAIR: a 2-CTA cluster computes a 256 x BN tile with tcgen05 cta_group::2;
+// each CTA holds its 128 rows of A and half (BN/2 rows) of B.
+template <int BN, int NEPI = 4, int STG = 1, bool PAIR = false>
 struct TcCfg {
-    static constexpr int STAGES = (BN >= 256) ? 4 : (BN >= 128 ? 6 : 8);
+    static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
+    static constexpr int STAGES = PAIR ? 6 : ((BN >= 256) ? 4 : (BN >= 128 ? 6 : 8));
     static constexpr int THREADS = 64 + 32 * NEPI;
     static constexpr int A_BYTES = BM * BK * 2;
-    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int B_BYTES = B_ROWS * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int EPI_BYTES = NEPI * STG * 32 * 32 * 4;   // 32x32-word tiles per epilogue warp
@@ -163,6 +166,21 @@ __device__ __forceinline__ void load_chunk(uint32_t taddr, float (&v)[32]) {
     for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
 }
 
+// Hands a TMEM accumulator back to the MMA thread after this warp's last
+// tcgen05.ld of it. Single CTA: every epilogue thread arrives on the local
+// barrier. CTA pair: one arrival per warp on the leader CTA's barrier (cbar,
+// a shared::cluster address), whose MMAs write both CTAs' accumulators.
+struct AccRelease {
+    uint64_t *bar;
+    uint32_t cbar;     // 0: single CTA
+};
+__device__ __forceinline__ void acc_release(const AccRelease &r, int lane) {
+    tc_fence_before();
+    if (!r.cbar) { mbar_arrive(r.bar); return; }
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cluster(r.cbar);
+}
+
 // 16 values of one row (lane) as BF16 into 16-byte chunks c16 * 2, c16 * 2 + 1
 // of a 32-column staging tile (alt selects the tile, as in flush_bf16).
 __device__ __forceinline__ void stage_bf16_16(uint32_t *stg, int lane, int c16, int alt,
@@ -192,7 +210,7 @@ __device__ __forceinline__ void load_chunk16(uint32_t taddr, float (&v)[16]) {
 // row's token position / slot once, and the store loops take other rows'
 // destination addresses from their owners by shuffle.
 __device__ __forceinline__ void epilogue_qkv(const TcQkv &p, uint32_t *stg, int lane, uint32_t taddr,
-                                             int row0, int M, int head, uint64_t *tempty_bar) {
+                                             int row0, int M, int head, const AccRelease *rel) {
     const int m = row0 + lane;
     const bool row_ok = m < M;
     const int mc = row_ok ? m : M - 1;
@@ -232,7 +250,7 @@ __device__ __forceinline__ void epilogue_qkv(const TcQkv &p, uint32_t *stg, int 
         float a[16], b[16];
         load_chunk16(taddr + 16 * c, a);
         load_chunk16(taddr + 64 + 16 * c, b);
-        if (c == 3 && tempty_bar) { tc_fence_before(); mbar_arrive(tempty_bar); }
+        if (c == 3 && rel) acc_release(*rel, lane);
         if (normed) {
             // 16-byte loads: 2 (cos, sin) pairs, 8 norm weights per load.
             const float4 *cs4 = (const float4 *)(p.rope + (size_t)pos * 64 + 16 * c);
@@ -277,7 +295,7 @@ __device__ __forceinline__ void epilogue_qkv(const TcQkv &p, uint32_t *stg, int 
     }
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(TcCfg<BN, tc_epi_warps(BN, EPI)>::THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                const __grid_constant__ CUtensorMap tmB,
@@ -287,8 +305,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                int kt_per, float *ws, bool partials) {
     constexpr int NEPI = tc_epi_warps(BN, EPI);
     constexpr int STG = tc_stg_tiles(EPI);
-    using Cfg = TcCfg<BN, NEPI, STG>;
+    using Cfg = TcCfg<BN, NEPI, STG, PAIR>;
     constexpr int STAGES = Cfg::STAGES;
+    constexpr int BMT = PAIR ? 2 * BM : BM;            // output rows per tile
+    static_assert(!PAIR || BN == 256, "CTA pairs use 256-wide tiles");
     constexpr bool SILU = (EPI == TC_EPI_SILU_BF16);
     // Output columns per tile: SILU tiles hold BN/2 gate + BN/2 up columns.
     constexpr int OUT_N = SILU ? BN / 2 : BN;
@@ -306,7 +326,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
-    const int num_m = (M + BM - 1) / BM;
+    // CTA pairs: cluster c (CTAs 2c, 2c+1) walks the tiles; CTA `rank` owns
+    // rows rank*128.. of each 256-row tile.
+    const int rank = PAIR ? (int)cluster_ctarank() : 0;
+    const int u0 = PAIR ? (int)blockIdx.x / 2 : (int)blockIdx.x;
+    const int ustep = PAIR ? (int)gridDim.x / 2 : (int)gridDim.x;
+    const int num_m = (M + BMT - 1) / BMT;
     const int num_n = (N + OUT_N - 1) / OUT_N;
     const int num_k = (K + BK - 1) / BK;
     // Work unit u = (tile u / ksplit, K slice u % ksplit); with ksplit > 1 each
@@ -316,7 +341,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        for (int b = 0; b < 2; b++) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 32 * NEPI); }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], PAIR ? 2 * NEPI : 32 * NEPI);
+        }
         mbar_init(done, 1);
         fence_mbar_init();
     }
@@ -325,9 +353,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
         tma_prefetch_desc(&tmB);
         if (SILU) tma_prefetch_desc(&tmB2);
     }
-    if (warp == 1) { tmem_alloc(tmem_slot, Cfg::TMEM_COLS); tmem_relinquish(); }
+    if (warp == 1) {
+        if (PAIR) { tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS); tmem_relinquish_pair(); }
+        else { tmem_alloc(tmem_slot, Cfg::TMEM_COLS); tmem_relinquish(); }
+    }
     tc_fence_before();
     __syncthreads();
+    // the peer's loads signal the leader's barriers and the leader's MMAs write
+    // the peer's TMEM: both CTAs must be initialised first
+    if (PAIR) cluster_sync();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -338,7 +372,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+            for (int u = u0; u < total && ok; u += ustep) {
                 const int t = u / ksplit, sk = u - t * ksplit;
                 const int mb = m_fast ? t % num_m : t / num_n, nb = m_fast ? t / num_m : t % num_n;
                 const int kt0 = sk * kt_per, kt1 = min(num_k, kt0 + kt_per);
@@ -346,6 +380,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     if (!mbar_wait(&empty[stage], phase ^ 1)) { ok = false; break; }
                     uint8_t *sA = base + stage * Cfg::STAGE_BYTES;
                     uint8_t *sB = sA + Cfg::A_BYTES;
+                    if (PAIR) {
+                        // both CTAs' bytes complete on the leader's barrier
+                        const uint32_t cb = mapa_shared(smem_u32(&full[stage]), 0);
+                        if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+                        tma_load_2d_pair(sA, &tmA, cb, kt * BK, mb * BMT + rank * BM);
+                        if (SILU)   // the pair's B tile: gate rows (rank 0) | up rows (rank 1)
+                            tma_load_2d_pair(sB, rank ? &tmB2 : &tmB, cb, kt * BK, nb * (BN / 2));
+                        else
+                            tma_load_2d_pair(sB, &tmB, cb, kt * BK, nb * BN + rank * (BN / 2));
+                        issued++;
+                        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                        continue;
+                    }
                     mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
                     tma_load_2d(sA, &tmA, &full[stage], kt * BK, mb * BM);
                     if (SILU) {
@@ -359,24 +406,29 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     if (++stage == STAGES) { stage = 0; phase ^= 1; }
                 }
             }
-            // Drain: every load issued must have landed before the CTA exits.
+            // Drain: every load issued must have landed before the CTA exits
+            // (pair: the leader's barriers count both CTAs' loads, and the
+            // peer leaves only after the final cluster barrier).
             long long first = issued > STAGES ? issued - STAGES : 0;
-            for (long long i = first; i < issued; i++)
-                if (!mbar_wait(&full[i % STAGES], (uint32_t)((i / STAGES) & 1))) break;
+            if (!PAIR || rank == 0)
+                for (long long i = first; i < issued; i++)
+                    if (!mbar_wait(&full[i % STAGES], (uint32_t)((i / STAGES) & 1))) break;
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            constexpr uint32_t idesc = umma_idesc_bf16(BM, BN);
+        // (pair: only the leader issues; the peer's MMA warp only holds TMEM)
+        if (lane == 0 && (!PAIR || rank == 0)) {
+            constexpr uint32_t idesc = umma_idesc_bf16(BMT, BN);
             int stage = 0;
             uint32_t phase = 0;
             int ab = 0;
             uint32_t aphase = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+            for (int u = u0; u < total && ok; u += ustep) {
                 const int sk = u % ksplit;
                 const int kt0 = sk * kt_per, kt1 = min(num_k, kt0 + kt_per);
-                if (!mbar_wait(&tempty[ab], aphase ^ 1)) break;
+                if (!(PAIR ? mbar_wait_cluster(&tempty[ab], aphase ^ 1) : mbar_wait(&tempty[ab], aphase ^ 1)))
+                    break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(ab * BN);
                 for (int kt = kt0; kt < kt1; kt++) {
@@ -386,19 +438,27 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     const uint32_t b0 = a0 + Cfg::A_BYTES;
 #pragma unroll
                     for (int ks = 0; ks < BK / UMMA_K; ks++) {
-                        umma_bf16(d_tmem, umma_desc_sw128(a0 + ks * UMMA_K * 2),
-                                  umma_desc_sw128(b0 + ks * UMMA_K * 2), idesc,
-                                  (kt != kt0 || ks != 0) ? 1u : 0u);
+                        if (PAIR)
+                            umma_bf16_pair(d_tmem, umma_desc_sw128(a0 + ks * UMMA_K * 2),
+                                           umma_desc_sw128(b0 + ks * UMMA_K * 2), idesc,
+                                           (kt != kt0 || ks != 0) ? 1u : 0u);
+                        else
+                            umma_bf16(d_tmem, umma_desc_sw128(a0 + ks * UMMA_K * 2),
+                                      umma_desc_sw128(b0 + ks * UMMA_K * 2), idesc,
+                                      (kt != kt0 || ks != 0) ? 1u : 0u);
                     }
-                    umma_commit(&empty[stage]);
+                    if (PAIR) umma_commit_pair_mc(&empty[stage], 3);
+                    else umma_commit(&empty[stage]);
                     if (++stage == STAGES) { stage = 0; phase ^= 1; }
                 }
                 if (!ok) break;
-                umma_commit(&tfull[ab]);
+                if (PAIR) umma_commit_pair_mc(&tfull[ab], 3);
+                else umma_commit(&tfull[ab]);
                 if (++ab == 2) { ab = 0; aphase ^= 1; }
             }
             // Drain all MMAs of this thread before TMEM is released.
-            umma_commit(done);
+            if (PAIR) umma_commit_pair_mc(done, 1);
+            else umma_commit(done);
             mbar_wait(done, 0);
         }
     } else {
@@ -408,13 +468,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
         int chunks = 0;                          // residual chunks handed to the TMA
         int ab = 0;
         uint32_t aphase = 0;
-        for (int u = blockIdx.x; u < total; u += gridDim.x) {
+        for (int u = u0; u < total; u += ustep) {
             const int t = u / ksplit, sk = u - t * ksplit;
             const int mb = m_fast ? t % num_m : t / num_n, nb = m_fast ? t / num_m : t % num_n;
             if (!mbar_wait(&tfull[ab], aphase)) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
-            const int row0 = mb * BM + q * 32;          // first row of this warp's quarter
+            const int row0 = mb * BMT + rank * BM + q * 32;   // first row of this warp's quarter
+            AccRelease rel;
+            rel.bar = &tempty[ab];
+            rel.cbar = PAIR ? mapa_shared(smem_u32(&tempty[ab]), 0) : 0u;
             if (ksplit > 1 || partials) {
                 // Partial sums of K slice sk: raw FP32 accumulators into
                 // ws[sk][M][ldw]; SwiGLU tiles put gate at column n, up at N + n.
@@ -425,7 +488,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(taddr + cch, r);
                     tmem_ld_wait();
-                    if (cch + 32 == BN) { tc_fence_before(); mbar_arrive(&tempty[ab]); }
+                    if (cch + 32 == BN) acc_release(rel, lane);
                     const int n = SILU ? (cch < OUT_N ? nb * OUT_N + cch : N + nb * OUT_N + cch - OUT_N)
                                        : nb * BN + cch;
                     const int nlim = SILU ? (cch < OUT_N ? N : 2 * N) : N;
@@ -439,12 +502,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                 if (NEPI == 8) {
                     // warps 2-5: first head of the tile, warps 6-9: second
                     const int hh = (warp - 2) >> 2;
-                    epilogue_qkv(ep.qkv, stg, lane, taddr + hh * 128, row0, M, nb * 2 + hh, &tempty[ab]);
+                    epilogue_qkv(ep.qkv, stg, lane, taddr + hh * 128, row0, M, nb * 2 + hh, &rel);
                 } else {
 #pragma unroll 1
                     for (int hh = 0; hh < BN / 128; hh++)
                         epilogue_qkv(ep.qkv, stg, lane, taddr + hh * 128, row0, M,
-                                     nb * (BN / 128) + hh, hh + 1 == BN / 128 ? &tempty[ab] : nullptr);
+                                     nb * (BN / 128) + hh, hh + 1 == BN / 128 ? &rel : nullptr);
                 }
             } else if (SILU) {
 #pragma unroll 1
@@ -452,7 +515,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     float g[32], u[32];
                     load_chunk(taddr + cch, g);
                     load_chunk(taddr + OUT_N + cch, u);
-                    if (cch + 32 == OUT_N) { tc_fence_before(); mbar_arrive(&tempty[ab]); }
+                    if (cch + 32 == OUT_N) acc_release(rel, lane);
                     float h[32];
 #pragma unroll
                     for (int j = 0; j < 32; j++) h[j] = silu_mul_f(g[j], u[j]);
@@ -476,7 +539,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(taddr + cch, r);
                     tmem_ld_wait();
-                    if (cch + 32 == BN) { tc_fence_before(); mbar_arrive(&tempty[ab]); }
+                    if (cch + 32 == BN) acc_release(rel, lane);
                     const int n = nb * BN + cch;
                     uint32_t *sb = stg + (chunks & 1) * 32 * 32;
                     if (lane == 0) bulk_wait_group_read<1>();   // the reduce that last read sb
@@ -496,7 +559,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(taddr + cch, r);
                     tmem_ld_wait();
-                    if (cch + 32 == BN) { tc_fence_before(); mbar_arrive(&tempty[ab]); }
+                    if (cch + 32 == BN) acc_release(rel, lane);
                     const int n = nb * BN + cch;
                     if (EPI == TC_EPI_BF16) {
                         float v[32];
@@ -527,9 +590,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
 
     tc_fence_before();
     __syncthreads();
+    // pair: the leader's MMAs wrote the peer's TMEM and the peer's loads were
+    // counted on the leader's barriers -- neither CTA leaves before both are done
+    if (PAIR) cluster_sync();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+        if (PAIR) tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+        else tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
     }
 }
 
@@ -589,12 +656,13 @@ int num_sms() {
     return g_num_sms[dev];
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool PAIR = false>
 int launch_impl(cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tb,
                 const CUtensorMap &tb2, const TcEpilogue &ep, int M, int N, int K,
                 int max_ctas, int ksplit = 1, int kt_per = 1 << 30, float *ws = nullptr,
                 bool partials = false, const CUtensorMap *tc = nullptr) {
-    using Cfg = TcCfg<BN, tc_epi_warps(BN, EPI), tc_stg_tiles(EPI)>;
+    using Cfg = TcCfg<BN, tc_epi_warps(BN, EPI), tc_stg_tiles(EPI), PAIR>;
+    if (PAIR && (ksplit != 1 || partials)) return N550_ERR_ARG;
     CUtensorMap tmc;
     if (tc) tmc = *tc;
     else memset(&tmc, 0, sizeof tmc);
@@ -602,25 +670,63 @@ int launch_impl(cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tb,
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-        N550_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>,
+        N550_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, PAIR>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            Cfg::SMEM_BYTES));
         attr_done[dev] = true;
     }
     constexpr int OUT_N = (EPI == TC_EPI_SILU_BF16) ? BN / 2 : BN;
-    const long long tiles = (long long)((M + BM - 1) / BM) * ((N + OUT_N - 1) / OUT_N) * ksplit;
+    constexpr int BMT = PAIR ? 2 * BM : BM;
+    const long long tiles = (long long)((M + BMT - 1) / BMT) * ((N + OUT_N - 1) / OUT_N) * ksplit;
     int grid = num_sms();
     if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
-    if (tiles < grid) grid = (int)tiles;
+    const long long ctas = PAIR ? 2 * tiles : tiles;
+    if (ctas < grid) grid = (int)ctas;
+    if (PAIR) grid &= ~1;
+    if (grid < 1) return N550_ERR_ARG;
     // Resident CTAs work on consecutive tiles: walk M fastest when the weight
     // operand is the larger one (e.g. the 311 MB lm_head), so each B tile is
     // fetched from HBM once and reused from L2 by the CTAs of all M tiles;
     // otherwise walk N fastest so that A rows are shared.
     const int m_fast = (long long)N * (EPI == TC_EPI_SILU_BF16 ? 2 : 1) > (long long)M;
-    gemm_tc_kernel<BN, EPI><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tb2, tmc, ep, M, N, K, m_fast,
-                                                                     ksplit, kt_per, ws, partials);
-    N550_LAUNCH_CHECK();
+    if constexpr (!PAIR) {
+        gemm_tc_kernel<BN, EPI, false><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(
+            ta, tb, tb2, tmc, ep, M, N, K, m_fast, ksplit, kt_per, ws, partials);
+        N550_LAUNCH_CHECK();
+        return N550_OK;
+    } else {
+    // 2-CTA clusters: consecutive CTAs (2c, 2c+1) form pair c.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(Cfg::THREADS);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // persistent pairs: no more clusters than can be resident at once (SMs
+    // of a GPC that cannot be paired stay out)
+    static int max_clusters[64] = {};
+    if (dev >= 0 && dev < 64) {
+        if (!max_clusters[dev]) {
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<BN, EPI, true>, &cfg) != cudaSuccess || n < 1) {
+                (void)cudaGetLastError();
+                n = num_sms() / 2;
+            }
+            max_clusters[dev] = n;
+        }
+        if (grid > 2 * max_clusters[dev]) grid = 2 * max_clusters[dev];
+        cfg.gridDim = dim3(grid);
+    }
+    N550_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, EPI, true>, ta, tb, tb2, tmc, ep, M, N, K,
+                                     m_fast, ksplit, kt_per, ws, partials));
     return N550_OK;
+    }
 }
 
 // Sum of the ksplit partial tiles in slice order, then the epilogue.
@@ -702,13 +808,27 @@ int launch_gemm_tc_qkv(cudaStream_t st, const uint16_t *a, int lda, const uint16
     TcEpilogue ep{};
     ep.qkv = q;
     ep.vec_ok = 1;
+    if (bn == 256 && tc_use_pair(M, bn)) {
+        // pair tiles: each CTA's B box is one head (128 rows)
+        if ((rc = make_tmap(&tb, w, 4096, K, K, 128))) return rc;
+        return launch_impl<256, TC_EPI_QKV_ROPE, true>(st, ta, tb, tb, ep, M, 4096, K, max_ctas);
+    }
     if (bn == 256) return launch_impl<256, TC_EPI_QKV_ROPE>(st, ta, tb, tb, ep, M, 4096, K, max_ctas);
     return launch_impl<128, TC_EPI_QKV_ROPE>(st, ta, tb, tb, ep, M, 4096, K, max_ctas);
 }
 
-int g_tile_bn = 0;   // 0: automatic
+// 0: automatic; 128 / 256: single-CTA tiles of that width; 512: 256 x 256
+// tiles on 2-CTA clusters.
+int g_tile_bn = 0;
+
+bool tc_use_pair(int M, int bn) {
+    if (bn != 256 || g_tile_bn == 256) return false;
+    // a 256-row pair tile wants enough rows to fill both CTAs
+    return g_tile_bn == 512 || M >= 1024;
+}
 
 int n550_tile_bn(int M, int N) {
+    if (g_tile_bn == 512) return 256;
     if (g_tile_bn) return g_tile_bn;
     // 256-wide tiles halve the operand traffic per MMA (measured on prefill
     // shapes: 1.3 PFLOP/s vs 0.85); narrow outputs and skinny M keep 128 so
@@ -811,7 +931,10 @@ int launch_gemm_tc(cudaStream_t st, int epi, int bn, const uint16_t *a, int lda,
     int rc = get_encoder();
     if (rc) return rc;
     if (bn != 128 && bn != 256) bn = 128;
-    const int brows = (epi == TC_EPI_SILU_BF16) ? bn / 2 : bn;
+    const bool pair = tc_use_pair(M, bn);
+    // B rows per CTA and TMA box: SwiGLU tiles hold bn/2 gate + bn/2 up rows,
+    // pair tiles split a tile's bn rows between the two CTAs
+    const int brows = (epi == TC_EPI_SILU_BF16 || pair) ? bn / 2 : bn;
     CUtensorMap ta, tb, tb2;
     if ((rc = make_tmap(&ta, a, M, K, lda, BM))) return rc;
     if ((rc = make_tmap(&tb, b, N, K, ldb, brows))) return rc;
@@ -831,9 +954,15 @@ int launch_gemm_tc(cudaStream_t st, int epi, int bn, const uint16_t *a, int lda,
         ep.tma_resid = 1;
         tcp = &tc;
     }
-#define N550_TC_CASE(BNV, EV) \
-    if (bn == BNV && epi == EV)   \
-        return launch_impl<BNV, EV>(st, ta, tb, tb2, ep, M, N, K, max_ctas, 1, 1 << 30, nullptr, false, tcp);
+#define N550_TC_CASE(BNV, EV)                                                                   \
+    if (bn == BNV && epi == EV) {                                                               \
+        if constexpr (BNV == 256)                                                               \
+            if (pair)                                                                           \
+                return launch_impl<256, EV, true>(st, ta, tb, tb2, ep, M, N, K, max_ctas, 1,      \
+                                                  1 << 30, nullptr, false, tcp);                \
+        return launch_impl<BNV, EV>(st, ta, tb, tb2, ep, M, N, K, max_ctas, 1, 1 << 30, nullptr,  \
+                                    false, tcp);                                                \
+    }
     N550_TC_CASE(128, TC_EPI_F32)
     N550_TC_CASE(128, TC_EPI_BF16)
     N550_TC_CASE(128, TC_EPI_RESID_F32)

@@ -40,6 +40,8 @@ struct TcEpilogue {
 // g_tile_bn (n550_gemm_tile_config) overrides the automatic choice.
 extern int g_tile_bn;
 int n550_tile_bn(int M, int N);
+// True when a bn = 256 tile runs as a 256 x 256 tile on a 2-CTA cluster.
+bool tc_use_pair(int M, int bn);
 
 // True when the tensor-core path takes these operands (TMA constraints).
 bool tc_shape_ok(const void *a, int lda, const void *b, int ldb, int K);
