@@ -144,9 +144,11 @@ int n550_gemm_f32a_noalloc(void *stream, const float *a, int lda,
                            const uint16_t *b, int ldb, void *c, int c_type, int ldc,
                            int M, int N, int K);
 
-/* Tile width of the fast-mode tensor-core GEMMs: 128 or 256 output columns
- * per CTA tile, or 0 for the automatic choice (default). A tuning knob for
- * profiling; results do not depend on it beyond FP32 summation order. */
+/* Tile shape of the fast-mode tensor-core GEMMs: 128 or 256 output columns
+ * per single-CTA 128-row tile, 512 for 256 x 256 tiles computed by 2-CTA
+ * clusters (tcgen05 cta_group::2), or 0 for the automatic choice (default:
+ * pairs for M >= 1024 and N >= 1024). A tuning knob for profiling; results do
+ * not depend on it beyond FP32 summation order. */
 int n550_gemm_tile_config(int bn);
 
 /* Fused fast-mode GEMMs of the decoder layer (A BF16, weights BF16 [N,K]):
