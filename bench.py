@@ -213,15 +213,20 @@ def run_n550(args, world, rank, local):
         return max_over_ranks(ms, world, dev)
 
     K = args.steps
+    # Headline: the prefill as a user repeats it (from the second identical
+    # call the library replays a captured CUDA graph), no profiler attached.
     with ClockSampler(local) as clk:
-        ms = timed(step_device, K, prof=True)
+        ms = timed(step_device, K)
     clocks = clk.summary()
+    ms_e2e = timed(step_e2e, K)
+    # Per-kernel breakdown and the GEMM roofline: a separate eager pass with
+    # CUDA events around every launch (not used for `value`).
+    timed(step_device, K, prof=True)
     kind_ms = (C.c_double * 9)()
     kind_n = (C.c_int64 * 9)()
     n5.check(n5.lib().n550_qwen3_profile_read(m.handle, kind_ms, kind_n, 9))
     n5.check(n5.lib().n550_qwen3_profile(m.handle, 0))
     launches_per_step = sum(kind_n) / K
-    ms_e2e = timed(step_e2e, K)
 
     total_tokens = PREFILL_SEQS * PREFILL_LEN
     value = total_tokens / (ms / 1000.0)

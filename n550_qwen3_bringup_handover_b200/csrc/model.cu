@@ -418,6 +418,10 @@ struct n550_model {
     int g_n = 0;
     const void *g_key[4] = {};
     int32_t *step_counter = nullptr;
+    // captured prefill of the last repeated call (n550_qwen3_prefill)
+    cudaGraphExec_t pgraph = nullptr;
+    long long pg_key[7] = {};               // key of the captured call
+    long long pg_last[7] = {};              // key of the previous eager call
     cudaStream_t cap_stream = nullptr;      // capture/replay stream (the legacy
     cudaEvent_t ev_in = nullptr, ev_out = nullptr;   // stream cannot be captured)
 };
@@ -449,6 +453,7 @@ struct ProfScope {
 void model_release(n550_model *m) {
     if (!m) return;
     if (m->graph) cudaGraphExecDestroy(m->graph);
+    if (m->pgraph) cudaGraphExecDestroy(m->pgraph);
     if (m->step_counter) cudaFree(m->step_counter);
     if (m->cap_stream) cudaStreamDestroy(m->cap_stream);
     if (m->ev_in) cudaEventDestroy(m->ev_in);
@@ -793,12 +798,66 @@ void n550_qwen3_free(n550_model_t *m) {
     model_release(m);
 }
 
+static int prefill_eager(n550_model_t *m, cudaStream_t st, const int32_t *tokens,
+                         const int32_t *seq_ids, int n_seqs, int seq_len, int pos0, float *logits,
+                         int32_t *next_token);
+
+// A call that repeats the previous call's buffers and shape (a serving loop
+// over a fixed batch, a benchmark) is captured into a CUDA graph on its second
+// occurrence and replayed from then on: the ~1000 launches and tensor-map
+// encodings of a prefill leave the host. The first occurrence runs eagerly, so
+// one-time setup (kernel attributes) never enters a capture. With the
+// profiler on, every call runs eagerly.
 int n550_qwen3_prefill(n550_model_t *m, void *stream, const int32_t *tokens, const int32_t *seq_ids,
                        int n_seqs, int seq_len, int pos0, float *logits, int32_t *next_token) {
     if (!m || !tokens || !seq_ids || n_seqs < 1 || seq_len < 1 || pos0 < 0) return N550_ERR_ARG;
     const n550_model_config &c = m->cfg;
     if (pos0 + seq_len > c.max_len) return N550_ERR_ARG;
     cudaStream_t st = (cudaStream_t)stream;
+    if (m->prof.on) return prefill_eager(m, st, tokens, seq_ids, n_seqs, seq_len, pos0, logits, next_token);
+    const long long key[7] = {(long long)(uintptr_t)tokens, (long long)(uintptr_t)seq_ids,
+                              (long long)(uintptr_t)logits, (long long)(uintptr_t)next_token,
+                              n_seqs, seq_len, pos0};
+    const bool replay = m->pgraph && !memcmp(key, m->pg_key, sizeof key);
+    const bool capture = !replay && !memcmp(key, m->pg_last, sizeof key);
+    if (!replay && !capture) {
+        memcpy(m->pg_last, key, sizeof key);
+        return prefill_eager(m, st, tokens, seq_ids, n_seqs, seq_len, pos0, logits, next_token);
+    }
+    const cudaStream_t cs = m->cap_stream;
+    N550_CUDA_TRY(cudaEventRecord(m->ev_in, st));
+    N550_CUDA_TRY(cudaStreamWaitEvent(cs, m->ev_in, 0));
+    int rc = N550_OK;
+    if (capture) {
+        if (m->pgraph) { cudaGraphExecDestroy(m->pgraph); m->pgraph = nullptr; }
+        cudaGraph_t g = nullptr;
+        if (cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+            rc = N550_ERR_CUDA;
+        } else {
+            rc = prefill_eager(m, cs, tokens, seq_ids, n_seqs, seq_len, pos0, logits, next_token);
+            const cudaError_t ce = cudaStreamEndCapture(cs, &g);
+            if (!rc && ce != cudaSuccess) rc = N550_ERR_CUDA;
+        }
+        if (!rc && cudaGraphInstantiate(&m->pgraph, g, 0) != cudaSuccess) {
+            m->pgraph = nullptr;
+            rc = N550_ERR_CUDA;
+        }
+        if (g) cudaGraphDestroy(g);
+        (void)cudaGetLastError();
+        if (!rc) memcpy(m->pg_key, key, sizeof key);
+        else memset(m->pg_last, 0, sizeof m->pg_last);
+    }
+    if (!rc && cudaGraphLaunch(m->pgraph, cs) != cudaSuccess) rc = N550_ERR_CUDA;
+    N550_CUDA_TRY(cudaEventRecord(m->ev_out, cs));
+    N550_CUDA_TRY(cudaStreamWaitEvent(st, m->ev_out, 0));
+    if (rc) return rc;
+    return N550_OK;
+}
+
+static int prefill_eager(n550_model_t *m, cudaStream_t st, const int32_t *tokens,
+                         const int32_t *seq_ids, int n_seqs, int seq_len, int pos0, float *logits,
+                         int32_t *next_token) {
+    const n550_model_config &c = m->cfg;
     const int Lmax = std::min(seq_len, c.max_tokens);
     int rc;
     for (int s0 = 0; s0 < n_seqs;) {
