@@ -147,7 +147,7 @@ int n550_gemm_f32a_noalloc(void *stream, const float *a, int lda,
 /* Tile shape of the fast-mode tensor-core GEMMs: 128 or 256 output columns
  * per single-CTA 128-row tile, 512 for 256 x 256 tiles computed by 2-CTA
  * clusters (tcgen05 cta_group::2), or 0 for the automatic choice (default:
- * pairs for M >= 1024 and N >= 1024). A tuning knob for profiling; results do
+ * pairs for M >= 12288 and N >= 1024). A tuning knob for profiling; results do
  * not depend on it beyond FP32 summation order. */
 int n550_gemm_tile_config(int bn);
 

@@ -230,6 +230,47 @@ def test_residual_gemm_tma_add_is_exact(cuda, M, K, N, ld):
     assert torch.equal(x[:, N:], x0[:, N:])
 
 
+@pytest.mark.parametrize("tile", [128, 256, 512])
+@pytest.mark.parametrize("M,K,N,out", [(1100, 1024, 1000, "f32"), (2048, 2048, 1024, "resid"),
+                                       (1500, 1024, 768, "swiglu"), (1024, 1024, 4096, "bf16"),
+                                       (384, 3072, 1024, "f32")])
+def test_tile_shapes(cuda, tile, M, K, N, out):
+    """Every fast-GEMM tile shape -- 128- and 256-wide single-CTA tiles and
+    256 x 256 tiles on 2-CTA clusters (forced with n550_gemm_tile_config) --
+    on ragged M and N, for each epilogue, against binary64."""
+    import torch
+    A = oracle.synth_normal_bf16((M, K), 53, 0x41, 1.0)
+    B = oracle.synth_normal_bf16((N, K), 53, 0x42, 0.02)
+    dA, dB = to_dev_bf16(A, cuda), to_dev_bf16(B, cuda)
+    try:
+        n5.check(n5.lib().n550_gemm_tile_config(tile))
+        if out == "swiglu":
+            U = oracle.synth_normal_bf16((N, K), 53, 0x55, 0.02)
+            h = n5.gemm_swiglu(dA, dB, to_dev_bf16(U, cuda))
+            torch.cuda.synchronize()
+            g, u = f64_ref(A, B), f64_ref(A, U)
+            got = oracle.bf16_to_f32(bf16_bits(h)).astype(np.float64)
+            assert rel_err(got, g / (1.0 + np.exp(-g)) * u) <= BF16_OUT_TOL
+        elif out == "resid":
+            x0 = oracle.synth_normal_f32((M, N), 53, 0x58, 1.0)
+            x = torch.from_numpy(x0.copy()).to(cuda)
+            n5.gemm_residual(dA, dB, x)
+            torch.cuda.synchronize()
+            assert rel_err(x.cpu().numpy(), x0.astype(np.float64) + f64_ref(A, B)) <= FAST_TOL
+        elif out == "bf16":
+            c = n5.gemm(dA, dB, mode=n5.MODE_FAST, out_dtype=torch.bfloat16)
+            torch.cuda.synchronize()
+            got = oracle.bf16_to_f32(bf16_bits(c)).astype(np.float64)
+            assert rel_err(got, f64_ref(A, B)) <= BF16_OUT_TOL
+        else:
+            c = n5.gemm(dA, dB, mode=n5.MODE_FAST)
+            torch.cuda.synchronize()
+            assert rel_err(c.cpu().numpy(), f64_ref(A, B)) <= FAST_TOL
+    finally:
+        n5.lib().n550_gemm_tile_config(0)
+    assert n5.device_status() == n5.OK
+
+
 @pytest.mark.parametrize("M,K,N", [(300, 1024, 3072), (128, 1024, 200), (17, 1024, 64)])
 def test_fused_swiglu_gemm(cuda, M, K, N):
     """h = silu(A . Wg^T) * (A . Wu^T) in BF16 (gate/up qwen3_gemm then qwen3_op_silu_mul)."""

@@ -257,6 +257,36 @@ def test_fused_qkv_prefill_matches_split_path(cuda):
         assert rel(fused_dec[s], lg2) <= LOGIT_TOL
 
 
+@pytest.mark.parametrize("tile", [256, 512])
+def test_prefill_tile_shapes_agree(cuda, tile):
+    """The same 8 x 512-token prefill with the projection GEMMs forced onto
+    single-CTA 128 x 256 tiles or 256 x 256 CTA-pair tiles (the q/k/v epilogue
+    with QK-norm, RoPE and the KV write included) gives the same logits as the
+    automatic choice, and a repeated call (CUDA-graph replay) the same again."""
+    import torch
+    S, L = 8, 512
+    toks = torch.from_numpy(oracle.synth_tokens(S * L, 21, 0x544F4B).reshape(S, L)).cuda()
+    seq = torch.arange(S, dtype=torch.int32, device="cuda")
+    m = n5.Model(seed=0, max_seqs=S, max_len=L, max_tokens=S * L)
+    out = {}
+    try:
+        for cfg in (0, tile):
+            n5.check(n5.lib().n550_gemm_tile_config(cfg))
+            lg = torch.empty((S, 151936), dtype=torch.float32, device="cuda")
+            nx = torch.empty(S, dtype=torch.int32, device="cuda")
+            for _ in range(3):                      # eager, captured, replayed
+                m.prefill(toks, seq, 0, lg, nx)
+            torch.cuda.synchronize()
+            out[cfg] = (lg.cpu().numpy(), nx.cpu().numpy())
+    finally:
+        n5.lib().n550_gemm_tile_config(0)
+        m.close()
+    assert n5.device_status() == n5.OK
+    for s in range(S):
+        assert rel(out[tile][0][s], out[0][0][s]) <= LOGIT_TOL
+        assert same_choice(int(out[tile][1][s]), out[0][0][s])
+
+
 def test_decode_steps_graph_replay_matches_eager(cuda):
     """n550_qwen3_decode_steps: the CUDA-graph replay of a decode step gives
     exactly the ids, tokens and positions of the eager loop."""
