@@ -35,7 +35,7 @@ constexpr int UMMA_K = 16;
 // Epilogue warps: 4 (one per TMEM lane quarter); the two-head QKV tile gets
 // 8 (one head each), because its per-row RMSNorm + RoPE work is latency-bound.
 __host__ __device__ constexpr int tc_epi_warps(int BN, int EPI) {
-    return (EPI == TC_EPI_QKV_ROPE && BN == 256) ? 8 : 4;
+    return (EPI == TC_EPI_QKV_ROPE && BN == 256) ? 16 : 4;
 }
 
 // Staging tiles per epilogue warp: the residual epilogue double-buffers the
@@ -47,14 +47,19 @@ __host__ __device__ constexpr int tc_stg_tiles(int EPI) { return EPI == TC_EPI_R
 template <int BN, int NEPI = 4, int STG = 1, bool PAIR = false>
 struct TcCfg {
     static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
-    static constexpr int STAGES = PAIR ? 6 : ((BN >= 256) ? 4 : (BN >= 128 ? 6 : 8));
+    // (16 epilogue warps stage 64 KB: fewer operand stages fit)
+    static constexpr int STAGES = PAIR ? (NEPI == 16 ? 4 : 6)
+                                       : ((BN >= 256) ? (NEPI == 16 ? 3 : 4) : (BN >= 128 ? 6 : 8));
     static constexpr int THREADS = 64 + 32 * NEPI;
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = B_ROWS * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int EPI_BYTES = NEPI * STG * 32 * 32 * 4;   // 32x32-word tiles per epilogue warp
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
+    // + 512 B: the q/k norm weights of the fused QKV epilogue; + 4 KB: its
+    // sum-of-squares exchange between warp pairs ([tile parity][head][half][row])
+    static constexpr int SMEM_BYTES =
+        STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256 + 512 + (NEPI == 16 ? 4096 : 0);
     static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 };
 
@@ -183,13 +188,21 @@ __device__ __forceinline__ void acc_release(const AccRelease &r, int lane) {
 
 // 16 values of one row (lane) as BF16 into 16-byte chunks c16 * 2, c16 * 2 + 1
 // of a 32-column staging tile (alt selects the tile, as in flush_bf16).
+// (lo, hi) -> packed BF16x2 with one cvt.rn (round to nearest even; the q/k/v
+// values are finite).
+__device__ __forceinline__ uint32_t cvt_rn_bf16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
 __device__ __forceinline__ void stage_bf16_16(uint32_t *stg, int lane, int c16, int alt,
                                               const float (&v)[16]) {
 #pragma unroll
     for (int k = 0; k < 2; k++)
         *(uint4 *)(stg + (b16_word(lane, c16 * 2 + k) ^ alt)) =
-            make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]), pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
-                       pack_bf16x2(v[8 * k + 4], v[8 * k + 5]), pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
+            make_uint4(cvt_rn_bf16x2(v[8 * k], v[8 * k + 1]), cvt_rn_bf16x2(v[8 * k + 2], v[8 * k + 3]),
+                       cvt_rn_bf16x2(v[8 * k + 4], v[8 * k + 5]), cvt_rn_bf16x2(v[8 * k + 6], v[8 * k + 7]));
 }
 
 __device__ __forceinline__ void load_chunk16(uint32_t taddr, float (&v)[16]) {
@@ -210,13 +223,16 @@ __device__ __forceinline__ void load_chunk16(uint32_t taddr, float (&v)[16]) {
 // row's token position / slot once, and the store loops take other rows'
 // destination addresses from their owners by shuffle.
 __device__ __forceinline__ void epilogue_qkv(const TcQkv &p, uint32_t *stg, int lane, uint32_t taddr,
-                                             int row0, int M, int head, const AccRelease *rel) {
+                                             int row0, int M, int head, const AccRelease *rel,
+                                             const uint16_t *norm_w) {
     const int m = row0 + lane;
     const bool row_ok = m < M;
     const int mc = row_ok ? m : M - 1;
     const int pos = p.tok_pos[mc];
     const bool normed = head < 24;
-    const uint16_t *w = head < 16 ? p.q_norm : p.k_norm;
+    // norm weights staged in shared memory at kernel start (the rope-table
+    // stream would evict them from L1 between chunks)
+    const uint16_t *w = head < 16 ? norm_w : norm_w + 128;
     uint16_t *dst_row;                     // column 0 of this head in the destination row
     if (head < 16) {
         dst_row = p.q_bf16 + (size_t)mc * p.ldq + head * 128;
@@ -227,15 +243,25 @@ __device__ __forceinline__ void epilogue_qkv(const TcQkv &p, uint32_t *stg, int 
         dst_row = cache + (slot * p.max_len + pos) * 128;
     }
     if (!row_ok) dst_row = nullptr;
+    // (cos, sin) of this row's position for rotation pairs 16c .. 16c + 15:
+    // 8 float4 per chunk from the L2-resident table. Chunk c + 1 is loaded
+    // while chunk c is computed (and chunk 0 during the sum of squares), so
+    // the L2 latency stays off the critical path.
+    const float4 *cs_row = (const float4 *)(p.rope + (size_t)pos * 64);
+    float4 cs_next[8];
+    if (normed) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) cs_next[e] = __ldg(cs_row + e);
+    }
     float scale = 1.f;
     if (normed) {
         float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll 1
-        for (int c = 0; c < 8; c++) {
-            float v[16];
-            load_chunk16(taddr + 16 * c, v);
+        for (int c = 0; c < 4; c++) {
+            float v[32];
+            load_chunk(taddr + 32 * c, v);
 #pragma unroll
-            for (int j = 0; j < 16; j += 4) {
+            for (int j = 0; j < 32; j += 4) {
                 s0 = fmaf(v[j], v[j], s0);
                 s1 = fmaf(v[j + 1], v[j + 1], s1);
                 s2 = fmaf(v[j + 2], v[j + 2], s2);
@@ -252,17 +278,23 @@ __device__ __forceinline__ void epilogue_qkv(const TcQkv &p, uint32_t *stg, int 
         load_chunk16(taddr + 64 + 16 * c, b);
         if (c == 3 && rel) acc_release(*rel, lane);
         if (normed) {
-            // 16-byte loads: 2 (cos, sin) pairs, 8 norm weights per load.
-            const float4 *cs4 = (const float4 *)(p.rope + (size_t)pos * 64 + 16 * c);
+            float4 cs4[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) cs4[e] = cs_next[e];
+            if (c < 3) {
+#pragma unroll
+                for (int e = 0; e < 8; e++) cs_next[e] = __ldg(cs_row + 8 * (c + 1) + e);
+            }
+            // 8 norm weights per 16-byte shared load
             const uint4 *w_lo = (const uint4 *)(w + 16 * c);
             const uint4 *w_hi = (const uint4 *)(w + 64 + 16 * c);
 #pragma unroll
             for (int j8 = 0; j8 < 2; j8++) {
-                const uint4 wl = __ldg(w_lo + j8), wh = __ldg(w_hi + j8);
+                const uint4 wl = w_lo[j8], wh = w_hi[j8];
                 const uint32_t wlw[4] = {wl.x, wl.y, wl.z, wl.w}, whw[4] = {wh.x, wh.y, wh.z, wh.w};
 #pragma unroll
                 for (int j2 = 0; j2 < 4; j2++) {
-                    const float4 t = __ldg(cs4 + j8 * 4 + j2);
+                    const float4 t = cs4[j8 * 4 + j2];
 #pragma unroll
                     for (int e = 0; e < 2; e++) {
                         const int j = j8 * 8 + j2 * 2 + e;
@@ -295,6 +327,102 @@ __device__ __forceinline__ void epilogue_qkv(const TcQkv &p, uint32_t *stg, int 
     }
 }
 
+// Half of the fused QKV epilogue for one head: this warp owns rotation pairs
+// 32*half .. 32*half + 31, i.e. TMEM columns 32*half.. and 64 + 32*half.. of the
+// head. The two halves of a row exchange partial sums of squares through
+// shared memory (xss, [parity][head][half][128 rows], parity alternating per
+// tile so a slot is rewritten only after the partner passed the next
+// barrier) behind the pair's 64-thread named barrier bar_id.
+__device__ __forceinline__ void epilogue_qkv_half(const TcQkv &p, uint32_t *stg, int lane, uint32_t taddr,
+                                                  int row0, int M, int head, const AccRelease *rel,
+                                                  const uint16_t *norm_w, int half, int hh, int qrow,
+                                                  float *xss, int parity, int bar_id) {
+    const int m = row0 + lane;
+    const bool row_ok = m < M;
+    const int mc = row_ok ? m : M - 1;
+    const int pos = p.tok_pos[mc];
+    const bool normed = head < 24;
+    const uint16_t *w = head < 16 ? norm_w : norm_w + 128;
+    uint16_t *dst_row;
+    if (head < 16) {
+        dst_row = p.q_bf16 + (size_t)mc * p.ldq + head * 128;
+    } else {
+        const int kvh = (head - 16) & 7;
+        uint16_t *cache = head < 24 ? p.kc : p.vc;
+        const size_t slot = ((size_t)p.tok_seq[mc] * 28 + p.layer) * 8 + kvh;
+        dst_row = cache + (slot * p.max_len + pos) * 128;
+    }
+    if (!row_ok) dst_row = nullptr;
+    const float4 *cs_row = (const float4 *)(p.rope + (size_t)pos * 64) + 16 * half;
+    float scale = 1.f;
+    if (normed) {
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 2; c++) {
+            float v[32];
+            load_chunk(taddr + 64 * c + 32 * half, v);
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+                s0 = fmaf(v[j], v[j], s0);
+                s1 = fmaf(v[j + 1], v[j + 1], s1);
+                s2 = fmaf(v[j + 2], v[j + 2], s2);
+                s3 = fmaf(v[j + 3], v[j + 3], s3);
+            }
+        }
+        float *x = xss + ((parity * 2 + hh) * 2) * 128 + qrow;
+        x[half * 128] = (s0 + s1) + (s2 + s3);
+        asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+        const float ss = x[0] + x[128];
+        scale = 1.0f / sqrtf(ss / 128.0f + p.eps);
+    }
+#pragma unroll 1
+    for (int c = 0; c < 2; c++) {
+        // rotation pairs (32*half + 16c + j, 64 + 32*half + 16c + j), j < 16
+        const int col = 32 * half + 16 * c;
+        float a[16], b[16];
+        load_chunk16(taddr + col, a);
+        load_chunk16(taddr + 64 + col, b);
+        if (c == 1 && rel) acc_release(*rel, lane);
+        if (normed) {
+            const uint4 *w_lo = (const uint4 *)(w + col);
+            const uint4 *w_hi = (const uint4 *)(w + 64 + col);
+#pragma unroll
+            for (int j8 = 0; j8 < 2; j8++) {
+                const uint4 wl = w_lo[j8], wh = w_hi[j8];
+                const uint32_t wlw[4] = {wl.x, wl.y, wl.z, wl.w}, whw[4] = {wh.x, wh.y, wh.z, wh.w};
+#pragma unroll
+                for (int j2 = 0; j2 < 4; j2++) {
+                    const float4 t = __ldg(cs_row + 8 * c + j8 * 4 + j2);
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const int j = j8 * 8 + j2 * 2 + e;
+                        const float wa = __uint_as_float(e ? (wlw[j2] & 0xFFFF0000u) : (wlw[j2] << 16));
+                        const float wb = __uint_as_float(e ? (whw[j2] & 0xFFFF0000u) : (whw[j2] << 16));
+                        const float cs = e ? t.z : t.x, sn = e ? t.w : t.y;
+                        const float x0 = a[j] * scale * wa;
+                        const float x1 = b[j] * scale * wb;
+                        a[j] = x0 * cs - x1 * sn;
+                        b[j] = x1 * cs + x0 * sn;
+                    }
+                }
+            }
+        }
+        // dims col.. to the first staging tile, 64 + col.. to the second
+        stage_bf16_16(stg, lane, c, 0, a);
+        stage_bf16_16(stg, lane, c, 16, b);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int hi = 0; hi < 2; hi++) {
+        const int d0 = 32 * half + 64 * hi;
+        flush_bf16(stg, lane, [&](int r) -> uint16_t * {
+            uint16_t *d = (uint16_t *)__shfl_sync(0xFFFFFFFFu, (unsigned long long)dst_row, r);
+            return d ? d + d0 : nullptr;
+        }, 0, 32, true, hi ? 16 : 0);
+    }
+    __syncwarp();
+}
+
 template <int BN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(TcCfg<BN, tc_epi_warps(BN, EPI)>::THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -322,6 +450,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
     uint64_t *tempty = tfull + 2;           // [2]
     uint64_t *done = tempty + 2;            // [1] MMA drain at exit
     uint32_t *tmem_slot = (uint32_t *)(done + 1);
+    uint16_t *norm_w = (uint16_t *)((uint8_t *)full + 256);   // [q_norm 128 | k_norm 128]
+    float *xss = (float *)((uint8_t *)full + 768);              // QKV sum-of-squares exchange
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -347,6 +477,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
         }
         mbar_init(done, 1);
         fence_mbar_init();
+    }
+    if (EPI == TC_EPI_QKV_ROPE && warp >= 2 && threadIdx.x - 64 < 32) {
+        // 32 threads copy the two norm weight vectors (2 x 256 B) once
+        const int i = threadIdx.x - 64;
+        ((uint4 *)norm_w)[i] = i < 16 ? ((const uint4 *)ep.qkv.q_norm)[i]
+                                      : ((const uint4 *)ep.qkv.k_norm)[i - 16];
     }
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmA);
@@ -466,6 +602,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
         const int q = warp & 3;                 // TMEM lane quarter of this warp
         uint32_t *stg = (uint32_t *)(base + STAGES * Cfg::STAGE_BYTES) + (warp - 2) * STG * 32 * 32;
         int chunks = 0;                          // residual chunks handed to the TMA
+        int ab_tiles = 0;                        // tiles drained (QKV exchange parity)
         int ab = 0;
         uint32_t aphase = 0;
         for (int u = u0; u < total; u += ustep) {
@@ -499,15 +636,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     __syncwarp();
                 }
             } else if (EPI == TC_EPI_QKV_ROPE) {
-                if (NEPI == 8) {
-                    // warps 2-5: first head of the tile, warps 6-9: second
-                    const int hh = (warp - 2) >> 2;
-                    epilogue_qkv(ep.qkv, stg, lane, taddr + hh * 128, row0, M, nb * 2 + hh, &rel);
+                if (NEPI == 16) {
+                    // warps 2-9: first head of the tile, 10-17: second; within
+                    // a head, warps 2-5 / 10-13 take rotation pairs 0-31 and
+                    // 6-9 / 14-17 pairs 32-63 of their lane quarter
+                    const int sw = warp - 2;
+                    const int hh = sw >> 3, half = (sw >> 2) & 1;
+                    epilogue_qkv_half(ep.qkv, stg, lane, taddr + hh * 128, row0, M, nb * 2 + hh, &rel,
+                                      norm_w, half, hh, q * 32 + lane, xss, ab_tiles & 1,
+                                      1 + hh * 4 + q);
+                    ab_tiles++;
                 } else {
 #pragma unroll 1
                     for (int hh = 0; hh < BN / 128; hh++)
                         epilogue_qkv(ep.qkv, stg, lane, taddr + hh * 128, row0, M,
-                                     nb * (BN / 128) + hh, hh + 1 == BN / 128 ? &rel : nullptr);
+                                     nb * (BN / 128) + hh, hh + 1 == BN / 128 ? &rel : nullptr, norm_w);
                 }
             } else if (SILU) {
 #pragma unroll 1
