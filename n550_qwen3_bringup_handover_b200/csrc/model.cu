@@ -81,7 +81,10 @@ size_t tensor_elems(int idx, bool *is_norm) {
 }
 
 // Header checks in the order of qwen3_init (qwen3.c:93-146), same codes.
-int parse_qw3m(const uint8_t *b, size_t size, size_t *offs) {
+// Layouts: ROW, or TILE with 128 x 32 tiles -- the two the reference's
+// qwen3_set_weight_layout accepts with the AME kernel (kernels_ame.c:188-207);
+// *tiled reports which.
+int parse_qw3m(const uint8_t *b, size_t size, size_t *offs, bool *tiled = nullptr) {
     if (size < 256) return N550_ERR_SIZE;
     if (b[0] != 'Q' || b[1] != 'W' || b[2] != '3' || b[3] != 'M') return N550_ERR_MAGIC;
     if (rd_i32(b + 4) != 1) return N550_ERR_VERSION;
@@ -92,7 +95,10 @@ int parse_qw3m(const uint8_t *b, size_t size, size_t *offs) {
         return N550_ERR_SHAPE;
     const int align = rd_i32(b + 72);
     if (align < 128 || (align & (align - 1)) != 0) return N550_ERR_SHAPE;
-    if (rd_i32(b + 76) != N550_LAYOUT_ROW) return N550_ERR_LAYOUT;
+    const int layout = rd_i32(b + 76);
+    const bool tile = layout == N550_LAYOUT_TILE && rd_i32(b + 80) == 128 && rd_i32(b + 84) == 32;
+    if (layout != N550_LAYOUT_ROW && !tile) return N550_ERR_LAYOUT;
+    if (tiled) *tiled = tile;
     if (rd_f32(b + 48) != 1000000.0f) return N550_ERR_SHAPE;
     if (rd_f32(b + 52) != 1e-06f) return N550_ERR_SHAPE;
     size_t pos = (size_t)(uint32_t)rd_i32(b + 68);
@@ -106,6 +112,33 @@ int parse_qw3m(const uint8_t *b, size_t size, size_t *offs) {
     }
     if (pos != size) return N550_ERR_SIZE;
     return N550_OK;
+}
+
+// True for the per-layer GEMM weights (q, k, v, o, gate, up, down), the
+// tensors a tile-major export re-arranges; embed_tokens and the norms stay
+// row-major (GET_WEIGHTS.md of the reference's L4 demo).
+bool is_gemm_weight(int idx, int *N, int *K) {
+    if (idx == 0 || idx == N_TENSORS - 1) return false;
+    switch ((idx - 1) % 11) {
+    case 1: *N = QD; *K = H; return true;
+    case 2: case 3: *N = KVD; *K = H; return true;
+    case 6: *N = H; *K = QD; return true;
+    case 8: case 9: *N = INTER; *K = H; return true;
+    case 10: *N = H; *K = INTER; return true;
+    default: return false;
+    }
+}
+
+// Tile-major [N/128][K/32][128][32] -> row-major [N][K] (the element offset of
+// tile (n0, k0) is ((n0/128)*(K/32) + k0/32) * 4096, kernels_ame.c:212-215).
+__global__ void untile_weight_kernel(uint16_t *__restrict__ dst, const uint16_t *__restrict__ src,
+                                     int N, int K) {
+    const size_t total = (size_t)N * K;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const int n = (int)(i / K), k = (int)(i % K);
+        dst[i] = src[((size_t)(n >> 7) * (K >> 5) + (k >> 5)) * 4096 + (n & 127) * 32 + (k & 31)];
+    }
 }
 
 // The random-init blob header: the fields a QW3M exporter writes for
@@ -743,7 +776,8 @@ int n550_qwen3_init(n550_model_t **out, const void *blob, size_t blob_size,
     if (rc) return rc;
     n550_model *m = new n550_model();
     m->cfg = *cfg;
-    rc = parse_qw3m((const uint8_t *)blob, blob_size, m->off);
+    bool tiled = false;
+    rc = parse_qw3m((const uint8_t *)blob, blob_size, m->off, &tiled);
     if (rc) { model_release(m); return rc; }
     cudaGetDevice(&m->dev);
     m->blob_size = blob_size;
@@ -751,6 +785,26 @@ int n550_qwen3_init(n550_model_t **out, const void *blob, size_t blob_size,
     if (cudaMemcpy(m->blob, blob, blob_size, cudaMemcpyHostToDevice) != cudaSuccess) {
         model_release(m);
         return N550_ERR_CUDA;
+    }
+    if (tiled) {
+        // Tile-major GEMM weights are put back into row-major order in place
+        // (through a scratch copy), so every kernel sees one layout.
+        uint16_t *tmp = nullptr;
+        if (cudaMalloc(&tmp, (size_t)INTER * H * 2) != cudaSuccess) { model_release(m); return N550_ERR_OOM; }
+        for (int t = 0; t < N_TENSORS && !rc; t++) {
+            int N = 0, K = 0;
+            if (!is_gemm_weight(t, &N, &K)) continue;
+            uint16_t *w = (uint16_t *)(m->blob + m->off[t]);
+            if (cudaMemcpy(tmp, w, (size_t)N * K * 2, cudaMemcpyDeviceToDevice) != cudaSuccess) {
+                rc = N550_ERR_CUDA;
+                break;
+            }
+            untile_weight_kernel<<<1184, 256>>>(w, tmp, N, K);
+            if (cudaGetLastError() != cudaSuccess) rc = N550_ERR_CUDA;
+        }
+        if (!rc && cudaDeviceSynchronize() != cudaSuccess) rc = N550_ERR_CUDA;
+        cudaFree(tmp);
+        if (rc) { model_release(m); return rc; }
     }
     rc = model_setup(m);
     if (rc) { model_release(m); return rc; }

@@ -16,11 +16,11 @@ def header(**over):
     h[:4] = np.frombuffer(b"QW3M", np.uint8)
     vals = dict(version=1, hidden=1024, inter=3072, layers=28, heads=16, kv=8, hd=128,
                 vocab=151936, max_pos=40960, tie=1, dtype=1, bos=151643, eos0=151645,
-                eos1=151643, data_start=256, align=128, layout=0)
+                eos1=151643, data_start=256, align=128, layout=0, tile_n=0, tile_k=0)
     vals.update(over)
     off = dict(version=4, hidden=8, inter=12, layers=16, heads=20, kv=24, hd=28, vocab=32,
                max_pos=36, tie=40, dtype=44, bos=56, eos0=60, eos1=64, data_start=68,
-               align=72, layout=76)
+               align=72, layout=76, tile_n=80, tile_k=84)
     for k, o in off.items():
         h[o:o + 4] = np.frombuffer(np.int32(vals[k]).tobytes(), np.uint8)
     h[48:52] = np.frombuffer(np.float32(over.get("theta", 1000000.0)).tobytes(), np.uint8)
@@ -43,7 +43,10 @@ def init_status(blob, size=None):
     (dict(vocab=151000), n5.ERR_SHAPE),
     (dict(align=96), n5.ERR_SHAPE),
     (dict(align=64), n5.ERR_SHAPE),
-    (dict(layout=1), n5.ERR_LAYOUT),
+    (dict(layout=1), n5.ERR_LAYOUT),             # tile-major without a tile shape
+    (dict(layout=1, tile_n=64, tile_k=32), n5.ERR_LAYOUT),
+    (dict(layout=2, tile_n=128, tile_k=32), n5.ERR_LAYOUT),
+    (dict(layout=1, tile_n=128, tile_k=32, align=4096), n5.ERR_SIZE),   # accepted; header only
     (dict(theta=10000.0), n5.ERR_SHAPE),
     (dict(eps=1e-5), n5.ERR_SHAPE),
 ])

@@ -86,6 +86,50 @@ def test_init_from_blob_matches_random_init(cuda, blob):
     assert np.array_equal(a, b)
 
 
+def tile_major_blob(row_blob):
+    """The same weights exported tile-major (the reference's --layout tile):
+    every GEMM weight as 128 x 32 tiles in (n_tile, k_tile) order, tensors
+    aligned to 4096 bytes; embed_tokens and the norms stay row-major."""
+    shapes = [(151936, 1024)]
+    for _ in range(28):
+        shapes += [(1024,), (2048, 1024), (1024, 1024), (1024, 1024), (128,), (128,), (1024, 2048),
+                   (1024,), (3072, 1024), (3072, 1024), (1024, 3072)]
+    shapes += [(1024,)]
+    parts, pos, src = [], 256, 256
+    for t, shp in enumerate(shapes):
+        n = int(np.prod(shp))
+        w = row_blob[src:src + 2 * n].view(np.uint16)
+        src += 2 * n
+        if len(shp) == 2 and t != 0:
+            N, K = shp
+            w = w.reshape(N // 128, 128, K // 32, 32).transpose(0, 2, 1, 3).reshape(-1)
+        pad = (-pos) % 4096
+        parts.append(np.zeros(pad, np.uint8))
+        parts.append(np.ascontiguousarray(w).view(np.uint8))
+        pos += pad + 2 * n
+    hdr = row_blob[:256].copy()
+    for off, v in ((72, 4096), (76, 1), (80, 128), (84, 32)):
+        hdr[off:off + 4] = np.frombuffer(np.int32(v).tobytes(), np.uint8)
+    return np.concatenate([hdr] + parts)
+
+
+def test_tile_major_blob_loads_to_the_same_model(cuda, blob):
+    """A tile-major QW3M file (qwen3_set_weight_layout(TILE, 128, 32) in the
+    reference) is un-tiled on the device at load: the weights and the logits
+    are bit-identical to the row-major file's."""
+    tiled = tile_major_blob(blob)
+    toks = oracle.synth_tokens(8, 4, 0x544F4B)
+    mt = n5.Model(blob=tiled, max_seqs=1, max_len=64, max_tokens=64)
+    mr = n5.Model(blob=blob, max_seqs=1, max_len=64, max_tokens=64)
+    try:
+        for t in (0, 1, 2, 3, 4, 7, 9, 10, 11, 300, 308, 309):
+            assert np.array_equal(mt.weight_bits(t), mr.weight_bits(t)), t
+        assert np.array_equal(mt.forward_batch(toks, 0)[1], mr.forward_batch(toks, 0)[1])
+    finally:
+        mt.close()
+        mr.close()
+
+
 def test_prefill_and_decode_logits_vs_reference(model, blob):
     toks = oracle.synth_tokens(16, 1, 0x544F4B)
     ref = ref_model(blob)
