@@ -652,6 +652,29 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         epilogue_qkv(ep.qkv, stg, lane, taddr + hh * 128, row0, M,
                                      nb * (BN / 128) + hh, hh + 1 == BN / 128 ? &rel : nullptr, norm_w);
                 }
+            } else if (EPI == TC_EPI_ARGMAX) {
+                // running (max, lowest column of the max) of this row over the
+                // tile's columns, in increasing column order
+                float bv = -INFINITY;
+                int bi = 0x7FFFFFFF;
+#pragma unroll 1
+                for (int cch = 0; cch < BN; cch += 32) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(taddr + cch, r);
+                    tmem_ld_wait();
+                    if (cch + 32 == BN) acc_release(rel, lane);
+                    const int n0 = nb * BN + cch;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const float v = __uint_as_float(r[j]);
+                        if (n0 + j < N && (v > bv || (v == bv && n0 + j < bi))) { bv = v; bi = n0 + j; }
+                    }
+                }
+                const int m = row0 + lane;
+                if (m < M) {
+                    ep.amax[(size_t)m * ep.an + nb] = bv;
+                    ep.aidx[(size_t)m * ep.an + nb] = bi;
+                }
             } else if (SILU) {
 #pragma unroll 1
                 for (int cch = 0; cch < OUT_N; cch += 32) {
@@ -1060,6 +1083,63 @@ int launch_gemm_tc_splitk(cudaStream_t st, int epi, const uint16_t *a, int lda, 
     int rc = launch_gemm_tc_partials(st, pe, a, lda, b, ldb, b2, M, N, K, ws, ws_bytes, &got);
     if (rc) return rc;
     return launch_splitk_reduce(st, epi, ws, got, M, N, c, ldc);
+}
+
+namespace {
+// Merge the per-tile (max, index) pairs of a row (tiles in increasing column
+// order): larger value wins, ties keep the lower index; a row whose values
+// are all -inf or NaN gives index 0 (qwen3_op_argmax returns 0 there).
+__global__ void __launch_bounds__(256)
+argmax_tiles_kernel(const float *__restrict__ amax, const int32_t *__restrict__ aidx, int an,
+                    int32_t *idx) {
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    const float *rv = amax + (size_t)blockIdx.x * an;
+    const int32_t *ri = aidx + (size_t)blockIdx.x * an;
+    float bv = -INFINITY;
+    int bi = 0x7FFFFFFF;
+    for (int t = threadIdx.x; t < an; t += 256) {
+        const float v = rv[t];
+        const int i = ri[t];
+        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+        const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 8; w++)
+            if (sv[w] > sv[0] || (sv[w] == sv[0] && si[w] < si[0])) { sv[0] = sv[w]; si[0] = si[w]; }
+        idx[blockIdx.x] = si[0] == 0x7FFFFFFF ? 0 : si[0];
+    }
+}
+}  // namespace
+
+int launch_gemm_tc_argmax(cudaStream_t st, const uint16_t *a, int lda, const uint16_t *b, int ldb,
+                          int M, int N, int K, void *ws, size_t ws_bytes, int32_t *idx) {
+    if (M <= 0) return N550_OK;
+    if (N <= 0 || !idx) return N550_ERR_ARG;
+    if (!tc_shape_ok(a, lda, b, ldb, K)) return N550_ERR_UNSUPPORTED;
+    constexpr int BNA = 128;
+    const int an = (N + BNA - 1) / BNA;
+    if (!ws || ws_bytes < (size_t)M * an * 8 || ((uintptr_t)ws & 15)) return N550_ERR_ARG;
+    int rc = get_encoder();
+    if (rc) return rc;
+    CUtensorMap ta, tb;
+    if ((rc = make_tmap(&ta, a, M, K, lda, BM))) return rc;
+    if ((rc = make_tmap(&tb, b, N, K, ldb, BNA))) return rc;
+    TcEpilogue ep{};
+    ep.amax = (float *)ws;
+    ep.aidx = (int32_t *)((float *)ws + (size_t)M * an);
+    ep.an = an;
+    if ((rc = launch_impl<BNA, TC_EPI_ARGMAX>(st, ta, tb, tb, ep, M, N, K, 0))) return rc;
+    argmax_tiles_kernel<<<M, 256, 0, st>>>(ep.amax, ep.aidx, an, idx);
+    N550_LAUNCH_CHECK();
+    return N550_OK;
 }
 
 bool tc_shape_ok(const void *a, int lda, const void *b, int ldb, int K) {

@@ -12,7 +12,8 @@ enum {
     TC_EPI_BF16 = 1,       // C (BF16) = rne(acc)
     TC_EPI_RESID_F32 = 2,  // C (FP32) += acc           (residual add fused)
     TC_EPI_SILU_BF16 = 3,  // C (BF16) = silu(acc_gate) * acc_up (SwiGLU fused)
-    TC_EPI_QKV_ROPE = 4    // per-head RMSNorm + RoPE of q/k, q out, k/v into the KV cache
+    TC_EPI_QKV_ROPE = 4,   // per-head RMSNorm + RoPE of q/k, q out, k/v into the KV cache
+    TC_EPI_ARGMAX = 5      // per row and tile: (max, lowest index of the max), no C written
 };
 
 // Operands of the fused QKV epilogue (qwen3.c:477-511): a 128-column tile is
@@ -34,6 +35,9 @@ struct TcEpilogue {
     int vec_ok;            // 16-byte vector stores allowed
     int tma_resid;         // TC_EPI_RESID_F32 through TMA reduce-adds (C map given)
     TcQkv qkv;
+    float *amax;           // TC_EPI_ARGMAX: [M][an] best value per row and N tile
+    int32_t *aidx;         //                [M][an] its column
+    int an;                //                number of N tiles
 };
 
 // Tile width (BN) used by the fast GEMMs for an M x N output: 128 or 256;
@@ -72,6 +76,15 @@ int launch_splitk_reduce(cudaStream_t st, int epi, const float *ws, int ks, int 
                          int ldc);
 // Number of K slices launch_gemm_tc_splitk uses (1 = no split).
 int tc_splitk_plan(int M, int N, int K, int epi, int bn, int *kt_per);
+
+// lm_head + argmax (qwen3.c:547-573 followed by qwen3_op_argmax): C = A . B^T
+// is never written; each 128-column tile leaves (max, lowest index of the max)
+// per row in amax/aidx ([M][ceil(N/128)], ws of at least M * ceil(N/128) * 8
+// bytes), then one kernel merges the tiles into idx[M] with the rule of
+// qwen3_op_argmax (first index of the maximum; rows without a finite maximum
+// give 0).
+int launch_gemm_tc_argmax(cudaStream_t st, const uint16_t *a, int lda, const uint16_t *b, int ldb,
+                          int M, int N, int K, void *ws, size_t ws_bytes, int32_t *idx);
 
 // The QKV projection with the fused per-head epilogue (N = 4096, BN = 128).
 int launch_gemm_tc_qkv(cudaStream_t st, const uint16_t *a, int lda, const uint16_t *w,

@@ -753,11 +753,20 @@ int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t
 }
 
 // Last-token logits and argmax for Sc sequences whose rows are i*Lc + Lc - 1.
+// logits == nullptr: the caller wants only the next tokens. In fast mode the
+// lm_head GEMM then carries the argmax in its epilogue (per-tile maxima merged
+// by one small kernel) and the [Sc, 151936] FP32 logits are never written.
 int run_head(n550_model *m, cudaStream_t st, int Sc, int Lc, float *logits, int32_t *next,
              bool xl_ready = false) {
     int rc = N550_OK;
     if (!xl_ready)
         STEP(N550_PROF_RMSNORM, 1, launch_final_norm(st, m->xl, m->x, m->t[N_TENSORS - 1], Sc, Lc));
+    if (!logits && next && m->cfg.gemm_mode == N550_MODE_FAST && Sc > 8) {
+        STEP(N550_PROF_GEMM_LMHEAD, 2,
+             launch_gemm_tc_argmax(st, m->xl, H, m->t[0], H, Sc, VOCAB, H, m->ws, m->ws_bytes, next));
+        return N550_OK;
+    }
+    if (!logits) logits = m->logits;
     STEP(N550_PROF_GEMM_LMHEAD, 1,
          mgemm(m, st, TC_EPI_F32, m->xl, H, m->t[0], nullptr, logits, VOCAB, Sc, VOCAB, H));
     if (next) STEP(N550_PROF_OTHER, 1, launch_argmax(st, logits, Sc, VOCAB, VOCAB, next));
@@ -931,7 +940,7 @@ static int prefill_eager(n550_model_t *m, cudaStream_t st, const int32_t *tokens
             bool xl_ready = false;
             if ((rc = run_layers(m, st, T, false, seq_ids + s0, nullptr, Sc, Lc, p0, &xl_ready))) return rc;
             if (j0 + Lc == seq_len) {
-                float *lg = logits ? logits + (size_t)s0 * VOCAB : m->logits;
+                float *lg = logits ? logits + (size_t)s0 * VOCAB : nullptr;
                 if ((rc = run_head(m, st, Sc, Lc, lg, next_token ? next_token + s0 : nullptr)))
                     return rc;
             }
@@ -957,7 +966,7 @@ int n550_qwen3_decode(n550_model_t *m, void *stream, const int32_t *tokens, cons
     bool xl_ready = false;
     int rc = run_layers(m, st, n_seqs, true, seq_ids, pos, n_seqs, 1, 0, &xl_ready);
     if (rc) return rc;
-    return run_head(m, st, n_seqs, 1, logits ? logits : m->logits, next_token, xl_ready);
+    return run_head(m, st, n_seqs, 1, logits, next_token, xl_ready);
 }
 
 int n550_qwen3_decode_steps(n550_model_t *m, void *stream, int32_t *tokens, const int32_t *seq_ids,

@@ -331,6 +331,36 @@ def test_prefill_tile_shapes_agree(cuda, tile):
         assert same_choice(int(out[tile][1][s]), out[0][0][s])
 
 
+def test_fused_lm_head_argmax_matches_logits_argmax(cuda):
+    """Without a logits buffer (fast mode, more than 8 rows) the lm_head GEMM
+    carries the argmax in its epilogue and never writes the logits; the next
+    tokens are identical to the argmax of the materialised logits, in prefill
+    and in decode."""
+    import torch
+    S, L = 12, 40
+    toks = torch.from_numpy(oracle.synth_tokens(S * L, 31, 0x544F4B).reshape(S, L)).cuda()
+    seq = torch.arange(S, dtype=torch.int32, device="cuda")
+    m = n5.Model(seed=0, max_seqs=S, max_len=L + 4, max_tokens=S * L)
+    try:
+        lg = torch.empty((S, 151936), dtype=torch.float32, device="cuda")
+        a = torch.empty(S, dtype=torch.int32, device="cuda")
+        b = torch.empty(S, dtype=torch.int32, device="cuda")
+        m.prefill(toks, seq, 0, lg, a)
+        m.prefill(toks, seq, 0, None, b)
+        torch.cuda.synchronize()
+        assert torch.equal(a, b)
+        assert torch.equal(a.long(), lg.argmax(dim=1))
+        pos = torch.full((S,), L, dtype=torch.int32, device="cuda")
+        m.decode(a.clone(), seq, pos, lg, a)
+        m.decode(b.clone(), seq, pos, None, b)
+        torch.cuda.synchronize()
+        assert torch.equal(a, b)
+        assert torch.equal(a.long(), lg.argmax(dim=1))
+    finally:
+        m.close()
+    assert n5.device_status() == n5.OK
+
+
 def test_decode_steps_graph_replay_matches_eager(cuda):
     """n550_qwen3_decode_steps: the CUDA-graph replay of a decode step gives
     exactly the ids, tokens and positions of the eager loop."""
