@@ -151,6 +151,15 @@ int n550_gemm_f32a_noalloc(void *stream, const float *a, int lda,
  * not depend on it beyond FP32 summation order. */
 int n550_gemm_tile_config(int bn);
 
+/* Programmatic dependent launch (default on): every kernel of the library is
+ * launched so that it may start while the previous kernel of its stream
+ * finishes -- its launch, barrier/TMEM setup and weight loads overlap that
+ * kernel's tail, and it waits for the previous kernels' results before
+ * touching them. 0 launches with plain stream order. Results are identical
+ * either way; a profiling knob. Applies to launches made (and CUDA graphs
+ * captured) after the call. */
+int n550_set_pdl(int on);
+
 /* Fused fast-mode GEMMs of the decoder layer (A BF16, weights BF16 [N,K]):
  *   n550_gemm_residual: x[M,N] += A . B^T in FP32 -- qwen3_gemm followed by
  *     qwen3_op_residual_add (qwen3.c:520-523, 540-543);

@@ -14,6 +14,7 @@
 // tensor cores (attn_prefill_tc.cu).
 #include "attention.h"
 #include "common.cuh"
+#include "launch.h"
 
 namespace n550 {
 namespace {
@@ -59,6 +60,8 @@ attn_decode_kernel(AttnDecodeArgs p) {
     __shared__ float wm[DC_WARPS][2], wl[DC_WARPS][2];
     __shared__ __align__(16) float wo[DC_WARPS][2][HD];
 
+    dep_wait();
+    dep_launch();
     const int split = blockIdx.x, kvh = blockIdx.y, s = blockIdx.z;
     const int seq = p.seq_ids[s];
     const int kv_len = p.pos[s] + 1;
@@ -213,6 +216,8 @@ attn_decode_kernel(AttnDecodeArgs p) {
 }
 
 __global__ void attn_combine_kernel(AttnDecodeArgs p) {
+    dep_wait();
+    dep_launch();
     const int head = blockIdx.x, s = blockIdx.y, d = threadIdx.x;
     const size_t slot0 = ((size_t)s * 16 + head) * p.splits;
     float M = -INFINITY;
@@ -252,10 +257,10 @@ int launch_attn_decode(cudaStream_t st, const AttnDecodeArgs &a, int n_seqs) {
         dc_attr[dev] = true;
     }
     dim3 grid(a.splits, NKV, n_seqs);
-    attn_decode_kernel<<<grid, DC_THREADS, DC_SMEM, st>>>(a);
+    N550_CUDA_TRY(launch_k(attn_decode_kernel, grid, DC_THREADS, DC_SMEM, st, a));
     N550_LAUNCH_CHECK();
     if (a.splits > 1) {
-        attn_combine_kernel<<<dim3(16, n_seqs), HD, 0, st>>>(a);
+        N550_CUDA_TRY(launch_k(attn_combine_kernel, dim3(16, n_seqs), HD, 0, st, a));
         N550_LAUNCH_CHECK();
     }
     return N550_OK;

@@ -31,6 +31,7 @@
 
 #include "attention.h"
 #include "common.cuh"
+#include "launch.h"
 #include "tmap.h"
 
 namespace n550 {
@@ -161,6 +162,10 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // the TMEM is held: the next kernel may start; q and the cache come from
+    // the previous kernels
+    dep_launch();
+    dep_wait();
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
@@ -489,7 +494,7 @@ int launch_attn_prefill(cudaStream_t st, const AttnPrefillArgs &a, int n_seqs) {
     N550_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     // persistent: one CTA per SM walks the items
     const int grid = p.n_items < sms ? p.n_items : sms;
-    attn_prefill_tc_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(tq, tk, tv, p);
+    N550_CUDA_TRY(launch_k(attn_prefill_tc_kernel, grid, THREADS, SMEM_BYTES, st, tq, tk, tv, p));
     N550_LAUNCH_CHECK();
     return N550_OK;
 }

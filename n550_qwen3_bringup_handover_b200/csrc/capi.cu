@@ -6,6 +6,7 @@
 #include "attention.h"
 #include "common.cuh"
 #include "gemm_tc.h"
+#include "launch.h"
 #include "ops.h"
 #include "synth.cuh"
 
@@ -356,6 +357,11 @@ int n550_gemm(void *stream, int mode, int kblock, const void *a, int a_type, int
 int n550_gemm_tile_config(int bn) {
     if (bn != 0 && bn != 128 && bn != 256 && bn != 512) return N550_ERR_ARG;
     g_tile_bn = bn;
+    return N550_OK;
+}
+
+int n550_set_pdl(int on) {
+    g_pdl = on != 0;
     return N550_OK;
 }
 

@@ -43,6 +43,20 @@ __device__ __forceinline__ void report_timeout() {
 constexpr long long kWaitCycles = 2000000000ll;
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch. Kernels launched by launch_k() (launch.h)
+// may start while the previous kernel of the stream is still running:
+// dep_wait() blocks until every earlier grid has completed and its memory is
+// visible, so it must precede the first access to any buffer another kernel
+// writes or reads (only weights, tensor maps and constant tables may be read
+// before it). dep_launch() lets the next kernel start its own prologue; in
+// kernels that allocate TMEM it comes after the allocation (a dependent CTA
+// on the same SM must not take the columns this CTA still waits for).
+// Both are no-ops for a kernel launched without the attribute.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
 // BF16 bit helpers (no dependency on cuda_bf16 operator overloads)
 // ---------------------------------------------------------------------------
 __host__ __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {

@@ -19,6 +19,7 @@
 // Non-finite inputs are unpinned by the reference; they are summed in IEEE
 // binary64.
 #include "common.cuh"
+#include "launch.h"
 
 namespace n550 {
 
@@ -136,6 +137,8 @@ __global__ void __launch_bounds__(THREADS)
 gemm_exact_kernel(const void *__restrict__ a_ptr, int lda,
                   const uint16_t *__restrict__ b, int ldb,
                   float *__restrict__ c, int ldc, int M, int N, int K, int kblock) {
+    dep_wait();
+    dep_launch();
     __shared__ float As[MAXKB][TILE];
     __shared__ float Bs[MAXKB][TILE];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -235,13 +238,9 @@ int launch_gemm_exact(cudaStream_t st, const void *a, int a_type, int lda,
     const long long gy = (M + TILE - 1) / TILE, gx = (N + TILE - 1) / TILE;
     if (gy > 65535 || gx > 0x7FFFFFFF) return N550_ERR_UNSUPPORTED;
     dim3 grid((unsigned)gx, (unsigned)gy);
-    if (a_type == N550_F32)
-        gemm_exact_kernel<true><<<grid, THREADS, 0, st>>>(a, lda, b, ldb, c, ldc, M, N, K, kblock);
-    else if (a_type == N550_BF16)
-        gemm_exact_kernel<false><<<grid, THREADS, 0, st>>>(a, lda, b, ldb, c, ldc, M, N, K, kblock);
-    else
-        return N550_ERR_ARG;
-    N550_LAUNCH_CHECK();
+    if (a_type != N550_F32 && a_type != N550_BF16) return N550_ERR_ARG;
+    N550_CUDA_TRY(launch_k(a_type == N550_F32 ? gemm_exact_kernel<true> : gemm_exact_kernel<false>, grid,
+                           THREADS, 0, st, a, lda, b, ldb, c, ldc, M, N, K, kblock));
     return N550_OK;
 }
 

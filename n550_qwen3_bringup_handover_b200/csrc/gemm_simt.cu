@@ -8,6 +8,7 @@
 //  * f32_to_bf16: RNE staging of FP32 activations (kernels_ame.c:220-236).
 #include "common.cuh"
 #include "gemm_tc.h"
+#include "launch.h"
 
 namespace n550 {
 namespace {
@@ -25,6 +26,8 @@ template <int EPI>
 __global__ void __launch_bounds__(STHREADS)
 gemm_simt_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict__ b, int ldb,
                  void *c, int ldc, int M, int N, int K) {
+    dep_wait();
+    dep_launch();
     __shared__ float As[SK][ST + 1];
     __shared__ float Bs[SK][ST + 1];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -78,6 +81,8 @@ template <int MM, int EPI>
 __global__ void __launch_bounds__(GV_WARPS * 32)
 gemv_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict__ b, int ldb,
             void *c, int ldc, int N, int K) {
+    dep_wait();
+    dep_launch();
     const int lane = threadIdx.x & 31;
     const int n = blockIdx.x * GV_WARPS + (threadIdx.x >> 5);
     if (n >= N) return;
@@ -124,6 +129,8 @@ gemv_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict_
 
 __global__ void f32_to_bf16_kernel(uint16_t *out, int ldo, const float *in, int ldi,
                                    int rows, int cols) {
+    dep_wait();
+    dep_launch();
     const size_t total = (size_t)rows * cols;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
          i += (size_t)gridDim.x * blockDim.x) {
@@ -136,15 +143,15 @@ template <int MM>
 int gemv_dispatch(cudaStream_t st, int epi, const uint16_t *a, int lda, const uint16_t *b,
                   int ldb, void *c, int ldc, int N, int K) {
     const int grid = (N + GV_WARPS - 1) / GV_WARPS;
-    if (epi == TC_EPI_F32)
-        gemv_kernel<MM, TC_EPI_F32><<<grid, GV_WARPS * 32, 0, st>>>(a, lda, b, ldb, c, ldc, N, K);
-    else if (epi == TC_EPI_BF16)
-        gemv_kernel<MM, TC_EPI_BF16><<<grid, GV_WARPS * 32, 0, st>>>(a, lda, b, ldb, c, ldc, N, K);
-    else if (epi == TC_EPI_RESID_F32)
-        gemv_kernel<MM, TC_EPI_RESID_F32><<<grid, GV_WARPS * 32, 0, st>>>(a, lda, b, ldb, c, ldc, N, K);
-    else
-        return N550_ERR_ARG;
-    N550_LAUNCH_CHECK();
+    auto go = [&](auto kernel) {
+        return launch_k(kernel, grid, GV_WARPS * 32, 0, st, a, lda, b, ldb, c, ldc, N, K);
+    };
+    cudaError_t e;
+    if (epi == TC_EPI_F32) e = go(gemv_kernel<MM, TC_EPI_F32>);
+    else if (epi == TC_EPI_BF16) e = go(gemv_kernel<MM, TC_EPI_BF16>);
+    else if (epi == TC_EPI_RESID_F32) e = go(gemv_kernel<MM, TC_EPI_RESID_F32>);
+    else return N550_ERR_ARG;
+    N550_CUDA_TRY(e);
     return N550_OK;
 }
 
@@ -156,15 +163,15 @@ int launch_gemm_simt(cudaStream_t st, int epi, const uint16_t *a, int lda,
     const long long gy = (M + ST - 1) / ST;
     if (gy > 65535) return N550_ERR_UNSUPPORTED;
     dim3 grid((N + ST - 1) / ST, (unsigned)gy);
-    if (epi == TC_EPI_F32)
-        gemm_simt_kernel<TC_EPI_F32><<<grid, STHREADS, 0, st>>>(a, lda, b, ldb, c, ldc, M, N, K);
-    else if (epi == TC_EPI_BF16)
-        gemm_simt_kernel<TC_EPI_BF16><<<grid, STHREADS, 0, st>>>(a, lda, b, ldb, c, ldc, M, N, K);
-    else if (epi == TC_EPI_RESID_F32)
-        gemm_simt_kernel<TC_EPI_RESID_F32><<<grid, STHREADS, 0, st>>>(a, lda, b, ldb, c, ldc, M, N, K);
-    else
-        return N550_ERR_ARG;
-    N550_LAUNCH_CHECK();
+    auto go = [&](auto kernel) {
+        return launch_k(kernel, grid, STHREADS, 0, st, a, lda, b, ldb, c, ldc, M, N, K);
+    };
+    cudaError_t e;
+    if (epi == TC_EPI_F32) e = go(gemm_simt_kernel<TC_EPI_F32>);
+    else if (epi == TC_EPI_BF16) e = go(gemm_simt_kernel<TC_EPI_BF16>);
+    else if (epi == TC_EPI_RESID_F32) e = go(gemm_simt_kernel<TC_EPI_RESID_F32>);
+    else return N550_ERR_ARG;
+    N550_CUDA_TRY(e);
     return N550_OK;
 }
 
@@ -192,8 +199,7 @@ int launch_f32_to_bf16(cudaStream_t st, uint16_t *out, int ldo, const float *in,
     const size_t total = (size_t)rows * cols;
     int grid = (int)((total + 255) / 256);
     if (grid > 148 * 16) grid = 148 * 16;
-    f32_to_bf16_kernel<<<grid, 256, 0, st>>>(out, ldo, in, ldi, rows, cols);
-    N550_LAUNCH_CHECK();
+    N550_CUDA_TRY(launch_k(f32_to_bf16_kernel, grid, 256, 0, st, out, ldo, in, ldi, rows, cols));
     return N550_OK;
 }
 

@@ -24,6 +24,7 @@
 
 #include "common.cuh"
 #include "gemm_tc.h"
+#include "launch.h"
 #include "tmap.h"
 
 namespace n550 {
@@ -500,6 +501,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
     if (PAIR) cluster_sync();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // TMEM is held: the next kernel of the stream may start its prologue
+    dep_launch();
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
@@ -508,14 +511,45 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
+            // B is a weight operand that no kernel writes: the B tiles of the
+            // first ring pass are requested before waiting for the previous
+            // kernel, whose output A is.
+            auto load_b = [&](uint8_t *sB, int kt, int nb) {
+                if (SILU) {
+                    tma_load_2d(sB, &tmB, &full[stage], kt * BK, nb * (BN / 2));
+                    tma_load_2d(sB + (BN / 2) * BK * 2, &tmB2, &full[stage], kt * BK, nb * (BN / 2));
+                } else {
+                    tma_load_2d(sB, &tmB, &full[stage], kt * BK, nb * BN);
+                }
+            };
+            int pre = 0;
+            if (!PAIR && u0 < total) {
+                const int t = u0 / ksplit, sk = u0 - t * ksplit;
+                const int nb = m_fast ? t / num_m : t % num_n;
+                const int kt0 = sk * kt_per, kt1 = min(num_k, kt0 + kt_per);
+                pre = min(kt1 - kt0, STAGES);
+                for (stage = 0; stage < pre; stage++) {
+                    mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+                    load_b(base + stage * Cfg::STAGE_BYTES + Cfg::A_BYTES, kt0 + stage, nb);
+                }
+                stage = 0;
+            }
+            dep_wait();
             for (int u = u0; u < total && ok; u += ustep) {
                 const int t = u / ksplit, sk = u - t * ksplit;
                 const int mb = m_fast ? t % num_m : t / num_n, nb = m_fast ? t / num_m : t % num_n;
                 const int kt0 = sk * kt_per, kt1 = min(num_k, kt0 + kt_per);
                 for (int kt = kt0; kt < kt1; kt++) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1)) { ok = false; break; }
                     uint8_t *sA = base + stage * Cfg::STAGE_BYTES;
                     uint8_t *sB = sA + Cfg::A_BYTES;
+                    if (issued < pre) {
+                        // first ring pass: the slot is free and B is on its way
+                        tma_load_2d(sA, &tmA, &full[stage], kt * BK, mb * BM);
+                        issued++;
+                        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                        continue;
+                    }
+                    if (!mbar_wait(&empty[stage], phase ^ 1)) { ok = false; break; }
                     if (PAIR) {
                         // both CTAs' bytes complete on the leader's barrier
                         const uint32_t cb = mapa_shared(smem_u32(&full[stage]), 0);
@@ -531,13 +565,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     }
                     mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
                     tma_load_2d(sA, &tmA, &full[stage], kt * BK, mb * BM);
-                    if (SILU) {
-                        tma_load_2d(sB, &tmB, &full[stage], kt * BK, nb * (BN / 2));
-                        tma_load_2d(sB + (BN / 2) * BK * 2, &tmB2, &full[stage], kt * BK,
-                                    nb * (BN / 2));
-                    } else {
-                        tma_load_2d(sB, &tmB, &full[stage], kt * BK, nb * BN);
-                    }
+                    load_b(sB, kt, nb);
                     issued++;
                     if (++stage == STAGES) { stage = 0; phase ^= 1; }
                 }
@@ -599,6 +627,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
         }
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
+        dep_wait();                              // outputs and tables of earlier kernels
         const int q = warp & 3;                 // TMEM lane quarter of this warp
         uint32_t *stg = (uint32_t *)(base + STAGES * Cfg::STAGE_BYTES) + (warp - 2) * STG * 32 * 32;
         int chunks = 0;                          // residual chunks handed to the TMA
@@ -856,9 +885,8 @@ int launch_impl(cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tb,
     // otherwise walk N fastest so that A rows are shared.
     const int m_fast = (long long)N * (EPI == TC_EPI_SILU_BF16 ? 2 : 1) > (long long)M;
     if constexpr (!PAIR) {
-        gemm_tc_kernel<BN, EPI, false><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(
-            ta, tb, tb2, tmc, ep, M, N, K, m_fast, ksplit, kt_per, ws, partials);
-        N550_LAUNCH_CHECK();
+        N550_CUDA_TRY(launch_k(gemm_tc_kernel<BN, EPI, false>, grid, Cfg::THREADS, Cfg::SMEM_BYTES, st,
+                               ta, tb, tb2, tmc, ep, M, N, K, m_fast, ksplit, kt_per, ws, partials));
         return N550_OK;
     } else {
     // 2-CTA clusters: consecutive CTAs (2c, 2c+1) form pair c.
@@ -867,11 +895,13 @@ int launch_impl(cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tb,
     cfg.blockDim = dim3(Cfg::THREADS);
     cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     // persistent pairs: no more clusters than can be resident at once (SMs
@@ -889,6 +919,7 @@ int launch_impl(cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tb,
         if (grid > 2 * max_clusters[dev]) grid = 2 * max_clusters[dev];
         cfg.gridDim = dim3(grid);
     }
+    cfg.numAttrs = g_pdl ? 2 : 1;
     N550_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, EPI, true>, ta, tb, tb2, tmc, ep, M, N, K,
                                      m_fast, ksplit, kt_per, ws, partials));
     return N550_OK;
@@ -899,6 +930,8 @@ int launch_impl(cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tb,
 template <int EPI>
 __global__ void splitk_reduce_kernel(const float *__restrict__ ws, int ksplit, int M, int N, void *c,
                                      int ldc) {
+    dep_wait();
+    dep_launch();
     const int ldw = EPI == TC_EPI_SILU_BF16 ? 2 * N : N;
     const size_t slice = (size_t)M * ldw, total = (size_t)M * N;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
@@ -986,6 +1019,7 @@ int launch_gemm_tc_qkv(cudaStream_t st, const uint16_t *a, int lda, const uint16
 // 0: automatic; 128 / 256: single-CTA tiles of that width; 512: 256 x 256
 // tiles on 2-CTA clusters.
 int g_tile_bn = 0;
+bool g_pdl = true;
 
 bool tc_use_pair(int M, int bn) {
     if (bn != 256 || g_tile_bn == 256) return false;
@@ -1056,14 +1090,16 @@ int launch_splitk_reduce(cudaStream_t st, int epi, const float *ws, int ks, int 
     const size_t total = (size_t)M * N;
     if (!total) return N550_OK;
     const int grid = (int)std::min<size_t>((total + 255) / 256, 148 * 8);
+    auto go = [&](auto kernel) { return launch_k(kernel, grid, 256, 0, st, ws, ks, M, N, c, ldc); };
+    cudaError_t e;
     switch (epi) {
-    case TC_EPI_F32: splitk_reduce_kernel<TC_EPI_F32><<<grid, 256, 0, st>>>(ws, ks, M, N, c, ldc); break;
-    case TC_EPI_BF16: splitk_reduce_kernel<TC_EPI_BF16><<<grid, 256, 0, st>>>(ws, ks, M, N, c, ldc); break;
-    case TC_EPI_RESID_F32: splitk_reduce_kernel<TC_EPI_RESID_F32><<<grid, 256, 0, st>>>(ws, ks, M, N, c, ldc); break;
-    case TC_EPI_SILU_BF16: splitk_reduce_kernel<TC_EPI_SILU_BF16><<<grid, 256, 0, st>>>(ws, ks, M, N, c, ldc); break;
+    case TC_EPI_F32: e = go(splitk_reduce_kernel<TC_EPI_F32>); break;
+    case TC_EPI_BF16: e = go(splitk_reduce_kernel<TC_EPI_BF16>); break;
+    case TC_EPI_RESID_F32: e = go(splitk_reduce_kernel<TC_EPI_RESID_F32>); break;
+    case TC_EPI_SILU_BF16: e = go(splitk_reduce_kernel<TC_EPI_SILU_BF16>); break;
     default: return N550_ERR_ARG;
     }
-    N550_LAUNCH_CHECK();
+    N550_CUDA_TRY(e);
     return N550_OK;
 }
 
@@ -1092,6 +1128,8 @@ namespace {
 __global__ void __launch_bounds__(256)
 argmax_tiles_kernel(const float *__restrict__ amax, const int32_t *__restrict__ aidx, int an,
                     int32_t *idx) {
+    dep_wait();
+    dep_launch();
     __shared__ float sv[8];
     __shared__ int si[8];
     const float *rv = amax + (size_t)blockIdx.x * an;
@@ -1137,8 +1175,7 @@ int launch_gemm_tc_argmax(cudaStream_t st, const uint16_t *a, int lda, const uin
     ep.aidx = (int32_t *)((float *)ws + (size_t)M * an);
     ep.an = an;
     if ((rc = launch_impl<BNA, TC_EPI_ARGMAX>(st, ta, tb, tb, ep, M, N, K, 0))) return rc;
-    argmax_tiles_kernel<<<M, 256, 0, st>>>(ep.amax, ep.aidx, an, idx);
-    N550_LAUNCH_CHECK();
+    N550_CUDA_TRY(launch_k(argmax_tiles_kernel, M, 256, 0, st, ep.amax, ep.aidx, an, idx));
     return N550_OK;
 }
 

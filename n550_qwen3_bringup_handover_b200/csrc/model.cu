@@ -29,6 +29,7 @@
 #include "attention.h"
 #include "common.cuh"
 #include "gemm_tc.h"
+#include "launch.h"
 #include "ops.h"
 #include "synth.cuh"
 
@@ -183,6 +184,8 @@ __global__ void fill_u16_kernel(uint16_t *out, size_t n, uint16_t v) {
 // Per-token (position, KV slot) of a prefill chunk: token t = i*Lc + j.
 __global__ void setup_prefill_kernel(int32_t *tok_pos, int32_t *tok_seq, const int32_t *seq_ids,
                                      int Sc, int Lc, int p0) {
+    dep_wait();
+    dep_launch();
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= Sc * Lc) return;
     tok_pos[t] = p0 + t % Lc;
@@ -193,6 +196,8 @@ __global__ void setup_prefill_kernel(int32_t *tok_pos, int32_t *tok_seq, const i
 // row t = i*Lc + j is tokens[i*ld + off + j].
 __global__ void embed_kernel(float *x, const uint16_t *__restrict__ embed, const int32_t *tokens,
                              int Lc, int ld, int off) {
+    dep_wait();
+    dep_launch();
     const int t = blockIdx.x;
     const int i = t / Lc, j = t % Lc;
     int tok = tokens[(size_t)i * ld + off + j];
@@ -228,6 +233,8 @@ qknorm_rope_kv_kernel(const float *__restrict__ qkv, int ldqkv, int ks, size_t s
                       const float2 *__restrict__ rope, const int32_t *__restrict__ tok_pos,
                       const int32_t *__restrict__ tok_seq, int layer, uint16_t *kc, uint16_t *vc,
                       int max_len, uint16_t *q_bf16, float *q_f32, int ldq) {
+    dep_wait();
+    dep_launch();
     // One warp per head (32 per token): qkv row t, or (ks > 0) the sum of ks
     // split-K partial slices of it; RoPE factors from the per-position table.
     const int t = blockIdx.x;
@@ -283,6 +290,8 @@ __global__ void rope_table_kernel(float2 *t, int max_len) {
 // them back as the next step's tokens at the next positions.
 __global__ void decode_advance_kernel(const int32_t *next, int32_t *tokens, int32_t *pos,
                                       int32_t *out, int32_t *counter, int n) {
+    dep_wait();
+    dep_launch();
     const int step = *counter;
     for (int s = threadIdx.x; s < n; s += blockDim.x) {
         const int32_t id = next[s];
@@ -301,6 +310,8 @@ __global__ void decode_advance_kernel(const int32_t *next, int32_t *tokens, int3
 __global__ void __launch_bounds__(256)
 resid_norm_rows_kernel(float *x, const float *__restrict__ ws, int ks, size_t slice,
                        const uint16_t *__restrict__ w, uint16_t *out) {
+    dep_wait();
+    dep_launch();
     __shared__ float red[8];
     const int t = blockIdx.x;
     float *xr = x + (size_t)t * H;
@@ -336,6 +347,8 @@ resid_norm_rows_kernel(float *x, const float *__restrict__ ws, int ks, size_t sl
 __global__ void __launch_bounds__(256)
 norm_rows_bf16_kernel(uint16_t *__restrict__ out, const float *__restrict__ x,
                       const uint16_t *__restrict__ w, int T) {
+    dep_wait();
+    dep_launch();
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= T) return;
@@ -371,6 +384,8 @@ norm_rows_bf16_kernel(uint16_t *__restrict__ out, const float *__restrict__ x,
 // needs row NT-1): xl[i] = rmsnorm(x[i*Lc + Lc - 1]) in BF16.
 __global__ void __launch_bounds__(256)
 final_norm_kernel(uint16_t *xl, const float *__restrict__ x, const uint16_t *__restrict__ w, int Lc) {
+    dep_wait();
+    dep_launch();
     __shared__ float red[8];
     const float *xr = x + ((size_t)blockIdx.x * Lc + Lc - 1) * H;
     float ss = 0.f;
@@ -390,6 +405,8 @@ final_norm_kernel(uint16_t *xl, const float *__restrict__ x, const uint16_t *__r
 // h = silu(g) * u in BF16 (the unfused SwiGLU for the GEMV / exact paths).
 __global__ void silu_mul_bf16_kernel(uint16_t *h, const float *__restrict__ g,
                                      const float *__restrict__ u, size_t n) {
+    dep_wait();
+    dep_launch();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x) {
         const float gv = g[i];
@@ -589,8 +606,8 @@ int mgemm(n550_model *m, cudaStream_t st, int epi, const uint16_t *a, int lda, c
             int rc = launch_gemm_exact(st, a, N550_BF16, lda, w, K, m->tmp_a, N, M, N, K, m->cfg.kblock);
             if (!rc) rc = launch_gemm_exact(st, a, N550_BF16, lda, w2, K, m->tmp_b, N, M, N, K, m->cfg.kblock);
             if (rc) return rc;
-            silu_mul_bf16_kernel<<<grid1((size_t)M * N), 256, 0, st>>>((uint16_t *)c, m->tmp_a, m->tmp_b,
-                                                                    (size_t)M * N);
+            N550_CUDA_TRY(launch_k(silu_mul_bf16_kernel, grid1((size_t)M * N), 256, 0, st, (uint16_t *)c,
+                                   m->tmp_a, m->tmp_b, (size_t)M * N));
             N550_LAUNCH_CHECK();
             return N550_OK;
         }
@@ -601,8 +618,8 @@ int mgemm(n550_model *m, cudaStream_t st, int epi, const uint16_t *a, int lda, c
         int rc = launch_gemv(st, TC_EPI_F32, a, lda, w, K, m->tmp_a, N, M, N, K);
         if (!rc) rc = launch_gemv(st, TC_EPI_F32, a, lda, w2, K, m->tmp_b, N, M, N, K);
         if (rc) return rc;
-        silu_mul_bf16_kernel<<<grid1((size_t)M * N), 256, 0, st>>>((uint16_t *)c, m->tmp_a, m->tmp_b,
-                                                                (size_t)M * N);
+        N550_CUDA_TRY(launch_k(silu_mul_bf16_kernel, grid1((size_t)M * N), 256, 0, st, (uint16_t *)c,
+                               m->tmp_a, m->tmp_b, (size_t)M * N));
         N550_LAUNCH_CHECK();
         return N550_OK;
     }
@@ -614,17 +631,17 @@ int mgemm(n550_model *m, cudaStream_t st, int epi, const uint16_t *a, int lda, c
 
 int launch_qknorm_rope_kv(n550_model *m, cudaStream_t st, int T, int l, bool decode,
                           const float *src = nullptr, int ks = 0) {
-    qknorm_rope_kv_kernel<<<T, 1024, 0, st>>>(src ? src : m->qkv, QKVD, ks, (size_t)T * QKVD,
-                                             W(m, l, 4), W(m, l, 5), m->rope, m->tok_pos, m->tok_seq, l,
-                                             m->kc, m->vc, m->cfg.max_len,
-                                             decode ? nullptr : m->qb, decode ? m->qf : nullptr, QD);
+    N550_CUDA_TRY(launch_k(qknorm_rope_kv_kernel, T, 1024, 0, st, src ? src : m->qkv, QKVD, ks,
+                           (size_t)T * QKVD, W(m, l, 4), W(m, l, 5), m->rope, m->tok_pos, m->tok_seq, l,
+                           m->kc, m->vc, m->cfg.max_len, decode ? nullptr : m->qb,
+                           decode ? m->qf : nullptr, QD));
     N550_LAUNCH_CHECK();
     return N550_OK;
 }
 
 int launch_resid_norm(cudaStream_t st, float *x, const float *ws, int ks, int T,
                       const uint16_t *w, uint16_t *out) {
-    resid_norm_rows_kernel<<<T, 256, 0, st>>>(x, ws, ks, (size_t)T * H, w, out);
+    N550_CUDA_TRY(launch_k(resid_norm_rows_kernel, T, 256, 0, st, x, ws, ks, (size_t)T * H, w, out));
     N550_LAUNCH_CHECK();
     return N550_OK;
 }
@@ -638,13 +655,13 @@ int partials(n550_model *m, cudaStream_t st, const uint16_t *a, int lda, const u
 
 int launch_norm_rows(cudaStream_t st, uint16_t *out, const float *x, const uint16_t *w, int T) {
     if (T <= 0) return N550_OK;
-    norm_rows_bf16_kernel<<<(T + 7) / 8, 256, 0, st>>>(out, x, w, T);
+    N550_CUDA_TRY(launch_k(norm_rows_bf16_kernel, (T + 7) / 8, 256, 0, st, out, x, w, T));
     N550_LAUNCH_CHECK();
     return N550_OK;
 }
 
 int launch_final_norm(cudaStream_t st, uint16_t *xl, const float *x, const uint16_t *w, int Sc, int Lc) {
-    final_norm_kernel<<<Sc, 256, 0, st>>>(xl, x, w, Lc);
+    N550_CUDA_TRY(launch_k(final_norm_kernel, Sc, 256, 0, st, xl, x, w, Lc));
     N550_LAUNCH_CHECK();
     return N550_OK;
 }
@@ -931,10 +948,10 @@ static int prefill_eager(n550_model_t *m, cudaStream_t st, const int32_t *tokens
             const int p0 = pos0 + j0;
             {
                 ProfScope ps(m, st, N550_PROF_OTHER, 2);
-                setup_prefill_kernel<<<(T + 255) / 256, 256, 0, st>>>(m->tok_pos, m->tok_seq,
-                                                                      seq_ids + s0, Sc, Lc, p0);
-                embed_kernel<<<T, 128, 0, st>>>(m->x, m->t[0], tokens + (size_t)s0 * seq_len, Lc,
-                                                seq_len, j0);
+                N550_CUDA_TRY(launch_k(setup_prefill_kernel, (T + 255) / 256, 256, 0, st, m->tok_pos,
+                                       m->tok_seq, seq_ids + s0, Sc, Lc, p0));
+                N550_CUDA_TRY(launch_k(embed_kernel, T, 128, 0, st, m->x, m->t[0],
+                                       tokens + (size_t)s0 * seq_len, Lc, seq_len, j0));
                 N550_LAUNCH_CHECK();
             }
             bool xl_ready = false;
@@ -960,7 +977,7 @@ int n550_qwen3_decode(n550_model_t *m, void *stream, const int32_t *tokens, cons
     N550_CUDA_TRY(cudaMemcpyAsync(m->tok_seq, seq_ids, (size_t)n_seqs * 4, cudaMemcpyDeviceToDevice, st));
     {
         ProfScope ps(m, st, N550_PROF_OTHER, 1);
-        embed_kernel<<<n_seqs, 128, 0, st>>>(m->x, m->t[0], tokens, 1, 1, 0);
+        N550_CUDA_TRY(launch_k(embed_kernel, n_seqs, 128, 0, st, m->x, m->t[0], tokens, 1, 1, 0));
         N550_LAUNCH_CHECK();
     }
     bool xl_ready = false;
@@ -978,7 +995,8 @@ int n550_qwen3_decode_steps(n550_model_t *m, void *stream, int32_t *tokens, cons
     auto one_step = [&]() -> int {
         int rc = n550_qwen3_decode(m, st, tokens, seq_ids, pos, n_seqs, nullptr, m->next);
         if (rc) return rc;
-        decode_advance_kernel<<<1, 256, 0, st>>>(m->next, tokens, pos, out_ids, m->step_counter, n_seqs);
+        N550_CUDA_TRY(launch_k(decode_advance_kernel, 1, 256, 0, st, m->next, tokens, pos, out_ids,
+                               m->step_counter, n_seqs));
         N550_LAUNCH_CHECK();
         return N550_OK;
     };
@@ -997,7 +1015,8 @@ int n550_qwen3_decode_steps(n550_model_t *m, void *stream, int32_t *tokens, cons
     auto step_on = [&](cudaStream_t s_) -> int {
         int rc = n550_qwen3_decode(m, s_, tokens, seq_ids, pos, n_seqs, nullptr, m->next);
         if (rc) return rc;
-        decode_advance_kernel<<<1, 256, 0, s_>>>(m->next, tokens, pos, out_ids, m->step_counter, n_seqs);
+        N550_CUDA_TRY(launch_k(decode_advance_kernel, 1, 256, 0, s_, m->next, tokens, pos, out_ids,
+                               m->step_counter, n_seqs));
         N550_LAUNCH_CHECK();
         return N550_OK;
     };

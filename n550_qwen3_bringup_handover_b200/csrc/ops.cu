@@ -4,6 +4,7 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "launch.h"
 #include "ops.h"
 
 namespace n550 {
@@ -36,6 +37,8 @@ template <int OUT_BF16>
 __global__ void __launch_bounds__(RN_THREADS)
 rmsnorm_kernel(void *out, const float *__restrict__ x, const uint16_t *__restrict__ w,
                int n, float eps) {
+    dep_wait();
+    dep_launch();
     __shared__ float red[RN_THREADS / 32];
     const float *xr = x + (size_t)blockIdx.x * n;
     float ss = 0.f;
@@ -51,6 +54,8 @@ rmsnorm_kernel(void *out, const float *__restrict__ x, const uint16_t *__restric
 
 // One CTA per row, one thread per rotation pair (i, i+64) of one head.
 __global__ void rope_kernel(float *v, int n_heads, int pos0) {
+    dep_wait();
+    dep_launch();
     const int pos = pos0 + blockIdx.x;
     float *row = v + (size_t)blockIdx.x * n_heads * 128;
     for (int t = threadIdx.x; t < n_heads * 64; t += blockDim.x) {
@@ -66,6 +71,8 @@ __global__ void rope_kernel(float *v, int n_heads, int pos0) {
 }
 
 __global__ void silu_mul_kernel(float *gate, const float *__restrict__ up, size_t n) {
+    dep_wait();
+    dep_launch();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x) {
         const float g = gate[i];
@@ -74,12 +81,16 @@ __global__ void silu_mul_kernel(float *gate, const float *__restrict__ up, size_
 }
 
 __global__ void residual_add_kernel(float *x, const float *__restrict__ y, size_t n) {
+    dep_wait();
+    dep_launch();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x)
         x[i] += y[i];
 }
 
 __global__ void bf16_to_f32_kernel(float *out, const uint16_t *__restrict__ in, size_t n) {
+    dep_wait();
+    dep_launch();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x)
         out[i] = bf16_bits_to_f32(in[i]);
@@ -88,6 +99,8 @@ __global__ void bf16_to_f32_kernel(float *out, const uint16_t *__restrict__ in, 
 constexpr int SM_THREADS = 512;
 
 __global__ void __launch_bounds__(SM_THREADS) softmax_kernel(float *x, int n) {
+    dep_wait();
+    dep_launch();
     __shared__ float red[SM_THREADS / 32];
     float *xr = x + (size_t)blockIdx.x * n;
     float mx = -INFINITY;
@@ -132,6 +145,8 @@ constexpr int AM_THREADS = 1024;
 
 __global__ void __launch_bounds__(AM_THREADS)
 argmax_kernel(const float *__restrict__ v, int n, int ld, int32_t *idx) {
+    dep_wait();
+    dep_launch();
     __shared__ float sv[AM_THREADS / 32];
     __shared__ int si[AM_THREADS / 32];
     const float *r = v + (size_t)blockIdx.x * ld;
@@ -155,6 +170,8 @@ constexpr int DOT_THREADS = 1024;
 // Single-CTA dot product (qwen3_op_dot, ops_scalar.c:68-72).
 __global__ void __launch_bounds__(DOT_THREADS)
 dot_kernel(const float *__restrict__ a, const float *__restrict__ b, int n, float *out) {
+    dep_wait();
+    dep_launch();
     __shared__ float red[DOT_THREADS / 32];
     float s = 0.f;
     for (int i = threadIdx.x; i < n; i += DOT_THREADS) s = fmaf(a[i], b[i], s);
@@ -164,6 +181,8 @@ dot_kernel(const float *__restrict__ a, const float *__restrict__ b, int n, floa
 
 // y += a * x (qwen3_op_axpy, ops_scalar.c:74-77).
 __global__ void axpy_kernel(float *y, float a, const float *__restrict__ x, size_t n) {
+    dep_wait();
+    dep_launch();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x)
         y[i] = __fadd_rn(y[i], __fmul_rn(a, x[i]));   // no FMA: bit-identical to the C loop
@@ -195,9 +214,9 @@ int launch_rmsnorm(cudaStream_t st, void *out, int out_type, const float *x,
                    const uint16_t *w, int rows, int n, float eps) {
     if (rows <= 0 || n <= 0) return rows < 0 || n < 0 ? N550_ERR_ARG : N550_OK;
     if (out_type == N550_BF16)
-        rmsnorm_kernel<1><<<rows, RN_THREADS, 0, st>>>(out, x, w, n, eps);
+        N550_CUDA_TRY(launch_k(rmsnorm_kernel<1>, rows, RN_THREADS, 0, st, out, x, w, n, eps));
     else if (out_type == N550_F32)
-        rmsnorm_kernel<0><<<rows, RN_THREADS, 0, st>>>(out, x, w, n, eps);
+        N550_CUDA_TRY(launch_k(rmsnorm_kernel<0>, rows, RN_THREADS, 0, st, out, x, w, n, eps));
     else
         return N550_ERR_ARG;
     N550_LAUNCH_CHECK();
@@ -208,56 +227,56 @@ int launch_rope(cudaStream_t st, float *v, int rows, int n_heads, int pos0) {
     if (rows <= 0 || n_heads <= 0) return rows < 0 || n_heads < 0 ? N550_ERR_ARG : N550_OK;
     int rc = ensure_rope_table();
     if (rc) return rc;
-    rope_kernel<<<rows, 256, 0, st>>>(v, n_heads, pos0);
+    N550_CUDA_TRY(launch_k(rope_kernel, rows, 256, 0, st, v, n_heads, pos0));
     N550_LAUNCH_CHECK();
     return N550_OK;
 }
 
 int launch_silu_mul(cudaStream_t st, float *gate, const float *up, size_t n) {
     if (!n) return N550_OK;
-    silu_mul_kernel<<<grid_for(n, 256), 256, 0, st>>>(gate, up, n);
+    N550_CUDA_TRY(launch_k(silu_mul_kernel, grid_for(n, 256), 256, 0, st, gate, up, n));
     N550_LAUNCH_CHECK();
     return N550_OK;
 }
 
 int launch_residual_add(cudaStream_t st, float *x, const float *y, size_t n) {
     if (!n) return N550_OK;
-    residual_add_kernel<<<grid_for(n, 256), 256, 0, st>>>(x, y, n);
+    N550_CUDA_TRY(launch_k(residual_add_kernel, grid_for(n, 256), 256, 0, st, x, y, n));
     N550_LAUNCH_CHECK();
     return N550_OK;
 }
 
 int launch_bf16_to_f32(cudaStream_t st, float *out, const uint16_t *in, size_t n) {
     if (!n) return N550_OK;
-    bf16_to_f32_kernel<<<grid_for(n, 256), 256, 0, st>>>(out, in, n);
+    N550_CUDA_TRY(launch_k(bf16_to_f32_kernel, grid_for(n, 256), 256, 0, st, out, in, n));
     N550_LAUNCH_CHECK();
     return N550_OK;
 }
 
 int launch_softmax(cudaStream_t st, float *x, int rows, int n) {
     if (rows <= 0 || n <= 0) return rows < 0 || n < 0 ? N550_ERR_ARG : N550_OK;
-    softmax_kernel<<<rows, SM_THREADS, 0, st>>>(x, n);
+    N550_CUDA_TRY(launch_k(softmax_kernel, rows, SM_THREADS, 0, st, x, n));
     N550_LAUNCH_CHECK();
     return N550_OK;
 }
 
 int launch_argmax(cudaStream_t st, const float *v, int rows, int n, int ld, int32_t *idx) {
     if (rows <= 0 || n <= 0 || ld < n) return N550_ERR_ARG;
-    argmax_kernel<<<rows, AM_THREADS, 0, st>>>(v, n, ld, idx);
+    N550_CUDA_TRY(launch_k(argmax_kernel, rows, AM_THREADS, 0, st, v, n, ld, idx));
     N550_LAUNCH_CHECK();
     return N550_OK;
 }
 
 int launch_dot(cudaStream_t st, const float *a, const float *b, int n, float *out) {
     if (n < 0) return N550_ERR_ARG;
-    dot_kernel<<<1, DOT_THREADS, 0, st>>>(a, b, n, out);
+    N550_CUDA_TRY(launch_k(dot_kernel, 1, DOT_THREADS, 0, st, a, b, n, out));
     N550_LAUNCH_CHECK();
     return N550_OK;
 }
 
 int launch_axpy(cudaStream_t st, float *y, float a, const float *x, size_t n) {
     if (!n) return N550_OK;
-    axpy_kernel<<<grid_for(n, 256), 256, 0, st>>>(y, a, x, n);
+    N550_CUDA_TRY(launch_k(axpy_kernel, grid_for(n, 256), 256, 0, st, y, a, x, n));
     N550_LAUNCH_CHECK();
     return N550_OK;
 }

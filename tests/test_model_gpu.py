@@ -393,3 +393,38 @@ def test_decode_steps_graph_replay_matches_eager(cuda):
     torch.cuda.synchronize()
     m.close()
     assert np.array_equal(one.cpu().numpy(), ie[0])
+
+
+def test_dependent_launch_on_off_bit_identical(cuda):
+    """Programmatic dependent launch only changes when kernels start: a
+    prefill on both GEMM paths (1280 and 320 tokens; eager, captured and
+    replayed) and a CUDA-graph decode loop give bit-identical logits and ids
+    with it on and off."""
+    import torch
+    S, L, steps = 8, 160, 4
+    toks = torch.from_numpy(oracle.synth_tokens(S * L, 41, 0x544F4B).reshape(S, L)).cuda()
+    seq = torch.arange(S, dtype=torch.int32, device="cuda")
+    runs = []
+    try:
+        for on in (1, 0):
+            n5.check(n5.lib().n550_set_pdl(on))
+            m = n5.Model(seed=0, max_seqs=S, max_len=L + steps + 8, max_tokens=S * L)
+            lg = torch.empty((S, 151936), dtype=torch.float32, device="cuda")
+            nx = torch.empty(S, dtype=torch.int32, device="cuda")
+            for _ in range(3):
+                m.prefill(toks, seq, 0, lg, nx)
+            half = torch.empty((S // 2, 151936), dtype=torch.float32, device="cuda")
+            hn = torch.empty(S // 2, dtype=torch.int32, device="cuda")
+            m.prefill(toks[: S // 2, : L // 2].contiguous(), seq[: S // 2], 0, half, hn)
+            tok = nx.clone()
+            pos = torch.full((S,), L, dtype=torch.int32, device="cuda")
+            ids = torch.zeros((steps, S), dtype=torch.int32, device="cuda")
+            m.decode_steps(tok, seq, pos, steps, ids, use_graph=True)
+            torch.cuda.synchronize()
+            runs.append([x.cpu().numpy() for x in (lg, nx, half, hn, ids)])
+            m.close()
+    finally:
+        n5.lib().n550_set_pdl(1)
+    assert n5.device_status() == n5.OK
+    for a, b in zip(*runs):
+        assert np.array_equal(a, b)
