@@ -32,9 +32,12 @@ __device__ __forceinline__ size_t kv_base(int seq, int layer, int kvh, int max_l
 // ---------------------------------------------------------------------------
 // decode (CUDA cores, split-KV)
 // ---------------------------------------------------------------------------
-constexpr int DC_THREADS = 128;     // 4 warps
+constexpr int DC_THREADS = 256;     // 8 warps
 constexpr int DC_WARPS = DC_THREADS / 32;
-constexpr int DC_TP = 64;           // positions per tile (16 per warp)
+constexpr int DC_TP = 64;           // positions per tile
+constexpr int DC_PPW = DC_TP / DC_WARPS;     // positions of a tile per warp (8)
+constexpr int DC_PASSES = DC_PPW / 4;        // 4 positions (8 lanes each) per pass
+static_assert(DC_PASSES * 4 == DC_PPW, "whole passes per warp");
 constexpr int DC_STAGES = 3;        // tiles in flight per CTA
 constexpr int DC_TILE_BYTES = DC_TP * HD * 2;   // 16 KB of K (and of V)
 constexpr int DC_SMEM = DC_STAGES * 2 * DC_TILE_BYTES + 1024;
@@ -48,15 +51,18 @@ __device__ __forceinline__ void bf16x8(const uint4 q, float (&f)[8]) {
 
 // One CTA per (split, kv head, sequence). K and V tiles of 64 positions
 // (16 KB each, contiguous in the cache) stream through a 3-stage shared
-// ring by bulk copies; warp w owns positions 16w..16w+15 of every tile and
+// ring by bulk copies; warp w owns positions 8w..8w+7 of every tile and
 // keeps its own online-softmax state, merged with the others at the end.
+// Eight warps per CTA (two CTAs per SM) keep enough independent work in
+// flight to stream the cache near HBM speed even when there are fewer CTAs
+// than SM slots (small decode batches).
 __global__ void __launch_bounds__(DC_THREADS)
 attn_decode_kernel(AttnDecodeArgs p) {
     extern __shared__ __align__(128) uint8_t dsm[];
     uint8_t *ring = (uint8_t *)(((uintptr_t)dsm + 127) & ~(uintptr_t)127);
     uint64_t *full = (uint64_t *)(ring + DC_STAGES * 2 * DC_TILE_BYTES);
     uint64_t *empty = full + DC_STAGES;
-    __shared__ __align__(16) float ps[DC_WARPS][2][16];
+    __shared__ __align__(16) float ps[DC_WARPS][2][DC_PPW];
     __shared__ float wm[DC_WARPS][2], wl[DC_WARPS][2];
     __shared__ __align__(16) float wo[DC_WARPS][2][HD];
 
@@ -113,11 +119,11 @@ attn_decode_kernel(AttnDecodeArgs p) {
         if (!mbar_wait(&full[st], par)) { ok = false; break; }
         const uint8_t *kt = ring + st * 2 * DC_TILE_BYTES;
         const uint8_t *vt = kt + DC_TILE_BYTES;
-        const int t0 = start + tile * DC_TP + warp * 16;     // this warp's first position
-        float sc[2][4];
+        const int t0 = start + tile * DC_TP + warp * DC_PPW;    // this warp's first position
+        float sc[2][DC_PASSES];
 #pragma unroll
-        for (int pass = 0; pass < 4; pass++) {
-            const int r = warp * 16 + pass * 4 + (lane >> 3);  // row in the tile
+        for (int pass = 0; pass < DC_PASSES; pass++) {
+            const int r = warp * DC_PPW + pass * 4 + (lane >> 3);  // row in the tile
             const uint4 *kr = (const uint4 *)(kt + r * (HD * 2) + 32 * g8);
             float kf[16];
             bf16x8(kr[0], *(float(*)[8])kf);
@@ -134,17 +140,19 @@ attn_decode_kernel(AttnDecodeArgs p) {
             sc[0][pass] = valid ? a0 : -INFINITY;
             sc[1][pass] = valid ? a1 : -INFINITY;
         }
-        // online softmax over this warp's 16 positions (4 per lane group)
+        // online softmax over this warp's DC_PPW positions (DC_PASSES per lane group)
 #pragma unroll
         for (int h = 0; h < 2; h++) {
-            float mx = fmaxf(fmaxf(sc[h][0], sc[h][1]), fmaxf(sc[h][2], sc[h][3]));
+            float mx = sc[h][0];
+#pragma unroll
+            for (int pass = 1; pass < DC_PASSES; pass++) mx = fmaxf(mx, sc[h][pass]);
             mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 8));
             mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 16));
             const float mn = fmaxf(m[h], mx);
             const float c = (mn == -INFINITY) ? 1.f : exp2f(m[h] - mn);
             float sum = 0.f;
 #pragma unroll
-            for (int pass = 0; pass < 4; pass++) {
+            for (int pass = 0; pass < DC_PASSES; pass++) {
                 const float e = (sc[h][pass] == -INFINITY) ? 0.f : exp2f(sc[h][pass] - mn);
                 sc[h][pass] = e;
                 sum += e;
@@ -158,15 +166,15 @@ attn_decode_kernel(AttnDecodeArgs p) {
         }
         if (g8 == 0) {
 #pragma unroll
-            for (int pass = 0; pass < 4; pass++) {
+            for (int pass = 0; pass < DC_PASSES; pass++) {
                 ps[warp][0][pass * 4 + (lane >> 3)] = sc[0][pass];
                 ps[warp][1][pass * 4 + (lane >> 3)] = sc[1][pass];
             }
         }
         __syncwarp();
-        const int nvalid = min(16, end - t0);
+        const int nvalid = min(DC_PPW, end - t0);
         for (int j = 0; j < nvalid; j++) {
-            const uint2 v2 = *(const uint2 *)(vt + (warp * 16 + j) * (HD * 2) + 8 * lane);
+            const uint2 v2 = *(const uint2 *)(vt + (warp * DC_PPW + j) * (HD * 2) + 8 * lane);
             const float w0 = ps[warp][0][j], w1 = ps[warp][1][j];
             const float v0 = __uint_as_float(v2.x << 16), v1 = __uint_as_float(v2.x & 0xFFFF0000u);
             const float v2f = __uint_as_float(v2.y << 16), v3 = __uint_as_float(v2.y & 0xFFFF0000u);

@@ -5,6 +5,7 @@
 
 #include "attention.h"
 #include "common.cuh"
+#include "gemm_skinny.h"
 #include "gemm_tc.h"
 #include "launch.h"
 #include "ops.h"
@@ -50,6 +51,15 @@ __global__ void untile_kernel(uint16_t *dst, const uint16_t *src, int N, int K) 
     }
 }
 
+// C = A . B^T in FP32 through the skinny-token GEMM (M <= SK_MAX_T).
+int skinny_f32(cudaStream_t st, const uint16_t *a, int lda, const uint16_t *b, int ldb, float *c,
+               int ldc, int M, int N, int K) {
+    SkEpilogue ep{};
+    ep.out = c;
+    ep.ldo = ldc;
+    return launch_gemm_skinny(st, SK_EPI_F32, a, lda, b, nullptr, ldb, M, N, K, ep);
+}
+
 int device_gemm(cudaStream_t st, int mode, int kblock, const void *a, int a_type, int lda,
                 const uint16_t *b, int ldb, void *c, int c_type, int ldc, int M, int N, int K) {
     if (M < 0 || N < 0 || K < 0) return N550_ERR_ARG;
@@ -83,6 +93,10 @@ int device_gemm(cudaStream_t st, int mode, int kblock, const void *a, int a_type
     int kt;
     if (M <= 8 && launch_gemv(st, epi, abf, ldab, b, ldb, c, ldc, M, N, K) == N550_OK) {
         rc = N550_OK;
+    } else if (skinny_route(M) && epi == TC_EPI_F32 &&
+               tc_shape_ok(abf, ldab, b, ldb, K) &&
+               (rc = skinny_f32(st, abf, ldab, b, ldb, (float *)c, ldc, M, N, K)) != N550_ERR_UNSUPPORTED) {
+        // weight-streaming GEMM (rc set)
     } else if (M < 1024 && tc_shape_ok(abf, ldab, b, ldb, K) &&
                tc_splitk_plan(M, N, K, epi, 64, &kt) > 1) {
         // skinny M: split the K loop, partials in a stream-ordered workspace
@@ -158,6 +172,16 @@ inline void set_status(int s) { t_status = s; }
 // with its partials in a stream-ordered workspace.
 int skinny_or_full(cudaStream_t st, int epi, const uint16_t *a, int lda, const uint16_t *b, int ldb,
                    const uint16_t *b2, void *c, int ldc, int M, int N, int K) {
+    if (skinny_route(M) &&
+        (epi == TC_EPI_F32 || epi == TC_EPI_RESID_F32 || epi == TC_EPI_SILU_BF16)) {
+        // weight-streaming GEMM, K split over a cluster, reduced on chip
+        SkEpilogue ep{};
+        if (epi == TC_EPI_SILU_BF16) { ep.h = (uint16_t *)c; ep.ldh = ldc; }
+        else { ep.out = (float *)c; ep.ldo = ldc; }
+        const int sk = epi == TC_EPI_SILU_BF16 ? SK_EPI_SILU : (epi == TC_EPI_F32 ? SK_EPI_F32 : SK_EPI_RESID);
+        const int rc = launch_gemm_skinny(st, sk, a, lda, b, b2, ldb, M, N, K, ep);
+        if (rc != N550_ERR_UNSUPPORTED) return rc;
+    }
     int kt;
     if (M < 1024 && tc_splitk_plan(M, N, K, epi, 64, &kt) > 1) {
         const size_t ws_bytes = (size_t)8 * M * N * (epi == TC_EPI_SILU_BF16 ? 2 : 1) * 4;
@@ -357,6 +381,12 @@ int n550_gemm(void *stream, int mode, int kblock, const void *a, int a_type, int
 int n550_gemm_tile_config(int bn) {
     if (bn != 0 && bn != 128 && bn != 256 && bn != 512) return N550_ERR_ARG;
     g_tile_bn = bn;
+    return N550_OK;
+}
+
+int n550_gemm_skinny_config(int cs) {
+    if (cs < -1 || cs > 16) return N550_ERR_ARG;
+    g_skinny_cs = cs;
     return N550_OK;
 }
 

@@ -1180,7 +1180,8 @@ int launch_gemm_tc_argmax(cudaStream_t st, const uint16_t *a, int lda, const uin
 }
 
 bool tc_shape_ok(const void *a, int lda, const void *b, int ldb, int K) {
-    return K > 0 && (K % 8) == 0 && (lda % 8) == 0 && (ldb % 8) == 0 &&
+    // K >= 64: the tensor maps' boxes are 64 elements wide
+    return K >= 64 && (K % 8) == 0 && (lda % 8) == 0 && (ldb % 8) == 0 &&
            (((uintptr_t)a) & 15) == 0 && (((uintptr_t)b) & 15) == 0;
 }
 

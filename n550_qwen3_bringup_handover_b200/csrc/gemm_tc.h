@@ -47,7 +47,8 @@ int n550_tile_bn(int M, int N);
 // True when a bn = 256 tile runs as a 256 x 256 tile on a 2-CTA cluster.
 bool tc_use_pair(int M, int bn);
 
-// True when the tensor-core path takes these operands (TMA constraints).
+// True when the tensor-core path takes these operands (TMA constraints: K >= 64,
+// 16-byte aligned rows and bases).
 bool tc_shape_ok(const void *a, int lda, const void *b, int ldb, int K);
 
 // C = A[M,K] . B[N,K]^T on tcgen05 tensor cores. For TC_EPI_SILU_BF16, B

@@ -28,6 +28,7 @@
 
 #include "attention.h"
 #include "common.cuh"
+#include "gemm_skinny.h"
 #include "gemm_tc.h"
 #include "launch.h"
 #include "ops.h"
@@ -193,12 +194,18 @@ __global__ void setup_prefill_kernel(int32_t *tok_pos, int32_t *tok_seq, const i
 }
 
 // x[t] = embed[token] in FP32 (qwen3_embed, qwen3.c:276-279); the token of
-// row t = i*Lc + j is tokens[i*ld + off + j].
+// row t = i*Lc + j is tokens[i*ld + off + j]. A decode step (pos given) also
+// records each row's position and KV slot for the layers.
 __global__ void embed_kernel(float *x, const uint16_t *__restrict__ embed, const int32_t *tokens,
-                             int Lc, int ld, int off) {
+                             int Lc, int ld, int off, const int32_t *pos, const int32_t *seq_ids,
+                             int32_t *tok_pos, int32_t *tok_seq) {
     dep_wait();
     dep_launch();
     const int t = blockIdx.x;
+    if (pos && threadIdx.x == 0) {
+        tok_pos[t] = pos[t];
+        tok_seq[t] = seq_ids[t];
+    }
     const int i = t / Lc, j = t % Lc;
     int tok = tokens[(size_t)i * ld + off + j];
     tok = min(max(tok, 0), VOCAB - 1);
@@ -726,6 +733,52 @@ int run_layers_split(n550_model *m, cudaStream_t st, int T, bool decode, const i
     return N550_OK;
 }
 
+// Token counts that skinny_route() gives to the weight-streaming GEMM (the
+// decode step of up to 32 sequences by default): every projection is one GEMM
+// whose epilogue finishes the op -- QKV with QK-norm, RoPE and the K/V write;
+// o and down with the residual add; gate/up with SwiGLU -- so a layer is 4
+// GEMMs, attention and 2 RMSNorms.
+int run_layers_skinny(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t *seq_ids,
+                      const int32_t *pos, int Sc, int Lc, int p0, bool *xl_ready) {
+    const n550_model_config &c = m->cfg;
+    int rc = N550_OK;
+    STEP(N550_PROF_RMSNORM, 1, launch_norm_rows(st, m->xb, m->x, W(m, 0, 0), T));
+    SkEpilogue resid{};
+    resid.out = m->x;
+    resid.ldo = H;
+    SkEpilogue swiglu{};
+    swiglu.h = m->h;
+    swiglu.ldh = INTER;
+    for (int l = 0; l < NLAYER; l++) {
+        SkEpilogue q{};
+        q.q_f32 = decode ? m->qf : nullptr;       // decode attention reads FP32 queries
+        q.q_bf16 = decode ? nullptr : m->qb;      // the tcgen05 prefill attention BF16
+        q.ldq = QD;
+        q.kc = m->kc; q.vc = m->vc; q.layer = l; q.max_len = c.max_len;
+        q.tok_pos = m->tok_pos; q.tok_seq = m->tok_seq;
+        q.q_norm = W(m, l, 4); q.k_norm = W(m, l, 5);
+        q.rope = m->rope;
+        STEP(N550_PROF_GEMM_QKV, 1,
+             launch_gemm_skinny(st, SK_EPI_QKV, m->xb, H, m->wqkv[l], nullptr, H, T, QKVD, H, q));
+        if ((rc = run_attention(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, l))) return rc;
+        STEP(N550_PROF_GEMM_O, 1,
+             launch_gemm_skinny(st, SK_EPI_RESID, m->attn, QD, W(m, l, 6), nullptr, QD, T, H, QD, resid));
+        STEP(N550_PROF_RMSNORM, 1, launch_norm_rows(st, m->xb, m->x, W(m, l, 7), T));
+        STEP(N550_PROF_GEMM_GATEUP, 1,
+             launch_gemm_skinny(st, SK_EPI_SILU, m->xb, H, W(m, l, 8), W(m, l, 9), H, T, INTER, H, swiglu));
+        STEP(N550_PROF_GEMM_DOWN, 1,
+             launch_gemm_skinny(st, SK_EPI_RESID, m->h, INTER, W(m, l, 10), nullptr, INTER, T, H, INTER,
+                                resid));
+        // input norm of the next layer; after the last, the final norm (decode:
+        // every row is a last token; prefill normalises its last rows later)
+        const uint16_t *wn = l + 1 < NLAYER ? W(m, l + 1, 0) : (decode ? m->t[N_TENSORS - 1] : nullptr);
+        uint16_t *dst = l + 1 < NLAYER ? m->xb : m->xl;
+        if (wn) STEP(N550_PROF_RMSNORM, 1, launch_norm_rows(st, dst, m->x, wn, T));
+    }
+    *xl_ready = decode;
+    return N550_OK;
+}
+
 // All 28 layers over T tokens already embedded in m->x, with tok_pos/tok_seq
 // set. decode: one token per sequence (seq_ids/pos arrays of n_seqs = T).
 int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t *seq_ids,
@@ -734,6 +787,8 @@ int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t
     int rc = N550_OK;
     *xl_ready = false;
     const bool exact = c.gemm_mode == N550_MODE_EXACT;
+    if (!exact && T > 8 && skinny_route(T))
+        return run_layers_skinny(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, xl_ready);
     if (!exact && T > 8 && T < 1024)
         return run_layers_split(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, xl_ready);
     const int gu_kernels = exact || T <= 8 ? 3 : 1;
@@ -951,7 +1006,8 @@ static int prefill_eager(n550_model_t *m, cudaStream_t st, const int32_t *tokens
                 N550_CUDA_TRY(launch_k(setup_prefill_kernel, (T + 255) / 256, 256, 0, st, m->tok_pos,
                                        m->tok_seq, seq_ids + s0, Sc, Lc, p0));
                 N550_CUDA_TRY(launch_k(embed_kernel, T, 128, 0, st, m->x, m->t[0],
-                                       tokens + (size_t)s0 * seq_len, Lc, seq_len, j0));
+                                       tokens + (size_t)s0 * seq_len, Lc, seq_len, j0, nullptr,
+                                       nullptr, nullptr, nullptr));
                 N550_LAUNCH_CHECK();
             }
             bool xl_ready = false;
@@ -973,11 +1029,10 @@ int n550_qwen3_decode(n550_model_t *m, void *stream, const int32_t *tokens, cons
     const n550_model_config &c = m->cfg;
     if (n_seqs > c.max_tokens || n_seqs > c.max_seqs) return N550_ERR_ARG;
     cudaStream_t st = (cudaStream_t)stream;
-    N550_CUDA_TRY(cudaMemcpyAsync(m->tok_pos, pos, (size_t)n_seqs * 4, cudaMemcpyDeviceToDevice, st));
-    N550_CUDA_TRY(cudaMemcpyAsync(m->tok_seq, seq_ids, (size_t)n_seqs * 4, cudaMemcpyDeviceToDevice, st));
     {
         ProfScope ps(m, st, N550_PROF_OTHER, 1);
-        N550_CUDA_TRY(launch_k(embed_kernel, n_seqs, 128, 0, st, m->x, m->t[0], tokens, 1, 1, 0));
+        N550_CUDA_TRY(launch_k(embed_kernel, n_seqs, 128, 0, st, m->x, m->t[0], tokens, 1, 1, 0, pos,
+                               seq_ids, m->tok_pos, m->tok_seq));
         N550_LAUNCH_CHECK();
     }
     bool xl_ready = false;

@@ -171,25 +171,32 @@ def test_greedy_64_tokens_match_reference(model):
 
 
 def test_batched_prefill_matches_single_sequence(cuda):
-    """Several sequences in one prefill call give each sequence's own logits."""
+    """Several sequences in one prefill call give each sequence's own logits.
+    Both calls take the split-K GEMMs (the 24-token single prefill would take
+    the skinny GEMM by default), so only the batching differs and the logits
+    agree to 1e-4."""
     import torch
     S, L = 4, 24
-    m = n5.Model(seed=0, max_seqs=S, max_len=64, max_tokens=S * L)
-    toks = oracle.synth_tokens(S * L, 5, 0x544F4B).reshape(S, L)
-    t = torch.from_numpy(toks).cuda()
-    seq = torch.arange(S, dtype=torch.int32, device="cuda")
-    logits = torch.empty((S, 151936), dtype=torch.float32, device="cuda")
-    nxt = torch.empty(S, dtype=torch.int32, device="cuda")
-    m.prefill(t, seq, 0, logits, nxt)
-    torch.cuda.synchronize()
-    batched = logits.cpu().numpy()
-    m.close()
-    for s in range(S):
-        single = n5.Model(seed=0, max_seqs=1, max_len=64, max_tokens=64)
-        a, lg = single.forward_batch(toks[s], 0)
-        single.close()
-        assert rel(batched[s], lg) <= 1e-4
-        assert int(nxt[s]) == a
+    n5.check(n5.lib().n550_gemm_skinny_config(-1))
+    try:
+        m = n5.Model(seed=0, max_seqs=S, max_len=64, max_tokens=S * L)
+        toks = oracle.synth_tokens(S * L, 5, 0x544F4B).reshape(S, L)
+        t = torch.from_numpy(toks).cuda()
+        seq = torch.arange(S, dtype=torch.int32, device="cuda")
+        logits = torch.empty((S, 151936), dtype=torch.float32, device="cuda")
+        nxt = torch.empty(S, dtype=torch.int32, device="cuda")
+        m.prefill(t, seq, 0, logits, nxt)
+        torch.cuda.synchronize()
+        batched = logits.cpu().numpy()
+        m.close()
+        for s in range(S):
+            single = n5.Model(seed=0, max_seqs=1, max_len=64, max_tokens=64)
+            a, lg = single.forward_batch(toks[s], 0)
+            single.close()
+            assert rel(batched[s], lg) <= 1e-4
+            assert int(nxt[s]) == a
+    finally:
+        n5.lib().n550_gemm_skinny_config(0)
 
 
 def test_batched_decode_positions_and_chunked_prefill(cuda, blob):
@@ -428,3 +435,41 @@ def test_dependent_launch_on_off_bit_identical(cuda):
     assert n5.device_status() == n5.OK
     for a, b in zip(*runs):
         assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("S,cfg", [(16, 0), (32, 0), (48, 4), (128, 8)])
+def test_skinny_decode_matches_split_path(cuda, S, cfg):
+    """Decode steps of up to 32 sequences (up to 128 with a forced cluster
+    size) run the weight-streaming GEMMs with the q/k/v, residual and SwiGLU
+    epilogues fused; forced back to the split-K GEMMs
+    (n550_gemm_skinny_config(-1)) the logits agree within the logit tolerance
+    and the greedy choices agree (or the reference margin is below it)."""
+    import torch
+    L = 24
+    toks = torch.from_numpy(oracle.synth_tokens(S * L, 51 + S, 0x544F4B).reshape(S, L)).cuda()
+    seq = torch.arange(S, dtype=torch.int32, device="cuda")
+    out = {}
+    try:
+        for c in (cfg, -1):
+            n5.check(n5.lib().n550_gemm_skinny_config(c))
+            m = n5.Model(seed=0, max_seqs=S, max_len=L + 8, max_tokens=S * L)
+            nx = torch.empty(S, dtype=torch.int32, device="cuda")
+            m.prefill(toks, seq, 0, None, nx)
+            lg = torch.empty((S, 151936), dtype=torch.float32, device="cuda")
+            dn = torch.empty(S, dtype=torch.int32, device="cuda")
+            m.decode(nx.clone(), seq, torch.full((S,), L, dtype=torch.int32, device="cuda"), lg, dn)
+            lg2 = torch.empty_like(lg)
+            dn2 = torch.empty_like(dn)
+            m.decode(dn.clone(), seq, torch.full((S,), L + 1, dtype=torch.int32, device="cuda"), lg2, dn2)
+            torch.cuda.synchronize()
+            out[c] = (lg.cpu().numpy(), dn.cpu().numpy(), lg2.cpu().numpy(), dn2.cpu().numpy())
+            m.close()
+    finally:
+        n5.lib().n550_gemm_skinny_config(0)
+    assert n5.device_status() == n5.OK
+    a, b = out[cfg], out[-1]
+    for s in range(S):
+        assert rel(a[0][s], b[0][s]) <= LOGIT_TOL
+        assert same_choice(int(a[1][s]), b[0][s])
+        if a[1][s] == b[1][s]:          # same first token: the second step is comparable
+            assert rel(a[2][s], b[2][s]) <= LOGIT_TOL
