@@ -8,13 +8,16 @@
 // V -- one (seq, layer, kv_head) is a contiguous run of positions, the
 // kvh-major order of qwen3.h:62-76, so decode streams it with coalesced loads.
 //
-// This file is the decode side: one query per sequence, split-KV on CUDA
-// cores fed by a bulk-copy shared-memory ring; the partial (max, sum, out) of
-// each split are merged by a combine kernel. Prefill runs on the tcgen05
+// This file is the decode side: one query per sequence, split-KV, the dot
+// products on mma.sync tensor-core fragments fed by a TMA shared-memory ring;
+// the partial (max, sum, out) of each split are merged by a combine kernel. Prefill runs on the tcgen05
 // tensor cores (attn_prefill_tc.cu).
+#include <cuda.h>
+
 #include "attention.h"
 #include "common.cuh"
 #include "launch.h"
+#include "tmap.h"
 
 namespace n550 {
 namespace {
@@ -30,39 +33,59 @@ __device__ __forceinline__ size_t kv_base(int seq, int layer, int kvh, int max_l
 }
 
 // ---------------------------------------------------------------------------
-// decode (CUDA cores, split-KV)
+// decode (split-KV; q.K^T and P.V on mma.sync tensor-core fragments)
 // ---------------------------------------------------------------------------
-constexpr int DC_THREADS = 256;     // 8 warps
+constexpr int DC_THREADS = 128;     // 4 warps
 constexpr int DC_WARPS = DC_THREADS / 32;
 constexpr int DC_TP = 64;           // positions per tile
-constexpr int DC_PPW = DC_TP / DC_WARPS;     // positions of a tile per warp (8)
-constexpr int DC_PASSES = DC_PPW / 4;        // 4 positions (8 lanes each) per pass
-static_assert(DC_PASSES * 4 == DC_PPW, "whole passes per warp");
+constexpr int DC_PPW = DC_TP / DC_WARPS;       // positions of a tile per warp (16)
 constexpr int DC_STAGES = 3;        // tiles in flight per CTA
-constexpr int DC_TILE_BYTES = DC_TP * HD * 2;   // 16 KB of K (and of V)
-constexpr int DC_SMEM = DC_STAGES * 2 * DC_TILE_BYTES + 1024;
+constexpr int DC_BOX = 64 * 64 * 2;            // 64 positions x 64 dims BF16, 128-byte swizzle
+constexpr int DC_STAGE_BYTES = 4 * DC_BOX;     // K dims 0-63 | K 64-127 | V 0-63 | V 64-127
+constexpr int DC_SMEM = DC_STAGES * DC_STAGE_BYTES + 1024 + 64;
+static_assert(DC_PPW == 16, "one 16-position MMA k-step of P.V per warp and tile");
 
-__device__ __forceinline__ void bf16x8(const uint4 q, float (&f)[8]) {
-    f[0] = __uint_as_float(q.x << 16); f[1] = __uint_as_float(q.x & 0xFFFF0000u);
-    f[2] = __uint_as_float(q.y << 16); f[3] = __uint_as_float(q.y & 0xFFFF0000u);
-    f[4] = __uint_as_float(q.z << 16); f[5] = __uint_as_float(q.z & 0xFFFF0000u);
-    f[6] = __uint_as_float(q.w << 16); f[7] = __uint_as_float(q.w & 0xFFFF0000u);
+// Byte offset of the 16-byte chunk (position p, dims d..d+7; d a multiple of
+// 8) in a tile held as two 128-byte-swizzled boxes of 64 dims: chunk c of a
+// 128-byte row r sits at chunk c ^ (r & 7), so the 8 rows of an 8 x 8
+// ldmatrix tile fall in 8 different bank groups.
+__device__ __forceinline__ uint32_t dc_off(int p, int d) {
+    return (uint32_t)((d >> 6) * DC_BOX + p * 128 + ((((d & 63) >> 3) ^ (p & 7)) << 4));
 }
 
-// One CTA per (split, kv head, sequence). K and V tiles of 64 positions
-// (16 KB each, contiguous in the cache) stream through a 3-stage shared
-// ring by bulk copies; warp w owns positions 8w..8w+7 of every tile and
-// keeps its own online-softmax state, merged with the others at the end.
-// Eight warps per CTA (two CTAs per SM) keep enough independent work in
-// flight to stream the cache near HBM speed even when there are fewer CTAs
-// than SM slots (small decode batches).
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+// D (16 x 8, FP32) += A (16 x 16 BF16, rows 8-15 zero) . B (16 x 8 BF16)
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0,
+                                               uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
+// One CTA per (split, kv head, sequence); its two query heads are rows 0-1
+// of 16-row MMA tiles (rows 2-15 zero). K and V tiles of 64 positions stream
+// through a 3-stage ring of TMA loads (3-D maps over the cache, 128-byte
+// swizzle). Warp w owns positions 16w..16w+15 of every tile: S = q.K^T over
+// them (2 x 8 MMAs of m16n8k16), an online softmax per head on the S
+// fragments, then O += P.V (16 MMAs, the S fragments reused as the A
+// operand in BF16, V read transposed by ldmatrix). The four warps' (max, sum,
+// O) are merged at the end.
 __global__ void __launch_bounds__(DC_THREADS)
-attn_decode_kernel(AttnDecodeArgs p) {
-    extern __shared__ __align__(128) uint8_t dsm[];
-    uint8_t *ring = (uint8_t *)(((uintptr_t)dsm + 127) & ~(uintptr_t)127);
-    uint64_t *full = (uint64_t *)(ring + DC_STAGES * 2 * DC_TILE_BYTES);
+attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                   AttnDecodeArgs p) {
+    extern __shared__ uint8_t dsm[];
+    uint8_t *ring = (uint8_t *)(((uintptr_t)dsm + 1023) & ~(uintptr_t)1023);
+    uint64_t *full = (uint64_t *)(ring + DC_STAGES * DC_STAGE_BYTES);
     uint64_t *empty = full + DC_STAGES;
-    __shared__ __align__(16) float ps[DC_WARPS][2][DC_PPW];
     __shared__ float wm[DC_WARPS][2], wl[DC_WARPS][2];
     __shared__ __align__(16) float wo[DC_WARPS][2][HD];
 
@@ -76,112 +99,123 @@ attn_decode_kernel(AttnDecodeArgs p) {
     chunk = (chunk + DC_TP - 1) / DC_TP * DC_TP;
     const int start = split * chunk, end = min(kv_len, start + chunk);
     const int n_tiles = end > start ? (end - start + DC_TP - 1) / DC_TP : 0;
-    const uint16_t *kbase = p.kc + kv_base(seq, p.layer, kvh, p.max_len);
-    const uint16_t *vbase = p.vc + kv_base(seq, p.layer, kvh, p.max_len);
+    const int plane = (seq * NL + p.layer) * NKV + kvh;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < DC_STAGES; i++) { mbar_init(&full[i], 1); mbar_init(&empty[i], DC_WARPS); }
         fence_mbar_init();
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
     }
     __syncthreads();
     auto issue = [&](int tile) {
         const int st = tile % DC_STAGES;
         const int t0 = start + tile * DC_TP;
-        const uint32_t bytes = (uint32_t)min(DC_TP, end - t0) * HD * 2;
-        uint8_t *kd = ring + st * 2 * DC_TILE_BYTES;
-        mbar_arrive_expect_tx(&full[st], 2 * bytes);
-        bulk_load(kd, kbase + (size_t)t0 * HD, bytes, &full[st]);
-        bulk_load(kd + DC_TILE_BYTES, vbase + (size_t)t0 * HD, bytes, &full[st]);
+        uint8_t *b = ring + st * DC_STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[st], DC_STAGE_BYTES);
+        tma_load_3d(b, &tmK, &full[st], 0, t0, plane);
+        tma_load_3d(b + DC_BOX, &tmK, &full[st], 64, t0, plane);
+        tma_load_3d(b + 2 * DC_BOX, &tmV, &full[st], 0, t0, plane);
+        tma_load_3d(b + 3 * DC_BOX, &tmV, &full[st], 64, t0, plane);
     };
     if (threadIdx.x == 0)
         for (int i = 0; i < min(DC_STAGES, n_tiles); i++) issue(i);
 
-    // q . k: 8 lanes per position, lane g8 = lane & 7 owns dims 16*g8 .. +15.
-    const int g8 = lane & 7;
-    float q0[16], q1[16];
-    {
-        const size_t qo = (size_t)s * p.ldq + (size_t)(kvh * 2) * HD + 16 * g8;
+    // A fragments of q (x scale x log2 e, BF16): row g = lane / 4 is query
+    // head 2 kvh + g for g < 2, zero otherwise; columns 16 kk + 2 tq (+1, +8).
+    const int g = lane >> 2, tq = lane & 3;
+    uint32_t qa[8][2];
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
-            const float a = p.q_f32 ? p.q_f32[qo + j] : bf16_bits_to_f32(p.q_bf16[qo + j]);
-            const float b = p.q_f32 ? p.q_f32[qo + HD + j] : bf16_bits_to_f32(p.q_bf16[qo + HD + j]);
-            q0[j] = a * (kScale * kLog2e);
-            q1[j] = b * (kScale * kLog2e);
+    for (int kk = 0; kk < 8; kk++)
+#pragma unroll
+        for (int h8 = 0; h8 < 2; h8++) {
+            float v0 = 0.f, v1 = 0.f;
+            if (g < 2) {
+                const size_t o = (size_t)s * p.ldq + (size_t)(kvh * 2 + g) * HD + 16 * kk + 8 * h8 + 2 * tq;
+                v0 = p.q_f32 ? p.q_f32[o] : bf16_bits_to_f32(p.q_bf16[o]);
+                v1 = p.q_f32 ? p.q_f32[o + 1] : bf16_bits_to_f32(p.q_bf16[o + 1]);
+            }
+            qa[kk][h8] = pack_bf16x2(v0 * (kScale * kLog2e), v1 * (kScale * kLog2e));
         }
-    }
-    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-    float acc[2][4] = {};                 // p . v: lane owns dims 4*lane .. +3
+    float m_r = -INFINITY, l_r = 0.f;        // softmax state of row g (log2 units)
+    float o[16][4];                           // O row g: dims 8 nt + 2 tq (+1)
+#pragma unroll
+    for (int nt = 0; nt < 16; nt++) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
     bool ok = true;
+    const int p0 = warp * DC_PPW;            // this warp's rows of every tile
 
     for (int tile = 0; tile < n_tiles && ok; tile++) {
         const int st = tile % DC_STAGES;
         const uint32_t par = (uint32_t)((tile / DC_STAGES) & 1);
         if (!mbar_wait(&full[st], par)) { ok = false; break; }
-        const uint8_t *kt = ring + st * 2 * DC_TILE_BYTES;
-        const uint8_t *vt = kt + DC_TILE_BYTES;
-        const int t0 = start + tile * DC_TP + warp * DC_PPW;    // this warp's first position
-        float sc[2][DC_PASSES];
-#pragma unroll
-        for (int pass = 0; pass < DC_PASSES; pass++) {
-            const int r = warp * DC_PPW + pass * 4 + (lane >> 3);  // row in the tile
-            const uint4 *kr = (const uint4 *)(kt + r * (HD * 2) + 32 * g8);
-            float kf[16];
-            bf16x8(kr[0], *(float(*)[8])kf);
-            bf16x8(kr[1], *(float(*)[8])(kf + 8));
-            float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-            for (int j = 0; j < 16; j++) { a0 = fmaf(q0[j], kf[j], a0); a1 = fmaf(q1[j], kf[j], a1); }
-#pragma unroll
-            for (int o = 4; o > 0; o >>= 1) {
-                a0 += __shfl_xor_sync(0xFFFFFFFFu, a0, o);
-                a1 += __shfl_xor_sync(0xFFFFFFFFu, a1, o);
+        uint8_t *kt = ring + st * DC_STAGE_BYTES;
+        const uint32_t kb = smem_u32(kt), vb = kb + 2 * DC_BOX;
+        const int t0 = start + tile * DC_TP + p0;              // this warp's first position
+        // V rows past the end of the range may hold anything (stale cache):
+        // zero them so that 0-weights do not meet NaN.
+        if (t0 + DC_PPW > end) {
+            for (int idx = lane; idx < DC_PPW * 16; idx += 32) {
+                const int r = idx >> 4, c = idx & 15;
+                if (t0 + r >= end)
+                    *(uint4 *)(kt + 2 * DC_BOX + (c >> 3) * DC_BOX + (p0 + r) * 128 + (c & 7) * 16) =
+                        make_uint4(0u, 0u, 0u, 0u);
             }
-            const bool valid = t0 + pass * 4 + (lane >> 3) < end;
-            sc[0][pass] = valid ? a0 : -INFINITY;
-            sc[1][pass] = valid ? a1 : -INFINITY;
+            __syncwarp();
         }
-        // online softmax over this warp's DC_PPW positions (DC_PASSES per lane group)
+        // S = q . K^T, positions p0 + 8 nt + (col): n-tiles of 8 positions
+        float sc[2][4];
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-            float mx = sc[h][0];
+        for (int nt = 0; nt < 2; nt++) {
+            sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
 #pragma unroll
-            for (int pass = 1; pass < DC_PASSES; pass++) mx = fmaxf(mx, sc[h][pass]);
-            mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 8));
-            mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 16));
-            const float mn = fmaxf(m[h], mx);
-            const float c = (mn == -INFINITY) ? 1.f : exp2f(m[h] - mn);
-            float sum = 0.f;
+            for (int k2 = 0; k2 < 4; k2++) {        // 32 dims per ldmatrix.x4
+                uint32_t b[4];
+                ldsm_x4(kb + dc_off(p0 + 8 * nt + (lane & 7), 32 * k2 + 8 * (lane >> 3)), b);
+                mma_bf16_16816(sc[nt], qa[2 * k2][0], qa[2 * k2][1], b[0], b[1]);
+                mma_bf16_16816(sc[nt], qa[2 * k2 + 1][0], qa[2 * k2 + 1][1], b[2], b[3]);
+            }
+        }
+        // online softmax of row g over this warp's 16 positions (4 per lane)
+        float sv[2][2];
+        float mx = -INFINITY;
 #pragma unroll
-            for (int pass = 0; pass < DC_PASSES; pass++) {
-                const float e = (sc[h][pass] == -INFINITY) ? 0.f : exp2f(sc[h][pass] - mn);
-                sc[h][pass] = e;
+        for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const bool valid = t0 + 8 * nt + 2 * tq + j < end;
+                sv[nt][j] = valid ? sc[nt][j] : -INFINITY;
+                mx = fmaxf(mx, sv[nt][j]);
+            }
+        mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
+        const float mn = fmaxf(m_r, mx);
+        const float corr = (mn == -INFINITY) ? 1.f : exp2f(m_r - mn);
+        float sum = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const float e = (sv[nt][j] == -INFINITY) ? 0.f : exp2f(sv[nt][j] - mn);
+                sv[nt][j] = e;
                 sum += e;
             }
-            sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 8);
-            sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 16);
-            l[h] = l[h] * c + sum;
-            m[h] = mn;
+        sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+        sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+        l_r = l_r * corr + sum;
+        m_r = mn;
 #pragma unroll
-            for (int d = 0; d < 4; d++) acc[h][d] *= c;
-        }
-        if (g8 == 0) {
+        for (int nt = 0; nt < 16; nt++) { o[nt][0] *= corr; o[nt][1] *= corr; }
+        // P as the A operand: columns 2 tq (+1) from n-tile 0, +8 from n-tile 1
+        const uint32_t pa0 = pack_bf16x2(sv[0][0], sv[0][1]);
+        const uint32_t pa2 = pack_bf16x2(sv[1][0], sv[1][1]);
+        // O += P . V: B fragments of V [position][dim] through ldmatrix.trans
 #pragma unroll
-            for (int pass = 0; pass < DC_PASSES; pass++) {
-                ps[warp][0][pass * 4 + (lane >> 3)] = sc[0][pass];
-                ps[warp][1][pass * 4 + (lane >> 3)] = sc[1][pass];
-            }
-        }
-        __syncwarp();
-        const int nvalid = min(DC_PPW, end - t0);
-        for (int j = 0; j < nvalid; j++) {
-            const uint2 v2 = *(const uint2 *)(vt + (warp * DC_PPW + j) * (HD * 2) + 8 * lane);
-            const float w0 = ps[warp][0][j], w1 = ps[warp][1][j];
-            const float v0 = __uint_as_float(v2.x << 16), v1 = __uint_as_float(v2.x & 0xFFFF0000u);
-            const float v2f = __uint_as_float(v2.y << 16), v3 = __uint_as_float(v2.y & 0xFFFF0000u);
-            acc[0][0] = fmaf(w0, v0, acc[0][0]); acc[0][1] = fmaf(w0, v1, acc[0][1]);
-            acc[0][2] = fmaf(w0, v2f, acc[0][2]); acc[0][3] = fmaf(w0, v3, acc[0][3]);
-            acc[1][0] = fmaf(w1, v0, acc[1][0]); acc[1][1] = fmaf(w1, v1, acc[1][1]);
-            acc[1][2] = fmaf(w1, v2f, acc[1][2]); acc[1][3] = fmaf(w1, v3, acc[1][3]);
+        for (int dn = 0; dn < 8; dn++) {            // 16 dims per ldmatrix.x4
+            const int i = lane >> 3;
+            uint32_t b[4];
+            ldsm_x4_t(vb + dc_off(p0 + (lane & 7) + 8 * (i & 1), 16 * dn + 8 * (i >> 1)), b);
+            mma_bf16_16816(o[2 * dn], pa0, pa2, b[0], b[1]);
+            mma_bf16_16816(o[2 * dn + 1], pa0, pa2, b[2], b[3]);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
@@ -195,9 +229,14 @@ attn_decode_kernel(AttnDecodeArgs p) {
     if (!ok && threadIdx.x == 0)
         for (int i = 0; i < min(DC_STAGES, n_tiles); i++) mbar_wait(&full[i], 0);
 
-    if (lane == 0) { wm[warp][0] = m[0]; wm[warp][1] = m[1]; wl[warp][0] = l[0]; wl[warp][1] = l[1]; }
+    if (g < 2) {
+        if (tq == 0) { wm[warp][g] = m_r; wl[warp][g] = l_r; }
 #pragma unroll
-    for (int d = 0; d < 4; d++) { wo[warp][0][4 * lane + d] = acc[0][d]; wo[warp][1][4 * lane + d] = acc[1][d]; }
+        for (int nt = 0; nt < 16; nt++) {
+            wo[warp][g][8 * nt + 2 * tq] = o[nt][0];
+            wo[warp][g][8 * nt + 2 * tq + 1] = o[nt][1];
+        }
+    }
     __syncthreads();
 
     for (int i = threadIdx.x; i < 2 * HD; i += DC_THREADS) {
@@ -243,8 +282,13 @@ __global__ void attn_combine_kernel(AttnDecodeArgs p) {
 }  // namespace
 
 int attn_decode_splits(int n_seqs, int max_kv_len, int max_splits) {
-    // Enough CTAs to cover the SMs twice (2 resident per SM); splits are
-    // rounded to whole 64-position tiles inside the kernel.
+    // Split the positions only when the (sequence, KV head) CTAs would leave
+    // more than half of the 148 SMs idle: from 10 sequences up one CTA per
+    // pair streams its positions faster than split CTAs plus the combine
+    // kernel (measured on B200 at 16-256 sequences x 1024 positions). Split CTAs
+    // cover the SMs twice (2 resident per SM); splits are rounded to whole
+    // 64-position tiles inside the kernel.
+    if (2 * n_seqs * NKV > 148) return 1;
     int splits = (2 * 148 + n_seqs * NKV - 1) / (n_seqs * NKV);
     const int by_len = (max_kv_len + 63) / 64;
     if (splits > by_len) splits = by_len;
@@ -256,6 +300,7 @@ int launch_attn_decode(cudaStream_t st, const AttnDecodeArgs &a, int n_seqs) {
     if (n_seqs <= 0) return N550_OK;
     if (a.splits < 1) return N550_ERR_ARG;
     if (a.splits > 1 && (!a.part_m || !a.part_l || !a.part_o)) return N550_ERR_ARG;
+    if (a.kv_planes < 1) return N550_ERR_ARG;
     static bool dc_attr[64];
     int dev = 0;
     N550_CUDA_TRY(cudaGetDevice(&dev));
@@ -264,8 +309,15 @@ int launch_attn_decode(cudaStream_t st, const AttnDecodeArgs &a, int n_seqs) {
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, DC_SMEM));
         dc_attr[dev] = true;
     }
+    // K and V as [planes][max_len][128] with 64 x 64 boxes (two per tile row)
+    CUtensorMap tk, tv;
+    int rc = tmap_bf16_sw128_3d(&tk, a.kc, (uint64_t)a.max_len, HD, HD, DC_TP, (uint64_t)a.kv_planes,
+                                (uint64_t)a.max_len * HD);
+    if (!rc) rc = tmap_bf16_sw128_3d(&tv, a.vc, (uint64_t)a.max_len, HD, HD, DC_TP, (uint64_t)a.kv_planes,
+                                     (uint64_t)a.max_len * HD);
+    if (rc) return rc;
     dim3 grid(a.splits, NKV, n_seqs);
-    N550_CUDA_TRY(launch_k(attn_decode_kernel, grid, DC_THREADS, DC_SMEM, st, a));
+    N550_CUDA_TRY(launch_k(attn_decode_kernel, grid, DC_THREADS, DC_SMEM, st, tk, tv, a));
     N550_LAUNCH_CHECK();
     if (a.splits > 1) {
         N550_CUDA_TRY(launch_k(attn_combine_kernel, dim3(16, n_seqs), HD, 0, st, a));

@@ -25,6 +25,7 @@ struct AttnDecodeArgs {
     uint16_t *out;
     const int32_t *seq_ids, *pos;
     int ldq, ldo, layer, max_len, splits;
+    int kv_planes;            // slots x 28 layers x 8 KV heads in the cache
     float *part_m, *part_l, *part_o;   // split-KV partials (splits > 1)
 };
 

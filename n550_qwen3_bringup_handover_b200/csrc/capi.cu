@@ -516,6 +516,7 @@ int n550_attention_decode(void *stream, const uint16_t *q, int ldq, const uint16
     AttnDecodeArgs a{};
     a.q_bf16 = q; a.kc = k_cache; a.vc = v_cache; a.out = out; a.seq_ids = seq_ids; a.pos = pos;
     a.ldq = ldq; a.ldo = ldo; a.layer = layer; a.max_len = max_len;
+    a.kv_planes = n_slots * 28 * 8;
     a.splits = 1;
     const size_t need = n550_attention_decode_workspace(n_seqs, max_len);
     if (workspace && workspace_bytes >= need && ((uintptr_t)workspace & 15) == 0) {

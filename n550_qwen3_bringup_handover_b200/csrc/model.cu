@@ -692,6 +692,7 @@ int run_attention(n550_model *m, cudaStream_t st, int T, bool decode, const int3
         a.kc = m->kc; a.vc = m->vc; a.out = m->attn;
         a.seq_ids = seq_ids; a.pos = pos;
         a.ldq = QD; a.ldo = QD; a.layer = l; a.max_len = c.max_len;
+        a.kv_planes = c.max_seqs * NLAYER * NKVH;
         a.splits = attn_decode_splits(T, c.max_len, MAX_SPLITS);
         a.part_m = m->part_m; a.part_l = m->part_l; a.part_o = m->part_o;
         STEP(N550_PROF_ATTN, a.splits > 1 ? 2 : 1, launch_attn_decode(st, a, T));
