@@ -155,10 +155,15 @@ int n550_gemm_tile_config(int bn);
  * the M rows (tokens) as its N side, K split over a thread-block cluster whose
  * partial tiles are summed on chip, the residual / SwiGLU / q-k-v epilogues
  * fused. 0 (default): fast-mode GEMMs and decoder layers with M <= 32 rows
- * take it; 1-16: every M <= 128 takes it with that cluster size; -1: off
+ * (n550_gemm_skinny_rows) take it; 1-16: every M <= 512 takes it with that
+ * cluster size; -1: off
  * (such GEMMs split K into FP32 partials in global memory). A tuning knob;
  * results change only by FP32 summation order. */
 int n550_gemm_skinny_config(int cs);
+
+/* Largest M (0-512, default 32) that takes the skinny-token GEMM automatically
+ * (n550_gemm_skinny_config 0). A tuning knob. */
+int n550_gemm_skinny_rows(int m);
 
 /* Programmatic dependent launch (default on): every kernel of the library is
  * launched so that it may start while the previous kernel of its stream

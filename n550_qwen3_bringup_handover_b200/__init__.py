@@ -71,6 +71,7 @@ def lib() -> C.CDLL:
         "n550_gemm_tile_config": (i, [i]),
         "n550_set_pdl": (i, [i]),
         "n550_gemm_skinny_config": (i, [i]),
+        "n550_gemm_skinny_rows": (i, [i]),
         "n550_gemm_swiglu": (i, [vp, vp, i, vp, vp, i, vp, i, i, i, i]),
         "n550_rope": (i, [vp, vp, i, i, i]),
         "n550_silu_mul": (i, [vp, vp, vp, sz]),

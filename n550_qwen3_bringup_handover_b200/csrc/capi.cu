@@ -390,6 +390,12 @@ int n550_gemm_skinny_config(int cs) {
     return N550_OK;
 }
 
+int n550_gemm_skinny_rows(int m) {
+    if (m < 0 || m > SK_MAX_T) return N550_ERR_ARG;
+    g_skinny_rows = m;
+    return N550_OK;
+}
+
 int n550_set_pdl(int on) {
     g_pdl = on != 0;
     return N550_OK;

@@ -7,14 +7,16 @@
 // weights per layer against a few hundred KB of activations. The layout is
 // chosen for that:
 //  * the weight rows are the MMA's M side (128 output features per tile, one
-//    TMEM lane each) and the tokens its N side (TN = 32/64/128 columns), so
-//    every tcgen05.mma covers all tokens at once;
-//  * K is split over a thread-block cluster of CS CTAs (CS <= 16) so that
-//    ~128-256 CTAs stream weights in parallel; every CTA requests all of its
-//    k-tiles at once (<= 8 stages of 16 KB of weights + TN x 128 B of
-//    activations), the weight tiles before the programmatic-dependent-launch
-//    wait (no kernel writes weights), so they stream while the previous
-//    kernel finishes;
+//    TMEM lane each) and the tokens its N side (TN = 32 columns for up to 32
+//    tokens, else 64-column token tiles), so every tcgen05.mma covers a whole
+//    token tile;
+//  * K is split over a thread-block cluster of CS CTAs (CS <= 16) until
+//    ~128-256 CTAs stream weights in parallel; each CTA's k-tiles (16 KB of
+//    weights + TN x 128 B of activations each) go through a ring of up to 8
+//    stages -- usually all of them at once -- and the first ring pass of
+//    weight tiles is requested before the programmatic-dependent-launch wait
+//    (no kernel writes weights), so it streams while the previous kernel
+//    finishes;
 //  * the CS partial accumulators are summed through distributed shared
 //    memory: CTA r owns token columns [r*tno, (r+1)*tno) of the tile, every
 //    CTA writes each column of its partial into the owner's receive slots,
@@ -36,11 +38,11 @@ namespace {
 
 constexpr int SK_THREADS = 192;        // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int SK_BK = 64;              // K per stage (one 128-byte swizzle row)
-constexpr int SK_MAX_KT = 8;           // stages (k-tiles) per CTA
+constexpr int SK_MAX_STAGES = 8;       // operand ring depth
 constexpr int SK_W_BYTES = 128 * SK_BK * 2;
 constexpr int SK_MAX_CS = 16;
 constexpr int SK_SMEM_MAX = 232448;    // opt-in shared memory per CTA
-constexpr int SK_BAR_BYTES = 8 * (SK_MAX_KT + 2) + 16;
+constexpr int SK_BAR_BYTES = 8 * (2 * SK_MAX_STAGES + 2) + 16;
 constexpr int HEAD = 128;
 constexpr int N_LAYERS = 28, N_KV_HEADS = 8;
 constexpr float NORM_EPS = 1e-6f;
@@ -55,8 +57,10 @@ struct SkCfg {
 struct SkParams {
     int T, N, K;
     int kt_per;         // k-tiles per CTA of the cluster
+    int stages;         // operand ring depth (<= SK_MAX_STAGES)
     int n_ttiles;       // token tiles
     int recv_off;       // shared-memory offset of the receive slots
+    int aux_off;        // QKV: positions, slots and RoPE rows of the owned tokens
     int bar_off;        // shared-memory offset of the barriers
     SkEpilogue ep;
 };
@@ -73,16 +77,17 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
     using Cfg = SkCfg<TN>;
     constexpr bool SILU = EPI == SK_EPI_SILU;
     // Global reads of the epilogue are issued before the accumulator wait:
-    // residual values of up to PF owned columns per thread (RESID), and
-    // positions, slots and RoPE factors of up to QT tokens per warp (QKV).
+    // residual values of up to PF owned columns per thread (RESID), and the
+    // positions, slots and RoPE rows of the owned tokens into shared memory
+    // (QKV).
     constexpr int PF = EPI == SK_EPI_RESID ? 32 : 1;
-    constexpr int QT = EPI == SK_EPI_QKV ? 8 : 1;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     float *stage = (float *)base;                         // [TN][128] own partial, after the MMAs
     float *recv = (float *)(base + p.recv_off);           // [cs][tno][128] peers' partials
-    uint64_t *full = (uint64_t *)(base + p.bar_off);      // [SK_MAX_KT], single use
-    uint64_t *tfull = full + SK_MAX_KT;                   // accumulator complete
+    uint64_t *full = (uint64_t *)(base + p.bar_off);      // [SK_MAX_STAGES] operands landed
+    uint64_t *empty = full + SK_MAX_STAGES;               // [SK_MAX_STAGES] operands consumed
+    uint64_t *tfull = empty + SK_MAX_STAGES;              // accumulator complete
     uint64_t *rfull = tfull + 1;                          // peers' slices received
     uint32_t *tmem_slot = (uint32_t *)(rfull + 1);
 
@@ -98,7 +103,7 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
     const int c_beg = r * tno, c_end = c_beg + ncols(r);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < SK_MAX_KT; s++) mbar_init(&full[s], 1);
+        for (int s = 0; s < SK_MAX_STAGES; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         mbar_init(tfull, 1);
         mbar_init(rfull, 1);
         fence_mbar_init();
@@ -120,40 +125,52 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
 
     bool ok = true;
     float xv[PF];
-    int qpos[QT], qseq[QT];
-    float2 qrope[QT][2];
     float qw[4];
+    int *apos = (int *)(base + p.aux_off);                // QKV: [tno] positions
+    int *aseq = apos + tno;                               //      [tno] KV slots
+    float2 *arope = (float2 *)(base + p.aux_off + ((tno * 8 + 15) & ~15));   // [tno][64]
     if (warp == 0) {
         if (lane == 0) {
-            // all weight tiles of this CTA, before the wait for the previous kernel
-            for (int i = 0; i < nkt; i++) {
-                uint8_t *sW = base + i * Cfg::STAGE;
+            auto load_w = [&](int i) {
+                const int st = i % p.stages;
+                uint8_t *sW = base + st * Cfg::STAGE;
                 const int k = (kt0 + i) * SK_BK;
-                mbar_arrive_expect_tx(&full[i], Cfg::STAGE);
+                mbar_arrive_expect_tx(&full[st], Cfg::STAGE);
                 if (SILU) {   // 64 gate rows over 64 up rows of the same features
-                    tma_load_2d(sW, &tmW, &full[i], k, ft * 64);
-                    tma_load_2d(sW + 64 * 128, &tmW2, &full[i], k, ft * 64);
+                    tma_load_2d(sW, &tmW, &full[st], k, ft * 64);
+                    tma_load_2d(sW + 64 * 128, &tmW2, &full[st], k, ft * 64);
                 } else {
-                    tma_load_2d(sW, &tmW, &full[i], k, ft * 128);
+                    tma_load_2d(sW, &tmW, &full[st], k, ft * 128);
                 }
-            }
+            };
+            // the first ring pass of weight tiles, before the wait for the
+            // previous kernel
+            const int pre = min(nkt, p.stages);
+            for (int i = 0; i < pre; i++) load_w(i);
             dep_wait();
-            for (int i = 0; i < nkt; i++)
-                tma_load_2d(base + i * Cfg::STAGE + SK_W_BYTES, &tmX, &full[i], (kt0 + i) * SK_BK,
-                            tt * TN);
+            for (int i = 0; i < nkt && ok; i++) {
+                const int st = i % p.stages;
+                if (i >= pre) {
+                    if (!(ok = mbar_wait(&empty[st], (uint32_t)(((i / p.stages) & 1) ^ 1)))) break;
+                    load_w(i);
+                }
+                tma_load_2d(base + st * Cfg::STAGE + SK_W_BYTES, &tmX, &full[st], (kt0 + i) * SK_BK, tt * TN);
+            }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc_bf16(128, TN);
             for (int i = 0; i < nkt && ok; i++) {
-                if (!(ok = mbar_wait(&full[i], 0))) break;
+                const int st = i % p.stages;
+                if (!(ok = mbar_wait(&full[st], (uint32_t)((i / p.stages) & 1)))) break;
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(base + i * Cfg::STAGE);
+                const uint32_t a0 = smem_u32(base + st * Cfg::STAGE);
                 const uint32_t b0 = a0 + SK_W_BYTES;
 #pragma unroll
                 for (int ks = 0; ks < SK_BK / 16; ks++)
                     umma_bf16(tmem, umma_desc_sw128(a0 + ks * 32), umma_desc_sw128(b0 + ks * 32), idesc,
                               (i | ks) != 0 ? 1u : 0u);
+                umma_commit(&empty[st]);
             }
             umma_commit(tfull);
         }
@@ -168,24 +185,26 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
                 xv[j] = (c_beg + j < c_end && t < p.T && n < p.N) ? p.ep.out[(size_t)t * p.ep.ldo + n] : 0.f;
             }
         }
-        if (EPI == SK_EPI_QKV && c_end - c_beg <= 4 * QT) {
-            // tokens c_beg + (warp - 2) + 4 k of this warp
-#pragma unroll
-            for (int k = 0; k < QT; k++) {
-                const int c = c_beg + (warp - 2) + 4 * k, t = tt * TN + c;
-                const bool v = c < c_end && t < p.T;
-                qpos[k] = v ? p.ep.tok_pos[t] : 0;
-                qseq[k] = v ? p.ep.tok_seq[t] : 0;
+        if (EPI == SK_EPI_QKV) {
+            // positions and slots of the owned tokens, then their RoPE rows
+            // (64 (cos, sin) pairs = 512 B each) into shared memory
+            const int i = threadIdx.x - 64;
+            for (int c = c_beg + i; c < c_end; c += 128) {
+                const int t = tt * TN + c;
+                apos[c - c_beg] = t < p.T ? p.ep.tok_pos[t] : 0;
+                aseq[c - c_beg] = t < p.T ? p.ep.tok_seq[t] : 0;
             }
+            named_bar_sync(1, 128);
             if (ft < 24) {
                 const uint16_t *w = ft < 16 ? p.ep.q_norm : p.ep.k_norm;
 #pragma unroll
                 for (int j = 0; j < 4; j++) qw[j] = bf16_bits_to_f32(w[lane + 32 * j]);
-#pragma unroll
-                for (int k = 0; k < QT; k++)
-#pragma unroll
-                    for (int j = 0; j < 2; j++)
-                        qrope[k][j] = p.ep.rope[(size_t)qpos[k] * 64 + lane + 32 * j];
+                const int n16 = (c_end - c_beg) * 32;         // 16-byte pieces
+#pragma unroll 4
+                for (int idx = i; idx < n16; idx += 128) {
+                    const int k = idx >> 5, piece = idx & 31;
+                    ((uint4 *)(arope + k * 64))[piece] = ((const uint4 *)(p.ep.rope + (size_t)apos[k] * 64))[piece];
+                }
             }
         }
         ok = mbar_wait(tfull, 0);
@@ -299,29 +318,14 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
             // token, lane holds features lane + 32 j (RoPE pairs j, j + 2), as
             // in the unfused per-head kernel.
             const int hd = ft;
-            const bool pre = c_end - c_beg <= 4 * QT;
-            if (!pre && hd < 24) {
-                const uint16_t *w = hd < 16 ? ep.q_norm : ep.k_norm;
-#pragma unroll
-                for (int j = 0; j < 4; j++) qw[j] = bf16_bits_to_f32(w[lane + 32 * j]);
-            }
 #pragma unroll 1
-            for (int c = c_beg + (warp - 2), k = 0; c < c_end; c += 4, k++) {
+            for (int c = c_beg + (warp - 2); c < c_end; c += 4) {
                 const int t = tt * TN + c;
                 if (t >= p.T) break;
-                int pos, seq;
+                const int pos = apos[c - c_beg], seq = aseq[c - c_beg];
                 float2 rp[2];
-                if (pre) {
-                    // k < QT: select the prefetched values (static indices)
-#pragma unroll
-                    for (int kk = 0; kk < QT; kk++)
-                        if (kk == k) { pos = qpos[kk]; seq = qseq[kk]; rp[0] = qrope[kk][0]; rp[1] = qrope[kk][1]; }
-                } else {
-                    pos = ep.tok_pos[t];
-                    seq = ep.tok_seq[t];
-                    if (hd < 24)
-                        for (int j = 0; j < 2; j++) rp[j] = ep.rope[(size_t)pos * 64 + lane + 32 * j];
-                }
+                if (hd < 24)
+                    for (int j = 0; j < 2; j++) rp[j] = arope[(c - c_beg) * 64 + lane + 32 * j];
                 float v[4] = {0.f, 0.f, 0.f, 0.f};
                 for (int s = 0; s < cs; s++) {
                     const float *src = s == r ? stage + c * 128 : recv + (s * tno + c - c_beg) * 128;
@@ -369,15 +373,23 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constan
     if (warp == 1) tmem_dealloc(tmem, TN);
 }
 
-// Shared memory: [operand stages | own partial [TN][128] FP32 once the MMAs
-// are done][receive slots [cs][tno][128] FP32][barriers].
-int sk_stage_region(int tn, int kt_per) {
+// Shared memory: [operand ring | own partial [TN][128] FP32 once the MMAs are
+// done][receive slots [cs][tno][128] FP32][QKV: positions, slots, RoPE rows of
+// the owned tokens][barriers].
+struct SkLayout {
+    int stage_region, recv_off, aux_off, bar_off, smem;
+};
+SkLayout sk_layout(int tn, int stages, int cs, int epi) {
+    SkLayout l;
     const int stage = 128 * SK_BK * 2 + tn * SK_BK * 2;
-    return std::max(kt_per * stage, tn * 128 * 4);
-}
-int sk_recv_bytes(int tn, int cs) { return cs > 1 ? cs * ((tn + cs - 1) / cs) * 128 * 4 : 0; }
-int sk_smem_bytes(int tn, int kt_per, int cs) {
-    return 1024 + sk_stage_region(tn, kt_per) + sk_recv_bytes(tn, cs) + SK_BAR_BYTES;
+    const int tno = (tn + cs - 1) / cs;
+    l.stage_region = std::max(stages * stage, tn * 128 * 4);
+    l.recv_off = l.stage_region;
+    l.aux_off = l.recv_off + (cs > 1 ? cs * tno * 128 * 4 : 0);
+    const int aux = epi == SK_EPI_QKV ? ((tno * 8 + 15) & ~15) + tno * 64 * 8 : 0;
+    l.bar_off = (l.aux_off + aux + 15) & ~15;
+    l.smem = 1024 + l.bar_off + SK_BAR_BYTES;
+    return l;
 }
 
 void sk_config(cudaLaunchConfig_t *cfg, cudaLaunchAttribute *attr, cudaStream_t st, int ctas, int cs,
@@ -437,42 +449,25 @@ bool sk_cluster_fits(int cs, int smem) {
 
 template <int TN, int EPI>
 int sk_launch(cudaStream_t st, const CUtensorMap &tw, const CUtensorMap &tw2, const CUtensorMap &tx,
-              const SkParams &p, int tiles, int cs, int smem) {
+              const SkParams &p, int ctas, int cs, int smem) {
     int rc = sk_prepare<TN, EPI>();
     if (rc) return rc;
     cudaLaunchConfig_t cfg;
     cudaLaunchAttribute attr[2];
-    sk_config(&cfg, attr, st, tiles * cs, cs, smem);
+    sk_config(&cfg, attr, st, ctas, cs, smem);
     N550_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_skinny_kernel<TN, EPI>, tw, tw2, tx, p));
     return N550_OK;
 }
 
 template <int TN>
 int sk_dispatch(cudaStream_t st, int epi, const CUtensorMap &tw, const CUtensorMap &tw2,
-                const CUtensorMap &tx, const SkParams &p, int tiles, int cs, int smem) {
+                const CUtensorMap &tx, const SkParams &p, int ctas, int cs, int smem) {
     switch (epi) {
-    case SK_EPI_F32: return sk_launch<TN, SK_EPI_F32>(st, tw, tw2, tx, p, tiles, cs, smem);
-    case SK_EPI_RESID: return sk_launch<TN, SK_EPI_RESID>(st, tw, tw2, tx, p, tiles, cs, smem);
-    case SK_EPI_SILU: return sk_launch<TN, SK_EPI_SILU>(st, tw, tw2, tx, p, tiles, cs, smem);
-    case SK_EPI_QKV: return sk_launch<TN, SK_EPI_QKV>(st, tw, tw2, tx, p, tiles, cs, smem);
+    case SK_EPI_F32: return sk_launch<TN, SK_EPI_F32>(st, tw, tw2, tx, p, ctas, cs, smem);
+    case SK_EPI_RESID: return sk_launch<TN, SK_EPI_RESID>(st, tw, tw2, tx, p, ctas, cs, smem);
+    case SK_EPI_SILU: return sk_launch<TN, SK_EPI_SILU>(st, tw, tw2, tx, p, ctas, cs, smem);
+    case SK_EPI_QKV: return sk_launch<TN, SK_EPI_QKV>(st, tw, tw2, tx, p, ctas, cs, smem);
     default: return N550_ERR_ARG;
-    }
-}
-
-// K split: kt_per k-tiles for each of *cs CTAs (none empty; the stages fit
-// the shared memory). False when no split of at most SK_MAX_CS CTAs does.
-bool sk_plan(int tn, int num_k, int *cs, int *kt_per) {
-    int c = std::min(std::min(std::max(*cs, 1), SK_MAX_CS), num_k);
-    for (;; c++) {
-        if (c > SK_MAX_CS) return false;
-        const int kt = (num_k + c - 1) / c;
-        const int used = (num_k + kt - 1) / kt;           // no CTA without k-tiles
-        if (kt <= SK_MAX_KT && sk_smem_bytes(tn, kt, used) <= SK_SMEM_MAX) {
-            if (used > tn) return false;                  // every rank owns a column
-            *cs = used;
-            *kt_per = kt;
-            return true;
-        }
     }
 }
 
@@ -486,17 +481,47 @@ bool sk_fits(int tn, int epi, int cs, int smem) {
     case 64 * 4 + SK_EPI_RESID: return sk_cluster_fits<64, SK_EPI_RESID>(cs, smem);
     case 64 * 4 + SK_EPI_SILU: return sk_cluster_fits<64, SK_EPI_SILU>(cs, smem);
     case 64 * 4 + SK_EPI_QKV: return sk_cluster_fits<64, SK_EPI_QKV>(cs, smem);
-    case 128 * 4 + SK_EPI_F32: return sk_cluster_fits<128, SK_EPI_F32>(cs, smem);
-    case 128 * 4 + SK_EPI_RESID: return sk_cluster_fits<128, SK_EPI_RESID>(cs, smem);
-    case 128 * 4 + SK_EPI_SILU: return sk_cluster_fits<128, SK_EPI_SILU>(cs, smem);
-    case 128 * 4 + SK_EPI_QKV: return sk_cluster_fits<128, SK_EPI_QKV>(cs, smem);
     default: return false;
     }
+}
+
+int sk_num_sms() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0, v = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess &&
+            cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
+            n = v;
+        else
+            n = 148;
+    }
+    return n;
+}
+
+// K split and ring depth for `tiles` output tiles: cs CTAs per tile with
+// kt_per k-tiles each (none empty), `stages` ring slots -- all k-tiles when
+// they fit, fewer so that two CTAs share an SM when the grid exceeds the SMs.
+bool sk_plan(int tn, int epi, int tiles, int num_k, int *cs, int *kt_per, int *stages, SkLayout *lay) {
+    int c = std::min(std::min(std::max(*cs, 1), SK_MAX_CS), num_k);
+    const int kt = (num_k + c - 1) / c;
+    c = (num_k + kt - 1) / kt;
+    if (c > tn) return false;                             // every rank owns a column
+    const int limit = tiles * c > sk_num_sms() ? (233472 - 2 * 1024) / 2 : SK_SMEM_MAX;
+    int sg = std::min(kt, SK_MAX_STAGES);
+    while (sg > 2 && sk_layout(tn, sg, c, epi).smem > limit) sg--;
+    const SkLayout l = sk_layout(tn, sg, c, epi);
+    if (l.smem > SK_SMEM_MAX) return false;
+    *cs = c;
+    *kt_per = kt;
+    *stages = sg;
+    *lay = l;
+    return true;
 }
 
 }  // namespace
 
 int g_skinny_cs = 0;
+int g_skinny_rows = SK_AUTO_T;
 
 int launch_gemm_skinny(cudaStream_t st, int epi, const uint16_t *x, int ldx, const uint16_t *w,
                        const uint16_t *w2, int ldw, int T, int N, int K, const SkEpilogue &ep, int cs) {
@@ -509,22 +534,24 @@ int launch_gemm_skinny(cudaStream_t st, int epi, const uint16_t *x, int ldx, con
     if (epi == SK_EPI_QKV && (N != 32 * HEAD || !ep.kc || !ep.vc || !ep.tok_pos || !ep.tok_seq ||
                               !ep.rope || !ep.q_norm || !ep.k_norm || (!ep.q_f32 && !ep.q_bf16)))
         return N550_ERR_ARG;
-    const int tn = T <= 32 ? 32 : (T <= 64 ? 64 : 128);
+    const int tn = T <= 32 ? 32 : 64;
+    const int n_tt = (T + tn - 1) / tn;
     const int rows = silu ? 64 : 128;
-    const int n_ft = (N + rows - 1) / rows;
-    const int tiles = n_ft;                               // one token tile (T <= 128)
+    const int tiles = (N + rows - 1) / rows * n_tt;
     const int num_k = (K + SK_BK - 1) / SK_BK;
     if (cs <= 0 && g_skinny_cs > 0) cs = g_skinny_cs;
     if (cs <= 0) {
         // enough CTAs to stream the weights from ~all SMs
         cs = 1;
-        while (cs < SK_MAX_CS && tiles * cs < 128 && 2 * cs <= num_k) cs *= 2;
+        while (cs < SK_MAX_CS && tiles * cs < 120 && 2 * cs <= num_k) cs *= 2;
     }
-    int kt_per = 0;
-    if (!sk_plan(tn, num_k, &cs, &kt_per)) return N550_ERR_UNSUPPORTED;
-    if (!sk_fits(tn, epi, cs, sk_smem_bytes(tn, kt_per, cs))) {
+    int kt_per = 0, stages = 0;
+    SkLayout lay;
+    if (!sk_plan(tn, epi, tiles, num_k, &cs, &kt_per, &stages, &lay)) return N550_ERR_UNSUPPORTED;
+    if (!sk_fits(tn, epi, cs, lay.smem)) {
         cs = 8;      // portable cluster size
-        if (!sk_plan(tn, num_k, &cs, &kt_per) || cs > 8) return N550_ERR_UNSUPPORTED;
+        if (!sk_plan(tn, epi, tiles, num_k, &cs, &kt_per, &stages, &lay) || cs > 8)
+            return N550_ERR_UNSUPPORTED;
     }
     int rc = N550_OK;
     CUtensorMap tw, tw2, tx;
@@ -540,17 +567,14 @@ int launch_gemm_skinny(cudaStream_t st, int epi, const uint16_t *x, int ldx, con
     p.N = N;
     p.K = K;
     p.kt_per = kt_per;
-    p.n_ttiles = 1;
-    p.recv_off = sk_stage_region(tn, kt_per);
-    p.bar_off = p.recv_off + sk_recv_bytes(tn, cs);
+    p.stages = stages;
+    p.n_ttiles = n_tt;
+    p.recv_off = lay.recv_off;
+    p.aux_off = lay.aux_off;
+    p.bar_off = lay.bar_off;
     p.ep = ep;
-    const int smem = sk_smem_bytes(tn, kt_per, cs);
-    if (smem > SK_SMEM_MAX) return N550_ERR_UNSUPPORTED;
-    switch (tn) {
-    case 32: return sk_dispatch<32>(st, epi, tw, tw2, tx, p, tiles, cs, smem);
-    case 64: return sk_dispatch<64>(st, epi, tw, tw2, tx, p, tiles, cs, smem);
-    default: return sk_dispatch<128>(st, epi, tw, tw2, tx, p, tiles, cs, smem);
-    }
+    if (tn == 32) return sk_dispatch<32>(st, epi, tw, tw2, tx, p, tiles * cs, cs, lay.smem);
+    return sk_dispatch<64>(st, epi, tw, tw2, tx, p, tiles * cs, cs, lay.smem);
 }
 
 }  // namespace n550

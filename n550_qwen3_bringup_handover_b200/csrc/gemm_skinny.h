@@ -30,22 +30,25 @@ struct SkEpilogue {
     const float2 *rope;         // [max_len][64] (cos, sin)
 };
 
-// n550_gemm_skinny_config: 0 = automatic (the skinny GEMM for M <= SK_AUTO_T
-// rows), 1-16 = the skinny GEMM for every M <= SK_MAX_T with that cluster size,
-// -1 = off (such GEMMs take the split-K path).
+// n550_gemm_skinny_config: 0 = automatic (the skinny GEMM for M <=
+// g_skinny_rows rows), 1-16 = the skinny GEMM for every M <= SK_MAX_T with that
+// cluster size, -1 = off (such GEMMs take the split-K path).
 extern int g_skinny_cs;
 
-// Largest token count the skinny GEMM takes, and the largest it is chosen for
-// automatically: measured on B200 in graph-replayed decode steps, it is ahead
-// of the split-K GEMMs with their separate reduction kernels at 32 tokens
-// (1.82 vs 1.95 ms per step) and behind at 64 and 128 (2.72 vs 2.53 and 4.80
-// vs 3.93 ms), where the partial tiles it exchanges grow with the tokens.
-constexpr int SK_MAX_T = 128;
+// Largest token count the skinny GEMM takes (tokens beyond 32 in 64-column
+// tiles), and the largest it is chosen for automatically: measured on B200 in
+// graph-replayed decode steps (1024-token context) it is ahead of the split-K
+// GEMMs with their separate reduction kernels at 16 and 32 tokens (1.50 vs
+// 1.72, 1.68 vs 1.77 ms per step) and behind from 64 on (2.43 vs 2.37, 4.09
+// vs 3.63, 6.52 vs 6.30 ms at 64/128/256), where its per-CTA partial tiles
+// and token-tile epilogues grow with the tokens.
+constexpr int SK_MAX_T = 512;
+extern int g_skinny_rows;     // n550_gemm_skinny_rows: automatic limit (default SK_AUTO_T)
 constexpr int SK_AUTO_T = 32;
 
 // Whether a fast-mode GEMM / layer of M rows takes the skinny GEMM.
 inline bool skinny_route(int M) {
-    return g_skinny_cs == 0 ? M <= SK_AUTO_T : (g_skinny_cs > 0 && M <= SK_MAX_T);
+    return g_skinny_cs == 0 ? M <= g_skinny_rows : (g_skinny_cs > 0 && M <= SK_MAX_T);
 }
 
 // Y = X . W^T for T <= SK_MAX_T tokens with epilogue `epi`. X BF16 [T][K]
