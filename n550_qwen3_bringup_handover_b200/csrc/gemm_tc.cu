@@ -25,6 +25,7 @@
 #include "common.cuh"
 #include "gemm_tc.h"
 #include "launch.h"
+#include "ops.h"
 #include "tmap.h"
 
 namespace n550 {
@@ -214,6 +215,19 @@ __device__ __forceinline__ void load_chunk16(uint32_t taddr, float (&v)[16]) {
     for (int j = 0; j < 16; j++) v[j] = __uint_as_float(r[j]);
 }
 
+// (cos, sin) of rotation pairs i and i + 1 at position pos: the expression the
+// model's RoPE table is filled with (sincosf of pos * inv_freq[i]), evaluated
+// in registers and so bit-identical to the table. Reading the table instead
+// costs every lane its own 512-byte row -- uncoalesced L1 traffic that, in
+// the epilogue of a persistent GEMM, slowed its tensor core by a third
+// (measured on B200: 0.297 vs 0.246 ms for the 32768 x 4096 x 1024 q/k/v GEMM).
+__device__ __forceinline__ float4 rope_cs2(int pos, int i) {
+    float s0, c0, s1, c1;
+    sincosf((float)pos * c_inv_freq[i], &s0, &c0);
+    sincosf((float)pos * c_inv_freq[i + 1], &s1, &c1);
+    return make_float4(c0, s0, c1, s1);
+}
+
 // Fused QKV epilogue (qwen3.c:477-511). A 128-column tile is one head of the
 // [q 16 | k 8 | v 8] x 128 qkv row. q and k heads: RMSNorm over the head
 // (qk_norm, qwen3.c:287-292; four partial sums of squares), RoPE pairs
@@ -231,8 +245,7 @@ __device__ __forceinline__ void epilogue_qkv(const TcQkv &p, uint32_t *stg, int 
     const int mc = row_ok ? m : M - 1;
     const int pos = p.tok_pos[mc];
     const bool normed = head < 24;
-    // norm weights staged in shared memory at kernel start (the rope-table
-    // stream would evict them from L1 between chunks)
+    // norm weights staged in shared memory at kernel start
     const uint16_t *w = head < 16 ? norm_w : norm_w + 128;
     uint16_t *dst_row;                     // column 0 of this head in the destination row
     if (head < 16) {
@@ -244,16 +257,6 @@ __device__ __forceinline__ void epilogue_qkv(const TcQkv &p, uint32_t *stg, int 
         dst_row = cache + (slot * p.max_len + pos) * 128;
     }
     if (!row_ok) dst_row = nullptr;
-    // (cos, sin) of this row's position for rotation pairs 16c .. 16c + 15:
-    // 8 float4 per chunk from the L2-resident table. Chunk c + 1 is loaded
-    // while chunk c is computed (and chunk 0 during the sum of squares), so
-    // the L2 latency stays off the critical path.
-    const float4 *cs_row = (const float4 *)(p.rope + (size_t)pos * 64);
-    float4 cs_next[8];
-    if (normed) {
-#pragma unroll
-        for (int e = 0; e < 8; e++) cs_next[e] = __ldg(cs_row + e);
-    }
     float scale = 1.f;
     if (normed) {
         float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
@@ -279,13 +282,10 @@ __device__ __forceinline__ void epilogue_qkv(const TcQkv &p, uint32_t *stg, int 
         load_chunk16(taddr + 64 + 16 * c, b);
         if (c == 3 && rel) acc_release(*rel, lane);
         if (normed) {
+            // (cos, sin) of this row's position for rotation pairs 16c .. 16c + 15
             float4 cs4[8];
 #pragma unroll
-            for (int e = 0; e < 8; e++) cs4[e] = cs_next[e];
-            if (c < 3) {
-#pragma unroll
-                for (int e = 0; e < 8; e++) cs_next[e] = __ldg(cs_row + 8 * (c + 1) + e);
-            }
+            for (int e = 0; e < 8; e++) cs4[e] = rope_cs2(pos, 16 * c + 2 * e);
             // 8 norm weights per 16-byte shared load
             const uint4 *w_lo = (const uint4 *)(w + 16 * c);
             const uint4 *w_hi = (const uint4 *)(w + 64 + 16 * c);
@@ -354,7 +354,6 @@ __device__ __forceinline__ void epilogue_qkv_half(const TcQkv &p, uint32_t *stg,
         dst_row = cache + (slot * p.max_len + pos) * 128;
     }
     if (!row_ok) dst_row = nullptr;
-    const float4 *cs_row = (const float4 *)(p.rope + (size_t)pos * 64) + 16 * half;
     float scale = 1.f;
     if (normed) {
         float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
@@ -393,7 +392,7 @@ __device__ __forceinline__ void epilogue_qkv_half(const TcQkv &p, uint32_t *stg,
                 const uint32_t wlw[4] = {wl.x, wl.y, wl.z, wl.w}, whw[4] = {wh.x, wh.y, wh.z, wh.w};
 #pragma unroll
                 for (int j2 = 0; j2 < 4; j2++) {
-                    const float4 t = __ldg(cs_row + 8 * c + j8 * 4 + j2);
+                    const float4 t = rope_cs2(pos, 2 * (16 * half + 8 * c + 4 * j8 + j2));
 #pragma unroll
                     for (int e = 0; e < 2; e++) {
                         const int j = j8 * 8 + j2 * 2 + e;
@@ -1007,7 +1006,10 @@ int launch_gemm_tc_qkv(cudaStream_t st, const uint16_t *a, int lda, const uint16
     TcEpilogue ep{};
     ep.qkv = q;
     ep.vec_ok = 1;
-    if (bn == 256 && tc_use_pair(M, bn)) {
+    // Single-CTA 128 x 256 tiles unless pairs are forced: with the RoPE
+    // factors computed in registers they are ahead of 256 x 256 pairs for
+    // this epilogue (measured on B200 at M = 32768: 0.246 vs 0.258 ms).
+    if (bn == 256 && g_tile_bn == 512) {
         // pair tiles: each CTA's B box is one head (128 rows)
         if ((rc = make_tmap(&tb, w, 4096, K, K, 128))) return rc;
         return launch_impl<256, TC_EPI_QKV_ROPE, true>(st, ta, tb, tb, ep, M, 4096, K, max_ctas);

@@ -25,7 +25,8 @@ struct TcQkv {
     int layer, max_len;
     const int32_t *tok_pos, *tok_seq;   // per row
     const uint16_t *q_norm, *k_norm;    // BF16 [128]
-    const float2 *rope;        // [max_len][64] (cos, sin) of pos * inv_freq[i]
+    const float2 *rope;        // [max_len][64] (cos, sin) of pos * inv_freq[i] (the epilogue
+                               // evaluates the same values in registers)
     float eps;
 };
 
