@@ -219,8 +219,8 @@ __device__ __forceinline__ void load_chunk16(uint32_t taddr, float (&v)[16]) {
 // model's RoPE table is filled with (sincosf of pos * inv_freq[i]), evaluated
 // in registers and so bit-identical to the table. Reading the table instead
 // costs every lane its own 512-byte row -- uncoalesced L1 traffic that, in
-// the epilogue of a persistent GEMM, slowed its tensor core by a third
-// (measured on B200: 0.297 vs 0.246 ms for the 32768 x 4096 x 1024 q/k/v GEMM).
+// the epilogue of a persistent GEMM, slowed its tensor core (measured on B200
+// for the 32768 x 4096 x 1024 q/k/v GEMM: 0.297 -> 0.258 ms on CTA pairs).
 __device__ __forceinline__ float4 rope_cs2(int pos, int i) {
     float s0, c0, s1, c1;
     sincosf((float)pos * c_inv_freq[i], &s0, &c0);
@@ -1006,10 +1006,11 @@ int launch_gemm_tc_qkv(cudaStream_t st, const uint16_t *a, int lda, const uint16
     TcEpilogue ep{};
     ep.qkv = q;
     ep.vec_ok = 1;
-    // Single-CTA 128 x 256 tiles unless pairs are forced: with the RoPE
-    // factors computed in registers they are ahead of 256 x 256 pairs for
-    // this epilogue (measured on B200 at M = 32768: 0.246 vs 0.258 ms).
-    if (bn == 256 && g_tile_bn == 512) {
+    // Pair tiles from M >= 12288 as for the other projections: in the model's
+    // prefill step they are ahead of single-CTA tiles for this GEMM too
+    // (measured on B200, 64 x 512 tokens: 32.4-32.7 vs 33.1 ms per step,
+    // although an isolated launch favours single-CTA tiles, 0.246 vs 0.258 ms).
+    if (bn == 256 && tc_use_pair(M, bn)) {
         // pair tiles: each CTA's B box is one head (128 rows)
         if ((rc = make_tmap(&tb, w, 4096, K, K, 128))) return rc;
         return launch_impl<256, TC_EPI_QKV_ROPE, true>(st, ta, tb, tb, ep, M, 4096, K, max_ctas);
