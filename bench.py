@@ -184,15 +184,46 @@ def run_n550(args, world, rank, local):
         m.prefill(tok_dev, seq_ids, 0, logits, nxt)
         gather()
 
+    # End to end: every step copies its tokens in from pinned host memory and
+    # its gathered logits and next tokens out to pinned host memory (rank 0).
+    # As in a serving loop the read-back of step i runs on a copy stream while
+    # step i+1 computes, through two result buffers (device and host); the
+    # timed region ends when the last read-back has landed.
+    copy_stream = torch.cuda.Stream(dev)
+    res_logits = [torch.empty((PREFILL_SEQS, VOCAB), dtype=torch.float32, device=dev) for _ in range(2)]
+    res_next = [torch.empty(PREFILL_SEQS, dtype=torch.int32, device=dev) for _ in range(2)]
+    host_logits = [out_logits_host, torch.empty_like(out_logits_host).pin_memory()]
+    host_next = [out_next_host, torch.empty_like(out_next_host).pin_memory()]
+    ev_ready = [torch.cuda.Event() for _ in range(2)]
+    ev_copied = [torch.cuda.Event() for _ in range(2)]
+    e2e_i = [0]
+
     def step_e2e():
+        b = e2e_i[0] & 1
+        e2e_i[0] += 1
         tok_dev.copy_(tok_host, non_blocking=True)
         m.prefill(tok_dev, seq_ids, 0, logits, nxt)
-        gather()
+        stream.wait_event(ev_copied[b])              # buffer b's previous read-back is done
+        if world > 1:
+            dist.all_gather_into_tensor(res_logits[b], logits)
+            dist.all_gather_into_tensor(res_next[b], nxt)
+        else:
+            res_logits[b].copy_(logits, non_blocking=True)
+            res_next[b].copy_(nxt, non_blocking=True)
         if rank == 0:
-            out_logits_host.copy_(gathered_logits, non_blocking=True)
-            out_next_host.copy_(gathered_next, non_blocking=True)
+            ev_ready[b].record(stream)
+            copy_stream.wait_event(ev_ready[b])
+            with torch.cuda.stream(copy_stream):
+                host_logits[b].copy_(res_logits[b], non_blocking=True)
+                host_next[b].copy_(res_next[b], non_blocking=True)
+            ev_copied[b].record(copy_stream)
 
-    def timed(fn, steps, prof=False):
+    def e2e_done():
+        if rank == 0:
+            for b in range(2):
+                stream.wait_event(ev_copied[b])
+
+    def timed(fn, steps, prof=False, finish=None):
         for _ in range(args.warmup):
             fn()
         torch.cuda.synchronize(dev)
@@ -205,6 +236,8 @@ def run_n550(args, world, rank, local):
         e0.record(stream)
         for _ in range(steps):
             fn()
+        if finish:
+            finish()
         e1.record(stream)
         torch.cuda.synchronize(dev)
         barrier(world)
@@ -218,7 +251,7 @@ def run_n550(args, world, rank, local):
     with ClockSampler(local) as clk:
         ms = timed(step_device, K)
     clocks = clk.summary()
-    ms_e2e = timed(step_e2e, K)
+    ms_e2e = timed(step_e2e, K, finish=e2e_done)
     # Per-kernel breakdown and the GEMM roofline: a separate eager pass with
     # CUDA events around every launch (not used for `value`).
     timed(step_device, K, prof=True)
