@@ -89,11 +89,13 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
     __shared__ float wm[DC_WARPS][2], wl[DC_WARPS][2];
     __shared__ __align__(16) float wo[DC_WARPS][2][HD];
 
-    dep_wait();
-    dep_launch();
+    // The sequence ids and positions are inputs of the whole step (written
+    // before the kernels this one depends on; read through L2), and cache
+    // positions below pos[s] hold K/V of earlier steps. Only position pos[s]
+    // and the queries come from the kernel this launch depends on.
     const int split = blockIdx.x, kvh = blockIdx.y, s = blockIdx.z;
-    const int seq = p.seq_ids[s];
-    const int kv_len = p.pos[s] + 1;
+    const int seq = __ldcg(p.seq_ids + s);
+    const int kv_len = __ldcg(p.pos + s) + 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int chunk = (kv_len + p.splits - 1) / p.splits;
     chunk = (chunk + DC_TP - 1) / DC_TP * DC_TP;
@@ -118,8 +120,15 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
         tma_load_3d(b + 2 * DC_BOX, &tmV, &full[st], 0, t0, plane);
         tma_load_3d(b + 3 * DC_BOX, &tmV, &full[st], 64, t0, plane);
     };
+    // Tiles that end before position pos[s] are requested before waiting for
+    // the previous kernel, so their latency overlaps its tail.
+    int pre = 0;
     if (threadIdx.x == 0)
-        for (int i = 0; i < min(DC_STAGES, n_tiles); i++) issue(i);
+        while (pre < min(DC_STAGES, n_tiles) && start + (pre + 1) * DC_TP <= kv_len - 1) issue(pre++);
+    dep_wait();
+    dep_launch();
+    if (threadIdx.x == 0)
+        for (int i = pre; i < min(DC_STAGES, n_tiles); i++) issue(i);
 
     // A fragments of q (x scale x log2 e, BF16): row g = lane / 4 is query
     // head 2 kvh + g for g < 2, zero otherwise; columns 16 kk + 2 tq (+1, +8).
