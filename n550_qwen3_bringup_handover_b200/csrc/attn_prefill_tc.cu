@@ -413,9 +413,8 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
             *my_sum = l_run;
             pair_sync(bar_id);
             const float inv = 1.0f / (l_run + *other_sum);
-            const int qi = it.q0 + row;
-            uint4 *dst = (uint4 *)(p.out + ((size_t)it.s * p.L + (qi < p.L ? qi : 0)) * p.ldo +
-                                   (2 * it.kvh + t) * HD + half * 64);
+            // O / l of this row as BF16: 64 output dims = 8 chunks of 16 bytes
+            uint32_t ch[8][4];
 #pragma unroll
             for (int c = 0; c < 2; c++) {
                 uint32_t o[32];
@@ -426,16 +425,42 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                     tc_fence_before();
                     mbar_arrive(&o_free[t]);
                 }
-                if (qi < p.L) {
 #pragma unroll
-                    for (int cc = 0; cc < 4; cc++) {
-                        uint4 w;
-                        w.x = cvt_bf16x2(__uint_as_float(o[8 * cc]) * inv, __uint_as_float(o[8 * cc + 1]) * inv);
-                        w.y = cvt_bf16x2(__uint_as_float(o[8 * cc + 2]) * inv, __uint_as_float(o[8 * cc + 3]) * inv);
-                        w.z = cvt_bf16x2(__uint_as_float(o[8 * cc + 4]) * inv, __uint_as_float(o[8 * cc + 5]) * inv);
-                        w.w = cvt_bf16x2(__uint_as_float(o[8 * cc + 6]) * inv, __uint_as_float(o[8 * cc + 7]) * inv);
-                        dst[c * 4 + cc] = w;
+                for (int cc = 0; cc < 4; cc++)
+#pragma unroll
+                    for (int w = 0; w < 4; w++)
+                        ch[c * 4 + cc][w] = cvt_bf16x2(__uint_as_float(o[8 * cc + 2 * w]) * inv,
+                                                        __uint_as_float(o[8 * cc + 2 * w + 1]) * inv);
+            }
+            // Transpose the chunks within each group of 8 lanes (= 8 rows) in
+            // three butterfly exchange stages, so that store k has lane 8g + j
+            // write chunk j of row 8g + k: each store instruction covers four
+            // whole 128-byte row pieces instead of 16 bytes of 32 rows (which
+            // cost the L1 one pass per row).
+            const int j8 = lane & 7;
+#pragma unroll
+            for (int m = 1; m < 8; m <<= 1) {
+                const bool up = (j8 & m) != 0;
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    if (c & m) continue;
+#pragma unroll
+                    for (int w = 0; w < 4; w++) {
+                        const uint32_t send = up ? ch[c][w] : ch[c | m][w];
+                        const uint32_t recv = __shfl_xor_sync(0xFFFFFFFFu, send, m);
+                        if (up) ch[c][w] = recv;
+                        else ch[c | m][w] = recv;
                     }
+                }
+            }
+            const int rbase = qw * 32 + (lane & ~7);          // first row of this lane's group
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const int qk = it.q0 + rbase + k;
+                if (qk < p.L) {
+                    uint4 *d = (uint4 *)(p.out + ((size_t)it.s * p.L + qk) * p.ldo + (2 * it.kvh + t) * HD +
+                                         half * 64);
+                    d[j8] = make_uint4(ch[k][0], ch[k][1], ch[k][2], ch[k][3]);
                 }
             }
         }
