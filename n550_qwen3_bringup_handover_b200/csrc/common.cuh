@@ -83,6 +83,31 @@ __host__ __device__ __forceinline__ uint16_t f32_to_bf16_rne(float f) {
     return (uint16_t)(u >> 16);
 }
 
+// sin and cos of a RoPE angle x = pos * inv_freq (x >= 0): Cody-Waite
+// reduction x = k * pi/2 + r with pi/2 split into P1 (13 significant bits, so
+// k * P1 is exact for k < 2^11) and P2 = fl32(pi/2 - P1), then the hardware
+// sine/cosine approximations on |r| <= pi/4 (absolute error ~2^-21) and the
+// quadrant k mod 4. Reduction error <= 3e-8 for x <= 3200 (checked against
+// binary64 over every position < 3200 and all 64 frequencies); beyond that
+// sincosf. About 10 instructions instead of sincosf's ~40: the fused q/k/v
+// GEMM evaluates 32 of these per thread and tile, and every instruction its
+// epilogue saves is power the power-capped tensor cores get back (measured on
+// B200: 32.21 -> 31.89 ms per 64 x 512-token prefill step).
+__device__ __forceinline__ void rope_sincos(float x, float *s, float *c) {
+    if (!(fabsf(x) <= 3200.0f)) {
+        sincosf(x, s, c);
+        return;
+    }
+    const float k = rintf(x * 0.636619772367581343f);          // 2 / pi
+    float r = fmaf(-k, 1.57080078125f, x);                     // P1 = 0x1.922p+0
+    r = fmaf(-k, -4.454454938240815e-06f, r);                  // P2 = -0x1.2aeef4p-18
+    const float sr = __sinf(r), cr = __cosf(r);
+    const int q = (int)k & 3;
+    const float sv = (q & 1) ? cr : sr, cv = (q & 1) ? sr : cr;
+    *s = (q & 2) ? -sv : sv;
+    *c = ((q + 1) & 2) ? -cv : cv;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return (uint32_t)f32_to_bf16_rne(lo) | ((uint32_t)f32_to_bf16_rne(hi) << 16);
 }

@@ -216,15 +216,16 @@ __device__ __forceinline__ void load_chunk16(uint32_t taddr, float (&v)[16]) {
 }
 
 // (cos, sin) of rotation pairs i and i + 1 at position pos: the expression the
-// model's RoPE table is filled with (sincosf of pos * inv_freq[i]), evaluated
-// in registers and so bit-identical to the table. Reading the table instead
-// costs every lane its own 512-byte row -- uncoalesced L1 traffic that, in
-// the epilogue of a persistent GEMM, slowed its tensor core (measured on B200
-// for the 32768 x 4096 x 1024 q/k/v GEMM: 0.297 -> 0.258 ms on CTA pairs).
+// model's RoPE table is filled with (rope_sincos of pos * inv_freq[i]),
+// evaluated in registers and so bit-identical to the table. Reading the table
+// instead costs every lane its own 512-byte row -- uncoalesced L1 traffic
+// that, in the epilogue of a persistent GEMM, slowed its tensor core (measured
+// on B200 for the 32768 x 4096 x 1024 q/k/v GEMM: 0.297 -> 0.258 ms on CTA
+// pairs).
 __device__ __forceinline__ float4 rope_cs2(int pos, int i) {
     float s0, c0, s1, c1;
-    sincosf((float)pos * c_inv_freq[i], &s0, &c0);
-    sincosf((float)pos * c_inv_freq[i + 1], &s1, &c1);
+    rope_sincos((float)pos * c_inv_freq[i], &s0, &c0);
+    rope_sincos((float)pos * c_inv_freq[i + 1], &s1, &c1);
     return make_float4(c0, s0, c1, s1);
 }
 

@@ -284,12 +284,13 @@ qknorm_rope_kv_kernel(const float *__restrict__ qkv, int ldqkv, int ks, size_t s
 }
 
 // (cos, sin) of pos * inv_freq[i] for every position and rotation pair: the
-// RoPE factors of ops_scalar.c:21-35, computed once per model.
+// RoPE factors of ops_scalar.c:21-35, computed once per model with the same
+// function the fused q/k/v GEMM epilogue evaluates in registers.
 __global__ void rope_table_kernel(float2 *t, int max_len) {
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= max_len * 64) return;
     float s, c;
-    sincosf((float)(idx >> 6) * c_inv_freq[idx & 63], &s, &c);
+    rope_sincos((float)(idx >> 6) * c_inv_freq[idx & 63], &s, &c);
     t[idx] = make_float2(c, s);
 }
 
