@@ -1,7 +1,7 @@
 """Regenerate the committed golden fixtures (run in a container that has the
 reference checkout; the fixtures themselves travel, the reference does not).
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <path of the reference checkout>
 
 Writes
   tests/golden/ame_cases.npz   the 12 shipped AME cases of
