@@ -789,7 +789,12 @@ int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t
     int rc = N550_OK;
     *xl_ready = false;
     const bool exact = c.gemm_mode == N550_MODE_EXACT;
-    if (!exact && T > 8 && skinny_route(T))
+    // From 4 tokens on the skinny GEMMs (7 kernels per layer) beat the GEMV
+    // path (10); below, the GEMV's shorter launches win. Measured on B200,
+    // graph-replayed decode steps with the lm_head routed alike: 1, 2, 4, 8
+    // sequences 886 / 986 / 1132 / 1563 us (GEMV) vs 1065 / 1081 / 1082 /
+    // 1189 us (skinny) per step.
+    if (!exact && T >= 4 && skinny_route(T))
         return run_layers_skinny(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, xl_ready);
     if (!exact && T > 8 && T < 1024)
         return run_layers_split(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, xl_ready);
@@ -835,7 +840,7 @@ int run_head(n550_model *m, cudaStream_t st, int Sc, int Lc, float *logits, int3
     int rc = N550_OK;
     if (!xl_ready)
         STEP(N550_PROF_RMSNORM, 1, launch_final_norm(st, m->xl, m->x, m->t[N_TENSORS - 1], Sc, Lc));
-    if (!logits && next && m->cfg.gemm_mode == N550_MODE_FAST && Sc > 8) {
+    if (!logits && next && m->cfg.gemm_mode == N550_MODE_FAST && Sc >= 4) {
         STEP(N550_PROF_GEMM_LMHEAD, 2,
              launch_gemm_tc_argmax(st, m->xl, H, m->t[0], H, Sc, VOCAB, H, m->ws, m->ws_bytes, next));
         return N550_OK;
