@@ -127,6 +127,76 @@ gemv_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict_
     }
 }
 
+// Gate and up rows of output n in one warp (h = silu(x . wg[n]) * (x . wu[n])
+// as BF16, ops_scalar.c:46-51): the SwiGLU of the few-token decode step in one
+// launch instead of two GEMVs and an elementwise kernel. Same per-row loop and
+// reduction order as gemv_kernel, so g and u are the values those GEMVs give.
+template <int MM>
+__global__ void __launch_bounds__(GV_WARPS * 32)
+gemv_swiglu_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict__ wg,
+                   const uint16_t *__restrict__ wu, int ldb, uint16_t *h, int ldh, int N, int K) {
+    dep_wait();
+    dep_launch();
+    const int lane = threadIdx.x & 31;
+    const int n = blockIdx.x * GV_WARPS + (threadIdx.x >> 5);
+    if (n >= N) return;
+    const uint16_t *grow = wg + (size_t)n * ldb, *urow = wu + (size_t)n * ldb;
+    float ag[MM], au[MM];
+#pragma unroll
+    for (int m = 0; m < MM; m++) ag[m] = au[m] = 0.f;
+    for (int k0 = lane * 8; k0 < K; k0 += 32 * 8 * 4) {
+        uint4 gq[4], uq[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int k = k0 + u * 256;
+            gq[u] = (k < K) ? __ldcs((const uint4 *)(grow + k)) : make_uint4(0, 0, 0, 0);
+            uq[u] = (k < K) ? __ldcs((const uint4 *)(urow + k)) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int k = k0 + u * 256;
+            if (k >= K) break;
+            float gf[8], uf[8];
+            bf16x8_to_f32(gq[u], gf);
+            bf16x8_to_f32(uq[u], uf);
+#pragma unroll
+            for (int m = 0; m < MM; m++) {
+                const uint4 aq = __ldg((const uint4 *)(a + (size_t)m * lda + k));
+                float af[8];
+                bf16x8_to_f32(aq, af);
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    ag[m] = fmaf(af[j], gf[j], ag[m]);
+                    au[m] = fmaf(af[j], uf[j], au[m]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < MM; m++) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            ag[m] += __shfl_xor_sync(0xFFFFFFFFu, ag[m], o);
+            au[m] += __shfl_xor_sync(0xFFFFFFFFu, au[m], o);
+        }
+    }
+    if (lane < MM) {
+        float g = ag[0], u = au[0];
+#pragma unroll
+        for (int m = 1; m < MM; m++)
+            if (lane == m) { g = ag[m]; u = au[m]; }
+        h[(size_t)lane * ldh + n] = f32_to_bf16_rne((g / (1.0f + expf(-g))) * u);
+    }
+}
+
+template <int MM>
+int gemv_swiglu_dispatch(cudaStream_t st, const uint16_t *a, int lda, const uint16_t *wg,
+                         const uint16_t *wu, int ldb, uint16_t *h, int ldh, int N, int K) {
+    N550_CUDA_TRY(launch_k(gemv_swiglu_kernel<MM>, (N + GV_WARPS - 1) / GV_WARPS, GV_WARPS * 32, 0, st,
+                           a, lda, wg, wu, ldb, h, ldh, N, K));
+    return N550_OK;
+}
+
 __global__ void f32_to_bf16_kernel(uint16_t *out, int ldo, const float *in, int ldi,
                                    int rows, int cols) {
     dep_wait();
@@ -190,6 +260,24 @@ int launch_gemv(cudaStream_t st, int epi, const uint16_t *a, int lda,
     case 6: return gemv_dispatch<6>(st, epi, a, lda, b, ldb, c, ldc, N, K);
     case 7: return gemv_dispatch<7>(st, epi, a, lda, b, ldb, c, ldc, N, K);
     default: return gemv_dispatch<8>(st, epi, a, lda, b, ldb, c, ldc, N, K);
+    }
+}
+
+int launch_gemv_swiglu(cudaStream_t st, const uint16_t *a, int lda, const uint16_t *wg,
+                       const uint16_t *wu, int ldb, uint16_t *h, int ldh, int M, int N, int K) {
+    if (M <= 0 || N <= 0) return N550_OK;
+    if (M > GV_MAXM || (K % 8) || (lda % 8) || (ldb % 8) || (((uintptr_t)a) & 15) ||
+        (((uintptr_t)wg) & 15) || (((uintptr_t)wu) & 15) || !h)
+        return N550_ERR_UNSUPPORTED;
+    switch (M) {
+    case 1: return gemv_swiglu_dispatch<1>(st, a, lda, wg, wu, ldb, h, ldh, N, K);
+    case 2: return gemv_swiglu_dispatch<2>(st, a, lda, wg, wu, ldb, h, ldh, N, K);
+    case 3: return gemv_swiglu_dispatch<3>(st, a, lda, wg, wu, ldb, h, ldh, N, K);
+    case 4: return gemv_swiglu_dispatch<4>(st, a, lda, wg, wu, ldb, h, ldh, N, K);
+    case 5: return gemv_swiglu_dispatch<5>(st, a, lda, wg, wu, ldb, h, ldh, N, K);
+    case 6: return gemv_swiglu_dispatch<6>(st, a, lda, wg, wu, ldb, h, ldh, N, K);
+    case 7: return gemv_swiglu_dispatch<7>(st, a, lda, wg, wu, ldb, h, ldh, N, K);
+    default: return gemv_swiglu_dispatch<8>(st, a, lda, wg, wu, ldb, h, ldh, N, K);
     }
 }
 

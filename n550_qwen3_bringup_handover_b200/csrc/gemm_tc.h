@@ -105,6 +105,9 @@ int launch_gemm_simt(cudaStream_t st, int epi, const uint16_t *a, int lda,
 // Skinny-M GEMV (M <= 8): streams B once with 16-byte loads.
 int launch_gemv(cudaStream_t st, int epi, const uint16_t *a, int lda,
                 const uint16_t *b, int ldb, void *c, int ldc, int M, int N, int K);
+// h[m][n] = bf16(silu(a[m] . wg[n]) * (a[m] . wu[n])) for M <= 8 rows, one launch.
+int launch_gemv_swiglu(cudaStream_t st, const uint16_t *a, int lda, const uint16_t *wg,
+                       const uint16_t *wu, int ldb, uint16_t *h, int ldh, int M, int N, int K);
 
 // FP32 -> BF16 RNE staging copy of a row-major [rows, cols] matrix.
 int launch_f32_to_bf16(cudaStream_t st, uint16_t *out, int ldo, const float *in, int ldi,

@@ -623,13 +623,8 @@ int mgemm(n550_model *m, cudaStream_t st, int epi, const uint16_t *a, int lda, c
     }
     if (M <= 8) {
         if (epi != TC_EPI_SILU_BF16) return launch_gemv(st, epi, a, lda, w, K, c, ldc, M, N, K);
-        int rc = launch_gemv(st, TC_EPI_F32, a, lda, w, K, m->tmp_a, N, M, N, K);
-        if (!rc) rc = launch_gemv(st, TC_EPI_F32, a, lda, w2, K, m->tmp_b, N, M, N, K);
-        if (rc) return rc;
-        N550_CUDA_TRY(launch_k(silu_mul_bf16_kernel, grid1((size_t)M * N), 256, 0, st, (uint16_t *)c,
-                               m->tmp_a, m->tmp_b, (size_t)M * N));
-        N550_LAUNCH_CHECK();
-        return N550_OK;
+        // gate, up and SiLU . mul in one GEMV launch
+        return launch_gemv_swiglu(st, a, lda, w, w2, K, (uint16_t *)c, ldc, M, N, K);
     }
     if (M < 1024)   // skinny (decode, short prompts): split the K loop over more SMs
         return launch_gemm_tc_splitk(st, epi, a, lda, w, K, w2, c, ldc, M, N, K, m->ws, m->ws_bytes);
@@ -798,7 +793,7 @@ int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t
         return run_layers_skinny(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, xl_ready);
     if (!exact && T > 8 && T < 1024)
         return run_layers_split(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, xl_ready);
-    const int gu_kernels = exact || T <= 8 ? 3 : 1;
+    const int gu_kernels = exact ? 3 : 1;
     const int res_kernels = exact ? 2 : 1;
     for (int l = 0; l < NLAYER; l++) {
         STEP(N550_PROF_RMSNORM, 1, launch_norm_rows(st, m->xb, m->x, W(m, l, 0), T));
