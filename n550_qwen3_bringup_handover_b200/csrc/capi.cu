@@ -422,6 +422,10 @@ int n550_gemm_swiglu(void *stream, const uint16_t *a, int lda, const uint16_t *w
         ldh < N)
         return N550_ERR_ARG;
     if (M == 0 || N == 0) return N550_OK;
+    // up to 8 rows: gate, up and SiLU . mul in one GEMV launch (as the other
+    // few-row GEMMs of this interface)
+    if (M <= 8 && launch_gemv_swiglu(st, a, lda, wg, wu, ldw, h, ldh, M, N, K) == N550_OK)
+        return N550_OK;
     if (!tc_shape_ok(a, lda, wg, ldw, K) || !tc_shape_ok(a, lda, wu, ldw, K))
         return N550_ERR_UNSUPPORTED;
     return skinny_or_full(st, TC_EPI_SILU_BF16, a, lda, wg, ldw, wu, h, ldh, M, N, K);

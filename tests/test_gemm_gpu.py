@@ -271,9 +271,11 @@ def test_tile_shapes(cuda, tile, M, K, N, out):
     assert n5.device_status() == n5.OK
 
 
-@pytest.mark.parametrize("M,K,N", [(300, 1024, 3072), (128, 1024, 200), (17, 1024, 64)])
+@pytest.mark.parametrize("M,K,N", [(300, 1024, 3072), (128, 1024, 200), (17, 1024, 64),
+                                   (1, 1024, 3072), (3, 1024, 3072), (8, 1024, 200)])
 def test_fused_swiglu_gemm(cuda, M, K, N):
-    """h = silu(A . Wg^T) * (A . Wu^T) in BF16 (gate/up qwen3_gemm then qwen3_op_silu_mul)."""
+    """h = silu(A . Wg^T) * (A . Wu^T) in BF16 (gate/up qwen3_gemm then qwen3_op_silu_mul);
+    up to 8 rows through the one-launch SwiGLU GEMV."""
     A = oracle.synth_normal_bf16((M, K), 41, 0x41, 1.0)
     G = oracle.synth_normal_bf16((N, K), 41, 0x47, 0.02)
     U = oracle.synth_normal_bf16((N, K), 41, 0x55, 0.02)
