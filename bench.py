@@ -142,6 +142,23 @@ def barrier(world):
         dist.barrier()
 
 
+def shard(n_total: int, world: int, rank: int):
+    """Rows [lo, hi) of n_total independent sequences that rank `rank` of
+    `world` processes (equal contiguous shards, rank order)."""
+    if n_total % world:
+        raise SystemExit("sequence counts must divide by the number of GPUs")
+    per = n_total // world
+    return rank * per, (rank + 1) * per
+
+
+def gather_rows(world: int, out, mine) -> None:
+    """Rank-ordered gather of every rank's rows `mine` into `out` (all ranks);
+    the only collective of the data-parallel path."""
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_gather_into_tensor(out, mine)
+
+
 # ----------------------------------------------------------------------------- n550 arm
 def run_n550(args, world, rank, local):
     import numpy as np
@@ -154,16 +171,16 @@ def run_n550(args, world, rank, local):
     dev = torch.device("cuda", local)
     dist = dist_init(world, local, "nccl")
 
-    if PREFILL_SEQS % world or DECODE_SEQS % world:
-        raise SystemExit("sequence counts must divide by the number of GPUs")
-    ps, ds = PREFILL_SEQS // world, DECODE_SEQS // world
+    p_lo, p_hi = shard(PREFILL_SEQS, world, rank)
+    d_lo, d_hi = shard(DECODE_SEQS, world, rank)
+    ps, ds = p_hi - p_lo, d_hi - d_lo
     max_len = DECODE_CTX + DECODE_STEPS
     max_tokens = ps * PREFILL_LEN
     m = n5.Model(seed=0, max_seqs=max(ps, ds), max_len=max_len, max_tokens=max_tokens)
 
     # seeded synthetic tokens of the whole job; this rank's shard of sequences
     all_prompts = n5.synth_tokens(PREFILL_SEQS * PREFILL_LEN, 0, TOKEN_STREAM).reshape(PREFILL_SEQS, PREFILL_LEN)
-    mine = np.ascontiguousarray(all_prompts[rank * ps:(rank + 1) * ps])
+    mine = np.ascontiguousarray(all_prompts[p_lo:p_hi])
     tok_host = torch.from_numpy(mine).pin_memory()
     tok_dev = tok_host.to(dev)
     seq_ids = torch.arange(ps, dtype=torch.int32, device=dev)
@@ -176,9 +193,8 @@ def run_n550(args, world, rank, local):
     stream = torch.cuda.current_stream(dev)
 
     def gather():
-        if world > 1:
-            dist.all_gather_into_tensor(gathered_logits, logits)
-            dist.all_gather_into_tensor(gathered_next, nxt)
+        gather_rows(world, gathered_logits, logits)
+        gather_rows(world, gathered_next, nxt)
 
     def step_device():
         m.prefill(tok_dev, seq_ids, 0, logits, nxt)
@@ -205,8 +221,8 @@ def run_n550(args, world, rank, local):
         m.prefill(tok_dev, seq_ids, 0, logits, nxt)
         stream.wait_event(ev_copied[b])              # buffer b's previous read-back is done
         if world > 1:
-            dist.all_gather_into_tensor(res_logits[b], logits)
-            dist.all_gather_into_tensor(res_next[b], nxt)
+            gather_rows(world, res_logits[b], logits)
+            gather_rows(world, res_next[b], nxt)
         else:
             res_logits[b].copy_(logits, non_blocking=True)
             res_next[b].copy_(nxt, non_blocking=True)
@@ -332,7 +348,8 @@ def run_decode(args, m, world, rank, dev, stream, ds, pk, timed):
     import ctypes as C
 
     ctx = n5.synth_tokens(DECODE_SEQS * DECODE_CTX, 1, TOKEN_STREAM).reshape(DECODE_SEQS, DECODE_CTX)
-    mine = torch.from_numpy(np.ascontiguousarray(ctx[rank * ds:(rank + 1) * ds])).to(dev)
+    d_lo, d_hi = shard(DECODE_SEQS, world, rank)
+    mine = torch.from_numpy(np.ascontiguousarray(ctx[d_lo:d_hi])).to(dev)
     seq = torch.arange(ds, dtype=torch.int32, device=dev)
     nxt = torch.empty(ds, dtype=torch.int32, device=dev)
     m.prefill(mine, seq, 0, None, nxt)                 # untimed: fills the KV cache
