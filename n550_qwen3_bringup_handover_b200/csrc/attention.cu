@@ -28,10 +28,6 @@ constexpr int NL = 28;
 constexpr float kScale = 0.08838834764831845f;     // qwen3.c:296
 constexpr float kLog2e = 1.4426950408889634f;
 
-__device__ __forceinline__ size_t kv_base(int seq, int layer, int kvh, int max_len) {
-    return ((size_t)(seq * NL + layer) * NKV + kvh) * (size_t)max_len * HD;
-}
-
 // ---------------------------------------------------------------------------
 // decode (split-KV; q.K^T and P.V on mma.sync tensor-core fragments)
 // ---------------------------------------------------------------------------
