@@ -69,3 +69,29 @@ def test_status_strings():
     for s in (n5.OK, n5.ERR_MAGIC, n5.ERR_LAYOUT, n5.ERR_ARG, n5.ERR_CUDA, n5.ERR_TIMEOUT):
         assert n5.strerror(s) and n5.strerror(s) != "unknown"
     assert n5.strerror(12345) == "unknown"
+
+
+def test_device_entry_points_reject_bad_arguments():
+    """Argument checks of the stream-ordered entry points run on the host
+    before any CUDA call (so this runs without a GPU): invalid shapes, strides,
+    layers and knob values give N550_ERR_ARG, empty problems N550_OK."""
+    L = n5.lib()
+    assert L.n550_gemm_tile_config(7) == n5.ERR_ARG
+    assert L.n550_gemm_tile_config(0) == n5.OK
+    assert L.n550_gemm_skinny_config(17) == n5.ERR_ARG
+    assert L.n550_gemm_skinny_config(-2) == n5.ERR_ARG
+    assert L.n550_gemm_skinny_config(0) == n5.OK
+    # n550_gemm_residual(stream, a, lda, b, ldb, x, ldx, M, N, K)
+    assert L.n550_gemm_residual(None, None, 8, None, 8, None, 8, -1, 8, 8) == n5.ERR_ARG
+    assert L.n550_gemm_residual(None, None, 4, None, 8, None, 8, 0, 8, 8) == n5.ERR_ARG   # lda < K
+    assert L.n550_gemm_residual(None, None, 8, None, 8, None, 8, 0, 8, 8) == n5.OK        # M = 0
+    # n550_gemm_swiglu(stream, a, lda, wg, wu, ldw, h, ldh, M, N, K)
+    assert L.n550_gemm_swiglu(None, None, 8, None, None, 8, None, 8, -1, 8, 8) == n5.ERR_ARG
+    assert L.n550_gemm_swiglu(None, None, 8, None, None, 8, None, 4, 2, 8, 8) == n5.ERR_ARG  # ldh < N
+    # attention: no KV slots, a layer past the 28th, null buffers
+    assert L.n550_attention_prefill(None, None, 2048, None, None, 0, 64, 0, None, 1, 8, 0, None,
+                                    2048) == n5.ERR_ARG
+    assert L.n550_attention_decode(None, None, 2048, None, None, 1, 64, 28, None, None, 1, None,
+                                   2048, None, 0) == n5.ERR_ARG
+    assert L.n550_attention_decode(None, None, 2048, None, None, 1, 64, 0, None, None, 0, None,
+                                   2048, None, 0) == n5.OK                                 # no sequences
