@@ -83,7 +83,7 @@ __host__ __device__ __forceinline__ uint16_t f32_to_bf16_rne(float f) {
     return (uint16_t)(u >> 16);
 }
 
-// sin and cos of a RoPE angle x = pos * inv_freq (x >= 0): Cody-Waite
+// sin and cos of a RoPE angle x = pos * inv_freq (ops_scalar.c:21-35; x >= 0): Cody-Waite
 // reduction x = k * pi/2 + r with pi/2 split into P1 (13 significant bits, so
 // k * P1 is exact for k < 2^11) and P2 = fl32(pi/2 - P1), then the hardware
 // sine/cosine approximations on |r| <= pi/4 (absolute error ~2^-21) and the
