@@ -128,15 +128,21 @@ int n550_gemm(void *stream, int mode, int kblock,
 /* Fast-mode C = bf16_rne(A) . B^T for callers that cannot allocate device
  * memory: runtimes that keep the reference's no-malloc discipline (a fixed
  * arena sized up front, qwen3.h:39-58) and hosts that must not let a call
- * synchronise the device, as cudaMalloc/cudaFree do. It is the FP32-activation
- * path of n550_gemm(MODE_FAST, a_type = N550_F32), with the BF16 staging copy
+ * synchronise the device, as cudaMalloc/cudaFree do. It computes what
+ * n550_gemm(MODE_FAST, a_type = N550_F32) computes, with the BF16 staging copy
  * of A held in a fixed 8 MiB array that this library places in every GPU
  * that loads it (for as long as the process lives) instead of a per-call
- * allocation. No counterpart in the reference.
+ * allocation. Routing: up to 8 rows the GEMV, then the weight-streaming GEMM
+ * (FP32 output, up to n550_gemm_skinny_rows rows), otherwise the tile GEMM in
+ * one pass -- n550_gemm's split-K route for 33-1023 rows is not taken (its
+ * partial sums would need a second array), so those shapes run slower here
+ * than through n550_gemm. No counterpart in the reference.
  *   Limit: M * round_up(K, 8) <= 4,194,304 (e.g. 4096 x 1024, 1365 x 3072);
  *   larger calls return N550_ERR_ARG and touch nothing.
  *   The first call on each device looks up the array's device address; make
- *   that first call before capturing the stream into a CUDA graph.
+ *   that first call before capturing the stream into a CUDA graph. The address
+ *   is kept for the life of the process: after cudaDeviceReset (or a release
+ *   of the device's primary context) this entry point must not be called.
  *   All calls share the one array: calls that can overlap on the GPU (other
  *   streams, other threads) race on it and must be serialised by the caller.
  *   c_type is N550_F32 or N550_BF16; other arguments as in n550_gemm. */
@@ -183,6 +189,31 @@ int n550_gemm_residual(void *stream, const uint16_t *a, int lda, const uint16_t 
                        float *x, int ldx, int M, int N, int K);
 int n550_gemm_swiglu(void *stream, const uint16_t *a, int lda, const uint16_t *wg,
                      const uint16_t *wu, int ldw, uint16_t *h, int ldh, int M, int N, int K);
+
+/* RoPE factor table of the fused q/k/v step: table[pos][i] = (cos, sin) of
+ * pos * inv_freq[i] as FP32 pairs, pos < max_len, i < 64, inv_freq[i] =
+ * 1 / powf(1e6, 2i / 128) as ops_scalar.c:24 computes it; table holds
+ * max_len * 128 floats (8-byte aligned). */
+int n550_rope_table(void *stream, float *table, int max_len);
+
+/* One decoder layer's q/k/v step (qwen3.c:477-511): qkv = x . Wqkv^T with
+ * Wqkv = [Wq; Wk; Wv] BF16 [4096, 1024] and x BF16 [M, ldx >= 1024]; then per
+ * head the RMSNorm over 128 with q_norm / k_norm (qk_norm, qwen3.c:287-292),
+ * RoPE of q and k at tok_pos[r] (ops_scalar.c:21-35, factors from
+ * n550_rope_table), the 16 query heads to q_out (q_type F32 or BF16, [M, ldq
+ * >= 2048]) and the 8 K and 8 V heads, rounded to BF16, to the caches at
+ * [tok_seq[r]][layer][kv_head][tok_pos[r]][128] (planes of max_len
+ * positions, 28 layers per sequence slot). Rows must name distinct (seq,
+ * pos). Route as the runtime's: the tile GEMM with this epilogue from 1024
+ * rows (BF16 q_out), the weight-streaming GEMM with it where
+ * n550_gemm_skinny_rows admits M (4 rows on), else FP32 q/k/v rows (GEMV up
+ * to 8 rows, split-K partials beyond, in a stream-ordered workspace) finished
+ * by one row kernel. */
+int n550_qkv_rope_kv(void *stream, const uint16_t *x, int ldx, const uint16_t *wqkv,
+                     const uint16_t *q_norm, const uint16_t *k_norm, const float *rope_table,
+                     const int32_t *tok_seq, const int32_t *tok_pos, int M,
+                     void *q_out, int q_type, int ldq, uint16_t *k_cache, uint16_t *v_cache,
+                     int max_len, int layer);
 
 /* Row-wise RMSNorm: out[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * w
  * (ops_scalar.c:11-15). out_type F32 or BF16. */
@@ -300,6 +331,12 @@ int n550_qwen3_forward_batch_host(n550_model_t *m, const int32_t *tokens,
  * n550_qwen3_init_random. No counterpart in the reference (its prompts come
  * from the tokenizer, which needs the unshipped tokenizer.bin). */
 int n550_synth_tokens(int32_t *out, size_t n, uint64_t seed, uint64_t stream, int vocab);
+
+/* Seeded synthetic BF16 values (the benchmark's GEMM operands), host memory:
+ * out[i] = bf16_rne(normal(sigma)) of u64(seed, stream, i), the generator
+ * n550_qwen3_init_random fills the weights with. No counterpart in the
+ * reference. */
+int n550_synth_normal_bf16(uint16_t *out, size_t n, uint64_t seed, uint64_t stream, double sigma);
 
 /* Device buffers of one weight tensor, for tests: which = 0 embed,
  * 1 + 11*l + j for layer l tensor j in QW3M order, 309 final norm.

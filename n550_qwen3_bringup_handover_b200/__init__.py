@@ -83,6 +83,8 @@ def lib() -> C.CDLL:
         "n550_attention_prefill": (i, [vp, vp, i, vp, vp, i, i, i, vp, i, i, i, vp, i]),
         "n550_attention_decode": (i, [vp, vp, i, vp, vp, i, i, i, vp, vp, i, vp, i, vp, sz]),
         "n550_attention_decode_workspace": (sz, [i, i]),
+        "n550_rope_table": (i, [vp, vp, i]),
+        "n550_qkv_rope_kv": (i, [vp, vp, i, vp, vp, vp, vp, vp, vp, i, vp, i, i, vp, vp, i, i]),
     }
     optional = {
         "n550_qwen3_init": (i, [C.POINTER(vp), vp, sz, C.POINTER(ModelConfig)]),
@@ -96,6 +98,7 @@ def lib() -> C.CDLL:
         "n550_qwen3_profile": (i, [vp, i]),
         "n550_qwen3_profile_read": (i, [vp, vp, vp, i]),
         "n550_synth_tokens": (i, [vp, sz, C.c_uint64, C.c_uint64, i]),
+        "n550_synth_normal_bf16": (i, [vp, sz, C.c_uint64, C.c_uint64, C.c_double]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -127,6 +130,15 @@ def synth_tokens(n: int, seed: int, stream: int, vocab: int = 151936):
     out = np.empty(n, np.int32)
     check(lib().n550_synth_tokens(out.ctypes.data_as(C.c_void_p), n, seed, stream, vocab),
           "n550_synth_tokens")
+    return out
+
+
+def synth_normal_bf16(shape, seed: int, stream: int, sigma: float):
+    """Seeded synthetic BF16 bits (numpy uint16), the library's generator."""
+    import numpy as np
+    out = np.empty(shape, np.uint16)
+    check(lib().n550_synth_normal_bf16(out.ctypes.data_as(C.c_void_p), out.size, seed, stream, sigma),
+          "n550_synth_normal_bf16")
     return out
 
 

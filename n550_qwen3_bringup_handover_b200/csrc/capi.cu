@@ -483,15 +483,29 @@ int n550_gemm_f32a_noalloc(void *stream, const float *a, int lda, const uint16_t
     if (rc) return rc;
     const int epi = c_type == N550_F32 ? TC_EPI_F32 : TC_EPI_BF16;
     if (M <= 8 && launch_gemv(st, epi, stage, ldab, b, ldb, c, ldc, M, N, K) == N550_OK) return N550_OK;
-    if (tc_shape_ok(stage, ldab, b, ldb, K))
-        return launch_gemm_tc(st, epi, n550_tile_bn(M, N), stage, ldab, b, ldb, nullptr, c, ldc, M, N, K, 0);
-    return launch_gemm_simt(st, epi, stage, ldab, b, ldb, c, ldc, M, N, K);
+    if (!tc_shape_ok(stage, ldab, b, ldb, K))
+        return launch_gemm_simt(st, epi, stage, ldab, b, ldb, c, ldc, M, N, K);
+    // the weight-streaming GEMM keeps its partial tiles on chip, as in n550_gemm
+    if (skinny_route(M) && epi == TC_EPI_F32) {
+        rc = skinny_f32(st, stage, ldab, b, ldb, (float *)c, ldc, M, N, K);
+        if (rc != N550_ERR_UNSUPPORTED) return rc;
+    }
+    // no split-K here: its FP32 partials would need a second, larger array
+    return launch_gemm_tc(st, epi, n550_tile_bn(M, N), stage, ldab, b, ldb, nullptr, c, ldc, M, N, K, 0);
 }
 
 int n550_synth_tokens(int32_t *out, size_t n, uint64_t seed, uint64_t stream, int vocab) {
     if ((n && !out) || vocab <= 0) return N550_ERR_ARG;
     const uint64_t key = synth_key(seed, stream);
     for (size_t i = 0; i < n; i++) out[i] = (int32_t)(synth_u64(key, i) % (uint64_t)vocab);
+    return N550_OK;
+}
+
+int n550_synth_normal_bf16(uint16_t *out, size_t n, uint64_t seed, uint64_t stream, double sigma) {
+    if (n && !out) return N550_ERR_ARG;
+    const uint64_t key = synth_key(seed, stream);
+    const float scale = synth_normal_scale(sigma);
+    for (size_t i = 0; i < n; i++) out[i] = f32_to_bf16_rne(synth_normal(synth_u64(key, i), scale));
     return N550_OK;
 }
 

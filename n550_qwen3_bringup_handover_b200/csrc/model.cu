@@ -1167,4 +1167,78 @@ const uint16_t *n550_qwen3_weight(const n550_model_t *m, int which, size_t *elem
     return m->t[which];
 }
 
+int n550_rope_table(void *stream, float *table, int max_len) {
+    if (max_len < 0 || (max_len && !table) || ((uintptr_t)table & 7)) return N550_ERR_ARG;
+    if (max_len == 0) return N550_OK;
+    int rc = ensure_rope_table();
+    if (rc) return rc;
+    rope_table_kernel<<<(max_len * 64 + 255) / 256, 256, 0, (cudaStream_t)stream>>>((float2 *)table,
+                                                                                    max_len);
+    N550_LAUNCH_CHECK();
+    return N550_OK;
+}
+
+// The decoder layer's q/k/v step on the route the runtime takes for M rows
+// (run_layers): tile GEMM with the fused epilogue from 1024 rows (BF16
+// queries), the weight-streaming GEMM with the fused epilogue where
+// skinny_route(M), else FP32 q/k/v rows (GEMV up to 8 rows, split-K partials
+// otherwise, in a stream-ordered workspace) finished by qknorm_rope_kv_kernel.
+int n550_qkv_rope_kv(void *stream, const uint16_t *x, int ldx, const uint16_t *wqkv,
+                     const uint16_t *q_norm, const uint16_t *k_norm, const float *rope_table,
+                     const int32_t *tok_seq, const int32_t *tok_pos, int M, void *q_out,
+                     int q_type, int ldq, uint16_t *k_cache, uint16_t *v_cache, int max_len,
+                     int layer) {
+    cudaStream_t st = (cudaStream_t)stream;
+    if (M < 0 || max_len <= 0 || layer < 0 || layer >= NLAYER) return N550_ERR_ARG;
+    if (M == 0) return N550_OK;
+    if (!x || !wqkv || !q_norm || !k_norm || !rope_table || !tok_seq || !tok_pos || !q_out ||
+        !k_cache || !v_cache || ldx < H || ldq < QD || (q_type != N550_F32 && q_type != N550_BF16))
+        return N550_ERR_ARG;
+    int rc = ensure_rope_table();
+    if (rc) return rc;
+    const float2 *rope = (const float2 *)rope_table;
+    uint16_t *qb = q_type == N550_BF16 ? (uint16_t *)q_out : nullptr;
+    float *qf = q_type == N550_F32 ? (float *)q_out : nullptr;
+    if (M >= 1024 && qb && tc_shape_ok(x, ldx, wqkv, H, H)) {
+        TcQkv q{};
+        q.q_bf16 = qb; q.ldq = ldq;
+        q.kc = k_cache; q.vc = v_cache; q.layer = layer; q.max_len = max_len;
+        q.tok_pos = tok_pos; q.tok_seq = tok_seq;
+        q.q_norm = q_norm; q.k_norm = k_norm; q.rope = rope; q.eps = EPS;
+        return launch_gemm_tc_qkv(st, x, ldx, wqkv, q, M, H, 0);
+    }
+    if (M >= 4 && skinny_route(M) && tc_shape_ok(x, ldx, wqkv, H, H)) {
+        SkEpilogue q{};
+        q.q_f32 = qf; q.q_bf16 = qb; q.ldq = ldq;
+        q.kc = k_cache; q.vc = v_cache; q.layer = layer; q.max_len = max_len;
+        q.tok_pos = tok_pos; q.tok_seq = tok_seq;
+        q.q_norm = q_norm; q.k_norm = k_norm; q.rope = rope;
+        rc = launch_gemm_skinny(st, SK_EPI_QKV, x, ldx, wqkv, nullptr, H, M, QKVD, H, q);
+        if (rc != N550_ERR_UNSUPPORTED) return rc;
+    }
+    int ks = 0, kt;
+    const bool split = M > 8 && tc_shape_ok(x, ldx, wqkv, H, H);
+    const size_t bytes = (size_t)(split ? 8 : 1) * M * QKVD * 4;
+    float *ws = nullptr;
+    if (cudaMallocAsync((void **)&ws, bytes, st) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return N550_ERR_OOM;
+    }
+    if (split && tc_splitk_plan(M, QKVD, H, TC_EPI_F32, 64, &kt) > 0)
+        rc = launch_gemm_tc_partials(st, TC_EPI_F32, x, ldx, wqkv, H, nullptr, M, QKVD, H, ws, bytes, &ks);
+    else if (M <= 8)
+        rc = launch_gemv(st, TC_EPI_F32, x, ldx, wqkv, H, ws, QKVD, M, QKVD, H);
+    else
+        rc = launch_gemm_simt(st, TC_EPI_F32, x, ldx, wqkv, H, ws, QKVD, M, QKVD, H);
+    if (!rc) {
+        if (launch_k(qknorm_rope_kv_kernel, M, 1024, 0, st, (const float *)ws, QKVD, ks,
+                     (size_t)M * QKVD, q_norm, k_norm, rope, tok_pos, tok_seq, layer, k_cache, v_cache,
+                     max_len, qb, qf, ldq) != cudaSuccess)
+            rc = N550_ERR_CUDA;
+        (void)cudaGetLastError();
+    }
+    cudaFreeAsync(ws, st);
+    return rc;
+}
+
 }  // extern "C"

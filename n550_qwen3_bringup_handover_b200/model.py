@@ -96,25 +96,3 @@ class _DeviceArray:
     def __init__(self, ptr: int, n: int):
         self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<i2", "data": (ptr, False),
                                          "version": 3, "strides": None}
-
-
-def smoke_forward(device) -> None:
-    """One prefill + one decode step of the random-init model, compared with
-    the oracle's restatement of qwen3_forward_batch on the same weights."""
-    import oracle
-    m = Model(seed=0, max_seqs=1, max_len=64, max_tokens=64)
-    toks = oracle.synth_tokens(8, 0, 0x544F4B)
-    nxt, lg = m.forward_batch(toks, 0)
-    blob = oracle.qw3m_blob(seed=0, sigma=0.02)
-    ref = oracle.OracleModel(blob, max_seq=64, gemm_kind=oracle.GEMM_HWSIM)
-    rl = ref.forward_batch(toks, 0)
-    err = float(np.abs(lg - rl).max() / np.abs(rl).max())
-    if not err <= 1e-2:
-        raise AssertionError(f"prefill logits rel err {err:.3e} > 1e-2")
-    nxt2, lg2 = m.forward_batch(np.array([nxt], np.int32), 8)
-    rl2 = ref.forward_batch(np.array([nxt], np.int32), 8)
-    err2 = float(np.abs(lg2 - rl2).max() / np.abs(rl2).max())
-    if not err2 <= 1e-2:
-        raise AssertionError(f"decode logits rel err {err2:.3e} > 1e-2")
-    m.close()
-    ref.close()

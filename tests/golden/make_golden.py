@@ -2,6 +2,7 @@
 reference checkout; the fixtures themselves travel, the reference does not).
 
     python tests/golden/make_golden.py --reference <path of the reference checkout>
+    python tests/golden/make_golden.py --greedy | --batched   (need only oracle/_ref)
 
 Writes
   tests/golden/ame_cases.npz   the 12 shipped AME cases of
@@ -15,6 +16,11 @@ Writes
       this project's seeded generator) evaluated by the reference's own
       generator function ame_gemm_ref (40_gen_ame_vectors.py:121-143), imported
       from the reference checkout with K_BLOCK set to 16 and to 32.
+  tests/golden/batched_ref.npz   rows of the two benched batches (bench.py's
+      configs[3] prefill and configs[4] decode inputs) run by the reference's
+      own qwen3.c + kernels_scalar.c (oracle/_ref) in 128-token calls: top-64
+      logits, the logits at every 37th id and max|logit| of each output row,
+      and the greedy ids.
 """
 from __future__ import annotations
 
@@ -23,6 +29,7 @@ import hashlib
 import importlib.util
 import json
 import multiprocessing as mp
+import os
 import struct
 import sys
 from pathlib import Path
@@ -143,18 +150,86 @@ def greedy_reference():
     return res
 
 
+# Benched batches (bench.py): configs[3] prefill = synth_tokens(64 * 512, 0,
+# TOKEN_STREAM) as 64 rows of 512; configs[4] decode context =
+# synth_tokens(256 * 1024, 1, TOKEN_STREAM) as 256 rows of 1024. The fixtures
+# hold the reference's logits for the first and the last row of each batch.
+TOKEN_STREAM = 0x544F4B
+CHUNK = 128                       # QWEN3_MAX_BATCH: tokens per qwen3_forward_batch call
+SAMPLE_STRIDE = 37                # logits kept at ids 0, 37, 74, ... (4107 of 151936)
+TOP = 64
+
+
+def _logit_summary(logits):
+    """Top-64 ids/values, the values at every 37th id and max|logit| of one row."""
+    order = np.argsort(-logits, kind="stable")[:TOP]
+    return (order.astype(np.int32), logits[order].astype(np.float32),
+            logits[::SAMPLE_STRIDE].astype(np.float32), np.float32(np.abs(logits).max()))
+
+
+def _batched_worker(job):
+    """One spawned process: the reference's own qwen3.c + kernels_scalar.c +
+    ops_scalar.c (oracle/_ref) on one row of a benched batch, prefilled in
+    128-token qwen3_forward_batch calls (the reference caps a call at
+    QWEN3_MAX_BATCH = 128, qwen3.c:461), then `steps` greedy single-token calls."""
+    kind, row, seqs, length, seed, steps = job
+    import oracle
+    blob = oracle.qw3m_blob(seed=0, sigma=0.02)
+    m = oracle.RefModel(blob, "scalar")
+    toks = oracle.synth_tokens(seqs * length, seed, TOKEN_STREAM)[row * length:(row + 1) * length]
+    for p0 in range(0, length, CHUNK):
+        logits = m.forward_batch(toks[p0:p0 + CHUNK], p0)
+    out = [_logit_summary(logits)]
+    chosen = [oracle.argmax(logits)]
+    pos = length
+    for _ in range(steps):
+        logits = m.forward_batch(np.array([chosen[-1]], np.int32), pos)
+        pos += 1
+        out.append(_logit_summary(logits))
+        chosen.append(oracle.argmax(logits))
+    print(kind, row, "done", chosen, flush=True)
+    return kind, row, out, chosen
+
+
+def batched_reference():
+    """configs[3] rows 0 and 63 (512-token prefill: last-token logits) and
+    configs[4] rows 0 and 255 (1024-token context: the prefill's last-token
+    logits, then 8 greedy steps at positions 1024-1031, 9 logit rows each)."""
+    jobs = [("c4", 0, 64, 512, 0, 0), ("c4", 63, 64, 512, 0, 0),
+            ("c5", 0, 256, 1024, 1, 8), ("c5", 255, 256, 1024, 1, 8)]
+    with mp.get_context("spawn").Pool(len(jobs)) as pool:
+        res = pool.map(_batched_worker, jobs)
+    out = {"sample_stride": np.int32(SAMPLE_STRIDE), "chunk": np.int32(CHUNK)}
+    for kind, rows in (("c4", (0, 63)), ("c5", (0, 255))):
+        got = {r[1]: r for r in res if r[0] == kind}
+        out[f"{kind}_rows"] = np.array(rows, np.int32)
+        for name, i in (("top_ids", 0), ("top_vals", 1), ("sampled", 2), ("absmax", 3)):
+            out[f"{kind}_{name}"] = np.stack([np.stack([s[i] for s in got[r][2]]) for r in rows])
+        out[f"{kind}_tokens"] = np.array([got[r][3] for r in rows], np.int32)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("N550_REFERENCE"),
+                    help="reference checkout (default: $N550_REFERENCE)")
     ap.add_argument("--skip-config1", action="store_true")
     ap.add_argument("--greedy", action="store_true", help="only the greedy-decode fixture")
+    ap.add_argument("--batched", action="store_true",
+                    help="only the benched-batch fixture (batched_ref.npz)")
     args = ap.parse_args()
-    ref = Path(args.reference)
     here = Path(__file__).resolve().parent
     if args.greedy:
         np.savez_compressed(here / "greedy_ref.npz", **greedy_reference())
         print("wrote greedy_ref.npz")
         return
+    if args.batched:
+        np.savez_compressed(here / "batched_ref.npz", **batched_reference())
+        print("wrote batched_ref.npz")
+        return
+    if not args.reference:
+        ap.error("--reference (or N550_REFERENCE) is required for the AME cases")
+    ref = Path(args.reference)
     cases = load_cases(ref)
     np.savez_compressed(here / "ame_cases.npz", **cases)
     print("wrote ame_cases.npz:", list(cases["case_ids"]))

@@ -95,3 +95,24 @@ def test_device_entry_points_reject_bad_arguments():
                                    2048, None, 0) == n5.ERR_ARG
     assert L.n550_attention_decode(None, None, 2048, None, None, 1, 64, 0, None, None, 0, None,
                                    2048, None, 0) == n5.OK                                 # no sequences
+    # n550_qkv_rope_kv(stream, x, ldx, wqkv, qn, kn, rope, seq, pos, M, q, q_type, ldq, kc, vc,
+    #                  max_len, layer): a layer past the 28th, ldq below 2048, no rows
+    assert L.n550_qkv_rope_kv(None, None, 1024, None, None, None, None, None, None, 4, None, n5.F32,
+                              2048, None, None, 64, 28) == n5.ERR_ARG
+    assert L.n550_qkv_rope_kv(None, None, 1024, None, None, None, None, None, None, 4, None, n5.F32,
+                              1024, None, None, 64, 0) == n5.ERR_ARG
+    assert L.n550_qkv_rope_kv(None, None, 1024, None, None, None, None, None, None, 0, None, n5.F32,
+                              2048, None, None, 64, 0) == n5.OK
+    assert L.n550_rope_table(None, None, -1) == n5.ERR_ARG
+    assert L.n550_rope_table(None, None, 0) == n5.OK
+
+
+def test_synth_normal_matches_oracle_generator():
+    """The library's seeded BF16 generator (bench.py's GEMM operands) is
+    bit-identical to the oracle's, which made the config-1 golden fixture."""
+    import numpy as np
+    import oracle
+    for shape, seed, stream, sigma in [((16, 1024), 0, 0x41, 1.0), ((2048, 1024), 0, 0x42, 0.02),
+                                       ((3, 5), 7, 9, 0.5)]:
+        assert np.array_equal(n5.synth_normal_bf16(shape, seed, stream, sigma),
+                              oracle.synth_normal_bf16(shape, seed, stream, sigma))

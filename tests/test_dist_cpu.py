@@ -1,8 +1,9 @@
-"""bench.py's multi-rank host logic on CPU: two processes over the gloo backend
-(the GPU runs use NCCL with the same calls). Covers the data-parallel path's
-sequence sharding, the rank-ordered gather of outputs (its only collective),
-the max over ranks of the step time, the barrier, and the reference arm's
-rule that rank 0 alone runs and prints.
+"""The data-parallel layer's host logic (n550_qwen3_bringup_handover_b200/dp.py)
+on CPU: two processes over the gloo backend (the GPU runs use NCCL with the
+same calls). Covers the sequence sharding, the rank-ordered gathers of outputs
+(the path's only collectives: last-token rows and per-step ids), the max over
+ranks of the step time, the barrier, and bench.py's reference-arm rule that
+rank 0 alone runs and prints.
 """
 import json
 import os
@@ -29,24 +30,31 @@ def rank_main(rank: int, world: int, port: int, q) -> None:
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
     sys.path.insert(0, str(ROOT))
-    import bench
-    w, r, _ = bench.dist_setup(world)
-    dist = bench.dist_init(w, r, "gloo")
+    from n550_qwen3_bringup_handover_b200 import dp
+    import torch.distributed as dist
+    w, r, _ = dp.init_process_group("gloo")
     try:
+        assert dp.world_and_rank() == (w, r)
         total, width = 64, 7
         rows = np.arange(total * width, dtype=np.int32).reshape(total, width)
-        lo, hi = bench.shard(total, w, r)
+        lo, hi = dp.shard(total, w, r)
         # stand-ins for the per-rank next tokens and logits
         mine_i = torch.from_numpy(rows[lo:hi] * 3 + 1)
         mine_f = torch.from_numpy(rows[lo:hi].astype(np.float32) * 0.5)
         out_i = torch.empty((total, width), dtype=torch.int32)
         out_f = torch.empty((total, width), dtype=torch.float32)
-        bench.gather_rows(w, out_i, mine_i)
-        bench.gather_rows(w, out_f, mine_f)
+        dp.gather_rows(out_i, mine_i)
+        dp.gather_rows(out_f, mine_f)
         gathered = bool(torch.equal(out_i, torch.from_numpy(rows * 3 + 1)) and
                         torch.equal(out_f, torch.from_numpy(rows.astype(np.float32) * 0.5)))
-        slowest = bench.max_over_ranks(10.0 + 2.5 * r, w, torch.device("cpu"))
-        bench.barrier(w)
+        # per-step ids of each rank's sequences: [steps, local] -> [steps, total]
+        steps = 5
+        ids = np.arange(steps * total, dtype=np.int32).reshape(steps, total) * 7
+        out_ids = torch.empty((steps, total), dtype=torch.int32)
+        dp.gather_columns(out_ids, torch.from_numpy(np.ascontiguousarray(ids[:, lo:hi])))
+        gathered = gathered and bool(torch.equal(out_ids, torch.from_numpy(ids)))
+        slowest = dp.max_over_ranks(10.0 + 2.5 * r, torch.device("cpu"))
+        dp.barrier()
         q.put(json.dumps({"rank": r, "lo": lo, "hi": hi, "gathered": gathered, "max": slowest}))
     finally:
         dist.destroy_process_group()
@@ -74,10 +82,28 @@ def test_two_ranks_shard_gather_and_time():
 
 def test_shard_rejects_uneven_split():
     sys.path.insert(0, str(ROOT))
-    import bench
-    assert bench.shard(256, 8, 7) == (224, 256)
-    with pytest.raises(SystemExit):
-        bench.shard(64, 3, 0)
+    from n550_qwen3_bringup_handover_b200 import dp
+    assert dp.shard(256, 8, 7) == (224, 256)
+    with pytest.raises(ValueError):
+        dp.shard(64, 3, 0)
+    with pytest.raises(ValueError):
+        dp.shard(64, 2, 2)
+
+
+def test_single_process_helpers_are_copies():
+    """Without a process group the gathers are plain copies and the max is the value."""
+    sys.path.insert(0, str(ROOT))
+    from n550_qwen3_bringup_handover_b200 import dp
+    assert dp.world_and_rank() == (1, 0)
+    a = torch.arange(12, dtype=torch.int32).reshape(3, 4)
+    out = torch.empty_like(a)
+    dp.gather_rows(out, a)
+    assert torch.equal(out, a)
+    out2 = torch.empty_like(a)
+    dp.gather_columns(out2, a)
+    assert torch.equal(out2, a)
+    assert dp.max_over_ranks(3.5, torch.device("cpu")) == 3.5
+    dp.barrier()
 
 
 def test_reference_arm_prints_on_rank_zero_only():

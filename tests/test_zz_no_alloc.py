@@ -5,9 +5,10 @@ the device). Its BF16 staging copy lives in a fixed array inside the library
 instead of a per-call allocation.
 
 Checked through the C ABI against the allocating entry point
-n550_gemm(MODE_FAST, a_type = F32) on two calls in a row (different shapes,
-so a stale array would show), within the fast-mode GEMM tolerance of the
-other GEMM tests; and an over-limit call is refused without writing C.
+n550_gemm(MODE_FAST, a_type = F32) and against a binary64 product on several
+calls in a row (different shapes, so a stale array would show), within the
+fast-mode GEMM tolerance of the other GEMM tests; and an over-limit call is
+refused without writing C.
 This file is collected last so that a failure here leaves every other test
 already run; it also passes alone in a fresh process.
 """
@@ -48,28 +49,48 @@ def rel_err(got, ref):
     return float(np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30))
 
 
+def f64_reference(a, b_bits):
+    """Binary64 product of the BF16-rounded activations and the BF16 weights."""
+    import oracle
+    a16 = oracle.bf16_to_f32(oracle.f32_to_bf16(a.cpu().numpy())).astype(np.float64)
+    return a16 @ oracle.bf16_to_f32(b_bits).astype(np.float64).T
+
+
 def test_noalloc_matches_allocating_entry_point_twice(cuda):
+    """Each route of the entry point on consecutive calls, smaller K after
+    larger K so that stale staging contents would show: GEMV (5 rows), the
+    CUDA-core kernel for a K that leaves the rows unaligned (17 x 1001, staged
+    rows padded to 1008), the tile GEMM, the weight-streaming GEMM (9 rows),
+    and the tile GEMM again. Each result is held to the fast-mode tolerance
+    against binary64 and against n550_gemm."""
     import torch
     rng = np.random.default_rng(77)
     import oracle
-    cases = [(300, 1024, 768), (5, 3072, 1024), (1024, 2048, 256)]   # TC, GEMV, TC paths
+    cases = [(5, 3072, 1024), (17, 1001, 256), (1024, 2048, 256), (9, 3072, 1024), (300, 1024, 768)]
     for M, K, N in cases:
         a = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(cuda)
-        b = to_dev_bf16(oracle.synth_normal_bf16((N, K), M, 0x42, 0.02), cuda)
+        b_bits = oracle.synth_normal_bf16((N, K), M, 0x42, 0.02)
+        b = to_dev_bf16(b_bits, cuda)
         want = n5.gemm(a, b, mode=n5.MODE_FAST)                    # allocating path
         got = torch.full((M, N), float("nan"), dtype=torch.float32, device=cuda)
         assert run_noalloc(a, b, got) == n5.OK
         torch.cuda.synchronize()
         assert n5.device_status() == n5.OK
-        assert rel_err(got, want) <= FAST_TOL
+        assert rel_err(got, want) <= FAST_TOL, (M, K, N)
+        ref = f64_reference(a, b_bits)
+        g = got.double().cpu().numpy()
+        assert float(np.abs(g - ref).max() / np.abs(ref).max()) <= FAST_TOL, (M, K, N)
     # BF16 output through the same array
     M, K, N = 64, 1024, 512
     a = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(cuda)
-    b = to_dev_bf16(oracle.synth_normal_bf16((N, K), 9, 0x42, 0.02), cuda)
+    b_bits = oracle.synth_normal_bf16((N, K), 9, 0x42, 0.02)
+    b = to_dev_bf16(b_bits, cuda)
     want = n5.gemm(a, b, mode=n5.MODE_FAST, out_dtype=torch.bfloat16)
     got = torch.empty((M, N), dtype=torch.bfloat16, device=cuda)
     assert run_noalloc(a, b, got) == n5.OK
     assert rel_err(got.float(), want.float()) <= 2.0 ** -7
+    ref = f64_reference(a, b_bits)
+    assert float(np.abs(got.double().cpu().numpy() - ref).max() / np.abs(ref).max()) <= 2.0 ** -7
 
 
 def test_noalloc_refuses_sizes_beyond_the_array(cuda):
