@@ -76,28 +76,38 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4 q, float (&f)[8]) {
     f[6] = __uint_as_float(q.w << 16); f[7] = __uint_as_float(q.w & 0xFFFF0000u);
 }
 
+// 16-byte loads of one lane's step of a weight row: 4 independent loads of 8
+// BF16 at k0, k0 + 256, k0 + 512, k0 + 768 (zeros past K).
+__device__ __forceinline__ void gv_load_step(uint4 (&q)[4], const uint16_t *row, int k0, int K) {
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        const int k = k0 + u * 256;
+        q[u] = (k < K) ? __ldcs((const uint4 *)(row + k)) : make_uint4(0, 0, 0, 0);
+    }
+}
+
 // One warp per output column n; requires K % 8 == 0 and 16-byte aligned rows.
+// The weights do not depend on the previous kernel, so the first step's loads
+// (the whole row for K <= 1024) are issued before the programmatic-launch
+// wait and overlap that kernel's tail; the activations are read after it.
 template <int MM, int EPI>
 __global__ void __launch_bounds__(GV_WARPS * 32)
 gemv_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict__ b, int ldb,
             void *c, int ldc, int N, int K) {
-    dep_wait();
-    dep_launch();
     const int lane = threadIdx.x & 31;
     const int n = blockIdx.x * GV_WARPS + (threadIdx.x >> 5);
+    const uint16_t *brow = b + (size_t)(n < N ? n : 0) * ldb;
+    uint4 bq[4];
+    gv_load_step(bq, brow, n < N ? lane * 8 : K, K);
+    dep_wait();
+    dep_launch();
     if (n >= N) return;
-    const uint16_t *brow = b + (size_t)n * ldb;
     float acc[MM];
 #pragma unroll
     for (int m = 0; m < MM; m++) acc[m] = 0.f;
     // 4 independent 16-byte loads in flight per lane per step.
     for (int k0 = lane * 8; k0 < K; k0 += 32 * 8 * 4) {
-        uint4 bq[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-            const int k = k0 + u * 256;
-            bq[u] = (k < K) ? __ldcs((const uint4 *)(brow + k)) : make_uint4(0, 0, 0, 0);
-        }
+        if (k0 != lane * 8) gv_load_step(bq, brow, k0, K);
 #pragma unroll
         for (int u = 0; u < 4; u++) {
             const int k = k0 + u * 256;
@@ -135,22 +145,24 @@ template <int MM>
 __global__ void __launch_bounds__(GV_WARPS * 32)
 gemv_swiglu_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict__ wg,
                    const uint16_t *__restrict__ wu, int ldb, uint16_t *h, int ldh, int N, int K) {
-    dep_wait();
-    dep_launch();
     const int lane = threadIdx.x & 31;
     const int n = blockIdx.x * GV_WARPS + (threadIdx.x >> 5);
+    const size_t row = (size_t)(n < N ? n : 0) * ldb;
+    const uint16_t *grow = wg + row, *urow = wu + row;
+    // first step's gate and up weights before the programmatic-launch wait
+    uint4 gq[4], uq[4];
+    gv_load_step(gq, grow, n < N ? lane * 8 : K, K);
+    gv_load_step(uq, urow, n < N ? lane * 8 : K, K);
+    dep_wait();
+    dep_launch();
     if (n >= N) return;
-    const uint16_t *grow = wg + (size_t)n * ldb, *urow = wu + (size_t)n * ldb;
     float ag[MM], au[MM];
 #pragma unroll
     for (int m = 0; m < MM; m++) ag[m] = au[m] = 0.f;
     for (int k0 = lane * 8; k0 < K; k0 += 32 * 8 * 4) {
-        uint4 gq[4], uq[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-            const int k = k0 + u * 256;
-            gq[u] = (k < K) ? __ldcs((const uint4 *)(grow + k)) : make_uint4(0, 0, 0, 0);
-            uq[u] = (k < K) ? __ldcs((const uint4 *)(urow + k)) : make_uint4(0, 0, 0, 0);
+        if (k0 != lane * 8) {
+            gv_load_step(gq, grow, k0, K);
+            gv_load_step(uq, urow, k0, K);
         }
 #pragma unroll
         for (int u = 0; u < 4; u++) {

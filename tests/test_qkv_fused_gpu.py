@@ -40,7 +40,8 @@ def rows_and_positions(M, rng):
     for s in range(n_slots):
         idx = np.nonzero(seq == s)[0]
         p = rng.permutation(MAX_LEN)[:len(idx)]
-        p[0] = MAX_LEN - 1
+        if MAX_LEN - 1 not in p:
+            p[0] = MAX_LEN - 1
         pos[idx] = p
     return seq, pos, n_slots
 
