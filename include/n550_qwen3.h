@@ -326,6 +326,54 @@ int n550_qwen3_decode_steps(n550_model_t *m, void *stream, int32_t *tokens,
 int n550_qwen3_forward_batch_host(n550_model_t *m, const int32_t *tokens,
                                   int n_token, int pos0, float *logits_host);
 
+/* The configuration a model was created with. */
+int n550_qwen3_get_config(const n550_model_t *m, n550_model_config *cfg);
+
+/* Most tokens per n550_qwen3_forward_rows call: QWEN3_SPEC_BATCH =
+ * QWEN3_MAX_BATCH (qwen3.h:82-88, 145-146). */
+#define N550_ROWS_MAX 128
+
+/* One sequence's n_token (1..N550_ROWS_MAX) tokens at positions
+ * pos0..pos0+n_token-1 of KV slot *seq_id (device int32), with the logits of
+ * EVERY row (qwen3_forward_batch built with QWEN3_SPECULATIVE, qwen3.c:556-566:
+ * row j's logits are the prediction after tokens[0..j]): logits
+ * [n_token][151936] FP32 (may be NULL) and their argmax next_ids[n_token]
+ * (may be NULL, not both). Device buffers, stream-ordered. */
+int n550_qwen3_forward_rows(n550_model_t *m, void *stream, const int32_t *tokens,
+                            const int32_t *seq_id, int n_token, int pos0, float *logits,
+                            int32_t *next_ids);
+
+/* The same on sequence slot 0 with HOST buffers (synchronous): next_ids_host
+ * [n_token] receives every row's argmax, logits_host [n_token][151936] every
+ * row's logits (may be NULL). Requires n_token <= the model's max_tokens. */
+int n550_qwen3_forward_rows_host(n550_model_t *m, const int32_t *tokens, int n_token, int pos0,
+                                 int32_t *next_ids_host, float *logits_host);
+
+/* Prompt-lookup drafting (lookup_draft, main_baremetal.c:567-584): the last
+ * `ngram` tokens of hist[n_hist] are searched for earlier in hist, newest
+ * match first; the up to max_k tokens that followed the match go to draft.
+ * Returns how many (0 when there is no match), or N550_ERR_ARG. */
+int n550_lookup_draft(const int32_t *hist, int n_hist, int ngram, int32_t *draft, int max_k);
+
+typedef struct {
+    int64_t rounds;      /* forward_rows calls after the prefill              */
+    int64_t drafted;     /* draft tokens proposed                             */
+    int64_t accepted;    /* draft tokens equal to the model's own choice      */
+} n550_spec_stats;
+
+/* Greedy generation with prompt-lookup speculative verification (the
+ * QWEN3_SPECULATIVE chat loop, main_baremetal.c:636-690) on sequence slot 0:
+ * prefill the prompt (n_prompt <= max_tokens) at position 0, then per round
+ * feed [next, draft...] (max_draft <= 127 drafts from n550_lookup_draft with
+ * `ngram`) through n550_qwen3_forward_rows and keep the drafts up to the first
+ * one that differs from the model's argmax. Stops after max_new tokens, at
+ * the end of the KV cache, or when the next token is one of eos[n_eos] (not
+ * emitted). out[max_new] receives the tokens, *n_out their count. With
+ * max_draft = 0 it is plain greedy decoding. */
+int n550_qwen3_generate_lookup(n550_model_t *m, const int32_t *prompt, int n_prompt, int max_new,
+                               int max_draft, int ngram, const int32_t *eos, int n_eos,
+                               int32_t *out, int *n_out, n550_spec_stats *stats);
+
 /* Seeded synthetic token ids (the benchmark's inputs), host memory:
  * out[i] = u64(seed, stream, i) mod vocab with the generator of
  * n550_qwen3_init_random. No counterpart in the reference (its prompts come

@@ -32,6 +32,10 @@ class N550Error(RuntimeError):
         super().__init__(f"{what}: {strerror(status)} ({status})" if what else strerror(status))
 
 
+class SpecStats(C.Structure):
+    _fields_ = [("rounds", C.c_int64), ("drafted", C.c_int64), ("accepted", C.c_int64)]
+
+
 class ModelConfig(C.Structure):
     _fields_ = [("max_seqs", C.c_int), ("max_len", C.c_int), ("max_tokens", C.c_int),
                 ("gemm_mode", C.c_int), ("kblock", C.c_int)]
@@ -98,6 +102,12 @@ def lib() -> C.CDLL:
         "n550_qwen3_profile": (i, [vp, i]),
         "n550_qwen3_profile_read": (i, [vp, vp, vp, i]),
         "n550_synth_tokens": (i, [vp, sz, C.c_uint64, C.c_uint64, i]),
+        "n550_qwen3_get_config": (i, [vp, C.POINTER(ModelConfig)]),
+        "n550_qwen3_forward_rows": (i, [vp, vp, vp, vp, i, i, vp, vp]),
+        "n550_qwen3_forward_rows_host": (i, [vp, vp, i, i, vp, vp]),
+        "n550_lookup_draft": (i, [vp, i, i, vp, i]),
+        "n550_qwen3_generate_lookup": (i, [vp, vp, i, i, i, i, vp, i, vp, C.POINTER(C.c_int),
+                                           C.POINTER(SpecStats)]),
         "n550_synth_normal_bf16": (i, [vp, sz, C.c_uint64, C.c_uint64, C.c_double]),
     }
     for name, (res, args) in sig.items():
@@ -140,6 +150,18 @@ def synth_normal_bf16(shape, seed: int, stream: int, sigma: float):
     check(lib().n550_synth_normal_bf16(out.ctypes.data_as(C.c_void_p), out.size, seed, stream, sigma),
           "n550_synth_normal_bf16")
     return out
+
+
+def lookup_draft(hist, ngram: int = 3, max_k: int = 127):
+    """Prompt-lookup draft tokens for the history `hist` (n550_lookup_draft)."""
+    import numpy as np
+    h = np.ascontiguousarray(hist, np.int32)
+    out = np.empty(max(max_k, 1), np.int32)
+    k = lib().n550_lookup_draft(h.ctypes.data_as(C.c_void_p), h.size, ngram,
+                                out.ctypes.data_as(C.c_void_p), max_k)
+    if k < 0:
+        check(k, "n550_lookup_draft")
+    return out[:k].copy()
 
 
 def set_gemm_mode(mode: int, kblock: int = 16) -> None:

@@ -558,15 +558,18 @@ int model_setup(n550_model *m) {
     ALLOC(m->qf, S * QD * 4);
     ALLOC(m->attn, T * QD * 2);
     ALLOC(m->h, T * INTER * 2);
-    ALLOC(m->xl, S * H * 2);
-    ALLOC(m->logits, S * (size_t)VOCAB * 4);
+    // last-token rows; n550_qwen3_forward_rows normalises every row of a
+    // call of up to N550_ROWS_MAX tokens into the same buffer
+    const size_t head_rows = std::max(S, std::min(T, (size_t)N550_ROWS_MAX));
+    ALLOC(m->xl, head_rows * H * 2);
+    ALLOC(m->logits, head_rows * (size_t)VOCAB * 4);
     m->tmp_rows = c.gemm_mode == N550_MODE_EXACT ? T : 8;
     ALLOC(m->tmp_a, m->tmp_rows * INTER * 4);
     ALLOC(m->tmp_b, m->tmp_rows * INTER * 4);
     ALLOC(m->tok_pos, T * 4);
     ALLOC(m->tok_seq, T * 4);
     ALLOC(m->next, S * 4);
-    ALLOC(m->host_tok, T * 4);
+    ALLOC(m->host_tok, (T + N550_ROWS_MAX) * 4);
     ALLOC(m->zero_seq, 4);
     const size_t slots = S * NH * MAX_SPLITS;
     ALLOC(m->part_m, slots * 4);
@@ -1115,6 +1118,55 @@ int n550_qwen3_decode_steps(n550_model_t *m, void *stream, int32_t *tokens, cons
     N550_CUDA_TRY(cudaEventRecord(m->ev_out, cs));
     N550_CUDA_TRY(cudaStreamWaitEvent(st, m->ev_out, 0));
     return rc;
+}
+
+int n550_qwen3_get_config(const n550_model_t *m, n550_model_config *cfg) {
+    if (!m || !cfg) return N550_ERR_ARG;
+    *cfg = m->cfg;
+    return N550_OK;
+}
+
+int n550_qwen3_forward_rows(n550_model_t *m, void *stream, const int32_t *tokens,
+                            const int32_t *seq_id, int n_token, int pos0, float *logits,
+                            int32_t *next_ids) {
+    if (!m || !tokens || !seq_id || n_token < 1 || n_token > N550_ROWS_MAX || pos0 < 0 ||
+        (!logits && !next_ids))
+        return N550_ERR_ARG;
+    const n550_model_config &c = m->cfg;
+    if (pos0 + n_token > c.max_len || n_token > c.max_tokens) return N550_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    {
+        ProfScope ps(m, st, N550_PROF_OTHER, 2);
+        N550_CUDA_TRY(launch_k(setup_prefill_kernel, (n_token + 255) / 256, 256, 0, st, m->tok_pos,
+                               m->tok_seq, seq_id, 1, n_token, pos0));
+        N550_CUDA_TRY(launch_k(embed_kernel, n_token, 128, 0, st, m->x, m->t[0], tokens, n_token,
+                               n_token, 0, nullptr, nullptr, nullptr, nullptr));
+        N550_LAUNCH_CHECK();
+    }
+    bool xl_ready = false;
+    int rc = run_layers(m, st, n_token, false, seq_id, nullptr, 1, n_token, pos0, &xl_ready);
+    if (rc) return rc;
+    // every row is a "last token" of its own (qwen3.c:556-566): the final norm
+    // and the lm_head (+ argmax) over all n_token rows
+    return run_head(m, st, n_token, 1, logits, next_ids);
+}
+
+int n550_qwen3_forward_rows_host(n550_model_t *m, const int32_t *tokens, int n_token, int pos0,
+                                 int32_t *next_ids_host, float *logits_host) {
+    if (!m || !tokens || !next_ids_host || n_token < 1 || n_token > N550_ROWS_MAX) return N550_ERR_ARG;
+    if (n_token > m->cfg.max_tokens) return N550_ERR_ARG;
+    cudaStream_t st = 0;
+    N550_CUDA_TRY(cudaMemcpyAsync(m->host_tok, tokens, (size_t)n_token * 4, cudaMemcpyHostToDevice, st));
+    int rc = n550_qwen3_forward_rows(m, st, m->host_tok, m->zero_seq, n_token, pos0,
+                                     logits_host ? m->logits : nullptr, m->host_tok + n_token);
+    if (rc) return rc;
+    N550_CUDA_TRY(cudaMemcpyAsync(next_ids_host, m->host_tok + n_token, (size_t)n_token * 4,
+                                  cudaMemcpyDeviceToHost, st));
+    if (logits_host)
+        N550_CUDA_TRY(cudaMemcpyAsync(logits_host, m->logits, (size_t)n_token * VOCAB * 4,
+                                      cudaMemcpyDeviceToHost, st));
+    N550_CUDA_TRY(cudaStreamSynchronize(st));
+    return N550_OK;
 }
 
 int n550_qwen3_forward_batch_host(n550_model_t *m, const int32_t *tokens, int n_token, int pos0,

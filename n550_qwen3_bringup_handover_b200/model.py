@@ -7,9 +7,10 @@ import ctypes as C
 
 import numpy as np
 
-from . import MODE_FAST, ModelConfig, check, lib
+from . import MODE_FAST, ModelConfig, SpecStats, check, lib
 
 VOCAB = 151936
+EOS_IDS = (151645, 151643)          # QWEN3_EOS_TOKEN_ID_0 / _1 (qwen3_config.h:29-30)
 
 
 class Model:
@@ -52,6 +53,33 @@ class Model:
         if r < 0:
             check(r, "n550_qwen3_forward_batch_host")
         return int(r), logits
+
+    def forward_rows(self, tokens, pos0: int, want_logits: bool = False):
+        """Every row's argmax (and logits) of one call on slot 0: the
+        QWEN3_SPECULATIVE qwen3_forward_batch (n550_qwen3_forward_rows_host)."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        ids = np.empty(t.size, np.int32)
+        logits = np.empty((t.size, VOCAB), np.float32) if want_logits else None
+        check(lib().n550_qwen3_forward_rows_host(
+            self._h, t.ctypes.data_as(C.c_void_p), t.size, pos0, ids.ctypes.data_as(C.c_void_p),
+            logits.ctypes.data_as(C.c_void_p) if want_logits else None), "n550_qwen3_forward_rows_host")
+        return ids, logits
+
+    def generate_lookup(self, prompt, max_new: int, max_draft: int = 127, ngram: int = 3,
+                        eos=EOS_IDS):
+        """Greedy generation with prompt-lookup speculative verification on
+        slot 0 (n550_qwen3_generate_lookup): (tokens, stats dict)."""
+        p = np.ascontiguousarray(prompt, np.int32)
+        e = np.ascontiguousarray(eos, np.int32)
+        out = np.empty(max(max_new, 1), np.int32)
+        n = C.c_int(0)
+        st = SpecStats()
+        check(lib().n550_qwen3_generate_lookup(
+            self._h, p.ctypes.data_as(C.c_void_p), p.size, max_new, max_draft, ngram,
+            e.ctypes.data_as(C.c_void_p), e.size, out.ctypes.data_as(C.c_void_p), C.byref(n),
+            C.byref(st)), "n550_qwen3_generate_lookup")
+        return out[:n.value].copy(), {"rounds": st.rounds, "drafted": st.drafted,
+                                       "accepted": st.accepted}
 
     # ---- batched device path (torch CUDA tensors) ----
     def prefill(self, tokens, seq_ids, pos0=0, logits=None, next_token=None, stream=None):

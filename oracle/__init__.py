@@ -254,6 +254,8 @@ class RefModel:
         L.ref_model_init.argtypes = [C.c_void_p, C.c_size_t]
         L.ref_forward_batch.argtypes = [C.c_void_p, C.c_int, C.c_int]
         L.ref_logits.restype = C.POINTER(C.c_float)
+        L.ref_logits_row.restype = C.POINTER(C.c_float)
+        L.ref_logits_row.argtypes = [C.c_int]
         L.ref_kernel_name.restype = C.c_char_p
         self.L = L
         self._blob = blob
@@ -266,6 +268,13 @@ class RefModel:
         t = np.ascontiguousarray(tokens, np.int32)
         self.L.ref_forward_batch(_p(t), t.size, pos0)
         return np.ctypeslib.as_array(self.L.ref_logits(), (VOCAB,)).copy()
+
+    def logits_rows(self):
+        """Every row of logits the last call left ([n_logits, VOCAB]); all rows
+        of the call in the QWEN3_SPECULATIVE build (libref_spec.so)."""
+        n = self.L.ref_n_logits()
+        return np.stack([np.ctypeslib.as_array(self.L.ref_logits_row(i), (VOCAB,)).copy()
+                         for i in range(n)])
 
     def gemm(self, a_f32, b_bf16):
         a = np.ascontiguousarray(a_f32, np.float32)
@@ -298,3 +307,65 @@ def ref_gemm(kernel, a_f32, b_bf16):
 
 def ref_available(kernel="scalar"):
     return (REF_DIR / f"libref_{kernel}.so").exists()
+
+
+# ---------------- prompt-lookup speculative decoding ----------------
+
+def lookup_draft(hist, ngram, max_k):
+    """Restates lookup_draft (main_baremetal.c:567-584): the last `ngram`
+    tokens of hist are searched for earlier, newest match first; up to max_k
+    tokens that followed the match are returned ([] without a match)."""
+    n = len(hist)
+    if n < ngram + 1 or max_k <= 0:
+        return []
+    pat = list(hist[n - ngram:])
+    for i in range(n - ngram - 1, -1, -1):
+        if list(hist[i:i + ngram]) != pat:
+            continue
+        out = list(hist[i + ngram:i + ngram + max_k])
+        if out:
+            return out
+    return []
+
+
+def speculative_generate(model, prompt, max_new, max_draft, ngram=3, eos=(151645, 151643),
+                         max_seq=2048):
+    """Restates the QWEN3_SPECULATIVE generation loop (main_baremetal.c:636-690)
+    on a RefModel of libref_spec.so (all-row logits): returns (tokens,
+    rounds, drafted, accepted)."""
+    hist = [int(t) for t in prompt]
+    logits = model.forward_batch(np.asarray(prompt, np.int32), 0)
+    nxt = argmax(logits)
+    limit = min(max_new, max_seq - len(prompt))
+    pos, out = len(prompt), []
+    rounds = drafted = accepted = 0
+    while len(out) < limit:
+        if nxt in eos:
+            break
+        draft = lookup_draft(hist, ngram, max_draft)[:max(0, limit - len(out) - 1)]
+        batch = np.asarray([nxt] + draft, np.int32)
+        model.forward_batch(batch, pos)
+        rows = model.logits_rows()
+        rounds += 1
+        drafted += len(draft)
+        out.append(nxt)
+        hist.append(nxt)
+        kept, done = 1, False
+        for j, d in enumerate(draft):
+            if len(out) >= limit:
+                break
+            pred = argmax(rows[j])
+            if pred != d:
+                nxt, done = pred, True
+                break
+            accepted += 1
+            if pred in eos:
+                nxt, done = pred, True
+                break
+            out.append(pred)
+            hist.append(pred)
+            kept += 1
+        if not done:
+            nxt = argmax(rows[len(draft)])
+        pos += kept
+    return out, rounds, drafted, accepted

@@ -25,6 +25,13 @@ void ref_forward_batch(const int *tokens, int n_token, int pos0) {
 
 const float *ref_logits(void) { return qwen3_last_logits(&g_model); }
 
+/* Rows of logits the last call left: all rows of a call of up to
+ * QWEN3_SPEC_BATCH tokens in a QWEN3_SPECULATIVE build (qwen3.c:556-566),
+ * otherwise the last row only. */
+int ref_n_logits(void) { return g_model.s.n_logits; }
+
+const float *ref_logits_row(int i) { return qwen3_logits_at(&g_model, i); }
+
 int ref_max_seq(void) { return QWEN3_MAX_SEQ; }
 
 const char *ref_kernel_name(void) { return qwen3_kernel_name(); }
