@@ -405,6 +405,60 @@ enum {
 int n550_qwen3_profile(n550_model_t *m, int enable);
 int n550_qwen3_profile_read(n550_model_t *m, double *ms, int64_t *launches, int n_kinds);
 
+/* ===========================================================================
+ * 4. Tokenizer and chat template (tokenizer.h, main.c:124-185): host code.
+ * ========================================================================= */
+typedef struct n550_tok n550_tok_t;
+
+/* Error codes of the tokenizer (QWEN3_TOK_ERR_*, tokenizer.h:47-54). */
+#define N550_TOK_ERR_MAGIC    (-1)
+#define N550_TOK_ERR_VERSION  (-2)
+#define N550_TOK_ERR_SIZE     (-3)
+#define N550_TOK_ERR_OVERFLOW (-5)
+
+/* Loads a QW3T v1 vocabulary (the reference's tok.bin: byte-level BPE
+ * vocabulary, ranked merges, Unicode letter/digit ranges, special tokens;
+ * qwen3_tok_init, tokenizer.c:65-110) from host memory; the bytes are copied.
+ * Returns N550_OK or an N550_TOK_ERR_* code. */
+int n550_tok_init(n550_tok_t **out, const void *blob, size_t size);
+void n550_tok_free(n550_tok_t *t);
+int n550_tok_vocab_size(const n550_tok_t *t);
+
+/* UTF-8 text -> token ids (qwen3_tok_encode, tokenizer.c:313-345): special
+ * tokens matched whole, the rest split by the GPT-style pre-tokenizer and
+ * byte-level BPE. Returns the count, or N550_TOK_ERR_OVERFLOW when more than
+ * max_out ids (or a piece longer than 2048 bytes) would result. */
+int n550_tok_encode(const n550_tok_t *t, const char *text, size_t len, int32_t *out, int max_out);
+
+/* Token ids -> bytes, '\0'-terminated (qwen3_tok_decode, tokenizer.c:347-358).
+ * Returns the bytes written (without the '\0') or N550_TOK_ERR_OVERFLOW.
+ * Ids outside the vocabulary decode to nothing. */
+int n550_tok_decode(const n550_tok_t *t, const int32_t *ids, int n, char *out, size_t max_out);
+
+/* The bytes of one token (qwen3_tok_piece), for streaming output. */
+const uint8_t *n550_tok_piece(const n550_tok_t *t, int id, size_t *len);
+
+/* Many texts at once on up to n_threads host threads (0: all cores): text i
+ * -> out[i * max_out ..], counts[i] its id count. The prompts of a
+ * data-parallel batch. No counterpart in the reference (one prompt at a time). */
+int n550_tok_encode_batch(const n550_tok_t *t, const char *const *texts, const size_t *lens,
+                          int n_texts, int32_t *out, int max_out, int32_t *counts, int n_threads);
+
+/* A user turn in Qwen3's chat template with thinking disabled
+ * (main.c:124-131): "<|im_start|>user\n" prompt
+ * "<|im_end|>\n<|im_start|>assistant\n<think>\n\n</think>\n\n", encoded. */
+int n550_chat_encode(const n550_tok_t *t, const char *prompt, size_t len, int32_t *out, int max_out);
+
+/* Chat end to end (chat_mode, main.c:137-185; with max_draft > 0 the
+ * speculative loop of main_baremetal.c:636-690): the prompt in the chat
+ * template (n550_chat_encode, at most max_tokens ids) on sequence slot 0 from
+ * position 0, up to max_new greedy tokens until an EOS (151645, 151643) or
+ * the end of the KV cache, ids[max_new] and *n_ids, and their text in
+ * text[max_text] ('\0'-terminated). Returns the text's length or an error. */
+int n550_qwen3_chat(n550_model_t *m, const n550_tok_t *tok, const char *prompt, size_t len,
+                    int max_new, int max_draft, char *text, size_t max_text, int32_t *ids,
+                    int *n_ids);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

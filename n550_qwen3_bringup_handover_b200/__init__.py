@@ -20,6 +20,7 @@ OK = 0
 ERR_MAGIC, ERR_VERSION, ERR_DTYPE, ERR_SHAPE, ERR_SIZE, ERR_OOM, ERR_LAYOUT = -1, -2, -3, -4, -5, -6, -7
 ERR_ARG, ERR_CUDA, ERR_UNSUPPORTED, ERR_TIMEOUT = -101, -102, -103, -104
 MODE_EXACT, MODE_FAST = 0, 1
+N550_TOK_ERR_MAGIC, N550_TOK_ERR_VERSION, N550_TOK_ERR_SIZE, N550_TOK_ERR_OVERFLOW = -1, -2, -3, -5
 F32, BF16 = 0, 1
 LAYOUT_ROW, LAYOUT_TILE = 0, 1
 
@@ -108,6 +109,15 @@ def lib() -> C.CDLL:
         "n550_lookup_draft": (i, [vp, i, i, vp, i]),
         "n550_qwen3_generate_lookup": (i, [vp, vp, i, i, i, i, vp, i, vp, C.POINTER(C.c_int),
                                            C.POINTER(SpecStats)]),
+        "n550_tok_init": (i, [C.POINTER(vp), vp, sz]),
+        "n550_tok_free": (None, [vp]),
+        "n550_tok_vocab_size": (i, [vp]),
+        "n550_tok_encode": (i, [vp, C.c_char_p, sz, vp, i]),
+        "n550_tok_decode": (i, [vp, vp, i, C.c_char_p, sz]),
+        "n550_tok_piece": (vp, [vp, i, C.POINTER(sz)]),
+        "n550_tok_encode_batch": (i, [vp, vp, vp, i, vp, i, vp, i]),
+        "n550_chat_encode": (i, [vp, C.c_char_p, sz, vp, i]),
+        "n550_qwen3_chat": (i, [vp, vp, C.c_char_p, sz, i, i, C.c_char_p, sz, vp, C.POINTER(C.c_int)]),
         "n550_synth_normal_bf16": (i, [vp, sz, C.c_uint64, C.c_uint64, C.c_double]),
     }
     for name, (res, args) in sig.items():
@@ -170,3 +180,4 @@ def set_gemm_mode(mode: int, kblock: int = 16) -> None:
 
 from .api import *  # noqa: E402,F401,F403
 from .model import Model  # noqa: E402,F401
+from .tokenizer import Tokenizer  # noqa: E402,F401

@@ -95,4 +95,24 @@ int n550_qwen3_generate_lookup(n550_model_t *m, const int32_t *prompt, int n_pro
     return N550_OK;
 }
 
+int n550_qwen3_chat(n550_model_t *m, const n550_tok_t *tok, const char *prompt, size_t len,
+                    int max_new, int max_draft, char *text, size_t max_text, int32_t *ids,
+                    int *n_ids) {
+    if (!m || !tok || (len && !prompt) || max_new < 0 || !text || !max_text || (max_new && !ids) ||
+        !n_ids)
+        return N550_ERR_ARG;
+    n550_model_config cfg{};
+    int rc = n550_qwen3_get_config(m, &cfg);
+    if (rc) return rc;
+    std::vector<int32_t> in(cfg.max_tokens);
+    const int n_in = n550_chat_encode(tok, prompt, len, in.data(), cfg.max_tokens);
+    if (n_in < 0) return n_in;
+    if (n_in == 0) return N550_ERR_ARG;
+    const int32_t eos[2] = {151645, 151643};          // QWEN3_EOS_TOKEN_ID_0 / _1
+    rc = n550_qwen3_generate_lookup(m, in.data(), n_in, max_new, max_draft, 3, eos, 2, ids, n_ids,
+                                    nullptr);
+    if (rc) return rc;
+    return n550_tok_decode(tok, ids, *n_ids, text, max_text);
+}
+
 }  // extern "C"

@@ -81,6 +81,19 @@ class Model:
         return out[:n.value].copy(), {"rounds": st.rounds, "drafted": st.drafted,
                                        "accepted": st.accepted}
 
+    def chat(self, tokenizer, prompt, max_new: int = 64, max_draft: int = 0,
+             max_text: int = 1 << 16):
+        """One chat turn (n550_qwen3_chat): (reply bytes, generated ids)."""
+        data = prompt.encode() if isinstance(prompt, str) else bytes(prompt)
+        ids = np.empty(max(max_new, 1), np.int32)
+        n = C.c_int(0)
+        buf = C.create_string_buffer(max_text)
+        r = lib().n550_qwen3_chat(self._h, tokenizer.handle, data, len(data), max_new, max_draft,
+                                  buf, max_text, ids.ctypes.data_as(C.c_void_p), C.byref(n))
+        if r < 0:
+            check(r, "n550_qwen3_chat")
+        return buf.raw[:r], ids[:n.value].copy()
+
     # ---- batched device path (torch CUDA tensors) ----
     def prefill(self, tokens, seq_ids, pos0=0, logits=None, next_token=None, stream=None):
         from .api import stream_ptr

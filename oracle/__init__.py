@@ -369,3 +369,37 @@ def speculative_generate(model, prompt, max_new, max_draft, ngram=3, eos=(151645
             nxt = argmax(rows[len(draft)])
         pos += kept
     return out, rounds, drafted, accepted
+
+
+# ---------------- tokenizer ----------------
+
+TOK_PATH = REF_DIR / "tok.bin"
+
+
+class RefTokenizer:
+    """The reference's own tokenizer.c (oracle/_ref/libref_tok.so) on a QW3T
+    vocabulary; one instance per process (the reference keeps static state)."""
+
+    def __init__(self, blob=None):
+        L = C.CDLL(str(REF_DIR / "libref_tok.so"), mode=os.RTLD_LOCAL)
+        L.ref_tok_init.argtypes = [C.c_void_p, C.c_size_t]
+        L.ref_tok_encode.argtypes = [C.c_char_p, C.c_size_t, C.c_void_p, C.c_int]
+        L.ref_tok_decode.argtypes = [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]
+        self.L = L
+        self._blob = np.frombuffer(TOK_PATH.read_bytes() if blob is None else blob, np.uint8).copy()
+        self.rc = L.ref_tok_init(_p(self._blob), self._blob.size)
+
+    def encode(self, data: bytes, max_out=4096):
+        out = np.zeros(max_out, np.int32)
+        n = self.L.ref_tok_encode(data, len(data), _p(out), max_out)
+        return n if n < 0 else out[:n].copy()
+
+    def decode(self, ids, max_out=1 << 16):
+        ids = np.ascontiguousarray(ids, np.int32)
+        buf = C.create_string_buffer(max_out)
+        n = self.L.ref_tok_decode(_p(ids), ids.size, buf, max_out)
+        return n if n < 0 else buf.raw[:n]
+
+
+def tokenizer_available():
+    return TOK_PATH.exists() and (REF_DIR / "libref_tok.so").exists()
