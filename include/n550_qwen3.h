@@ -326,6 +326,12 @@ int n550_qwen3_decode_steps(n550_model_t *m, void *stream, int32_t *tokens,
 int n550_qwen3_forward_batch_host(n550_model_t *m, const int32_t *tokens,
                                   int n_token, int pos0, float *logits_host);
 
+/* Token count (9..1024, default 1024) from which the runtime's decoder layers
+ * take whole-tile GEMMs with fused epilogues instead of split-K partial sums
+ * finished by row kernels. A tuning knob; results do not depend on it beyond
+ * FP32 summation order. */
+int n550_qwen3_split_rows(int rows);
+
 /* The configuration a model was created with. */
 int n550_qwen3_get_config(const n550_model_t *m, n550_model_config *cfg);
 

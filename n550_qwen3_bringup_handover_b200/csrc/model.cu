@@ -488,6 +488,12 @@ namespace {
 
 const uint16_t *W(const n550_model *m, int layer, int j) { return m->t[1 + 11 * layer + j]; }
 
+// Token counts from which a layer's GEMMs run as whole tiles with their fused
+// epilogues (q/k/v with QK-norm, RoPE and the KV write; residual adds by TMA
+// reduce-add; SwiGLU); below, down to 9 tokens, the K loop is split and the
+// partial sums are finished by row kernels (n550_qwen3_split_rows).
+int g_split_rows = 1024;
+
 // Brackets the kernels launched in its scope with an event pair of `kind`
 // (n kernels counted) while profiling is enabled.
 struct ProfScope {
@@ -629,7 +635,7 @@ int mgemm(n550_model *m, cudaStream_t st, int epi, const uint16_t *a, int lda, c
         // gate, up and SiLU . mul in one GEMV launch
         return launch_gemv_swiglu(st, a, lda, w, w2, K, (uint16_t *)c, ldc, M, N, K);
     }
-    if (M < 1024)   // skinny (decode, short prompts): split the K loop over more SMs
+    if (M < g_split_rows)   // skinny (decode, short prompts): split the K loop over more SMs
         return launch_gemm_tc_splitk(st, epi, a, lda, w, K, w2, c, ldc, M, N, K, m->ws, m->ws_bytes);
     return launch_gemm_tc(st, epi, n550_tile_bn(M, epi == TC_EPI_SILU_BF16 ? 2 * N : N), a, lda, w, K, w2, c,
                           ldc, M, N, K, 0);
@@ -794,13 +800,14 @@ int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t
     // 1189 us (skinny) per step.
     if (!exact && T >= 4 && skinny_route(T))
         return run_layers_skinny(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, xl_ready);
-    if (!exact && T > 8 && T < 1024)
+    if (!exact && T > 8 && T < g_split_rows)
         return run_layers_split(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, xl_ready);
+    const bool fused_qkv = !exact && T >= g_split_rows;
     const int gu_kernels = exact ? 3 : 1;
     const int res_kernels = exact ? 2 : 1;
     for (int l = 0; l < NLAYER; l++) {
         STEP(N550_PROF_RMSNORM, 1, launch_norm_rows(st, m->xb, m->x, W(m, l, 0), T));
-        if (!exact && T >= 1024) {
+        if (fused_qkv) {
             // One tcgen05 GEMM with QK-norm, RoPE and the K/V cache write in its epilogue.
             TcQkv q{};
             q.q_bf16 = m->qb;
@@ -816,7 +823,7 @@ int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t
             STEP(N550_PROF_QKNORM_ROPE, 1, launch_qknorm_rope_kv(m, st, T, l, decode));
         }
         // the fused QKV epilogue leaves BF16 queries (decode attention reads either)
-        if ((rc = run_attention(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, l, !exact && T >= 1024)))
+        if ((rc = run_attention(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, l, fused_qkv)))
             return rc;
         STEP(N550_PROF_GEMM_O, res_kernels,
              mgemm(m, st, TC_EPI_RESID_F32, m->attn, QD, W(m, l, 6), nullptr, m->x, H, T, H, QD));
@@ -1118,6 +1125,12 @@ int n550_qwen3_decode_steps(n550_model_t *m, void *stream, int32_t *tokens, cons
     N550_CUDA_TRY(cudaEventRecord(m->ev_out, cs));
     N550_CUDA_TRY(cudaStreamWaitEvent(st, m->ev_out, 0));
     return rc;
+}
+
+int n550_qwen3_split_rows(int rows) {
+    if (rows < 9 || rows > 1024) return N550_ERR_ARG;
+    g_split_rows = rows;
+    return N550_OK;
 }
 
 int n550_qwen3_get_config(const n550_model_t *m, n550_model_config *cfg) {
