@@ -332,6 +332,13 @@ int n550_qwen3_forward_batch_host(n550_model_t *m, const int32_t *tokens,
  * FP32 summation order. */
 int n550_qwen3_split_rows(int rows);
 
+/* Decode steps of 1-4 sequences as one persistent kernel (1, default) or as
+ * the per-layer kernel sequence (0). The persistent kernel runs the 28 layers
+ * on one CTA per SM, separated by bounded grid barriers, with the next phase's
+ * weights streamed into shared memory ahead of use (contexts up to 8192
+ * positions). Results agree within FP32 summation order. */
+int n550_qwen3_fused_decode(int on);
+
 /* The configuration a model was created with. */
 int n550_qwen3_get_config(const n550_model_t *m, n550_model_config *cfg);
 

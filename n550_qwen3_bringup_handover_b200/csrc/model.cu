@@ -28,6 +28,7 @@
 
 #include "attention.h"
 #include "common.cuh"
+#include "decode_fused.h"
 #include "gemm_skinny.h"
 #include "gemm_tc.h"
 #include "launch.h"
@@ -471,6 +472,9 @@ struct n550_model {
     float2 *rope = nullptr;                 // [max_len][64] (cos, sin)
     float *ws = nullptr;                    // split-K partials of skinny GEMMs
     size_t ws_bytes = 0;
+    FusedLayer *fd_layers = nullptr;        // layer tensors for the persistent decode kernel
+    int *fd_counters = nullptr;             // its attention-split arrivals [FD_MAX_TOKENS][8]
+    unsigned *fd_barrier = nullptr;         // its grid-barrier counter
     // captured decode step (n550_qwen3_decode_steps)
     cudaGraphExec_t graph = nullptr;
     int g_n = 0;
@@ -493,6 +497,25 @@ const uint16_t *W(const n550_model *m, int layer, int j) { return m->t[1 + 11 * 
 // reduce-add; SwiGLU); below, down to 9 tokens, the K loop is split and the
 // partial sums are finished by row kernels (n550_qwen3_split_rows).
 int g_split_rows = 1024;
+
+// Decode steps of up to FD_MAX_TOKENS sequences run as one persistent kernel
+// (n550_qwen3_fused_decode).
+bool g_fused_decode = false;
+
+int run_layers_fused(n550_model *m, cudaStream_t st, int T, const int32_t *seq_ids, const int32_t *pos) {
+    FusedDecodeArgs a{};
+    a.layers = m->fd_layers;
+    a.final_norm = m->t[N_TENSORS - 1];
+    a.kc = m->kc; a.vc = m->vc; a.max_len = m->cfg.max_len;
+    a.rope = m->rope;
+    a.seq_ids = seq_ids; a.pos = pos; a.T = T;
+    a.x = m->x; a.qkv = m->qkv; a.attn = m->attn; a.h = m->h;
+    a.part_m = m->part_m; a.part_l = m->part_l; a.part_o = m->part_o;
+    a.counters = m->fd_counters;
+    a.barrier = m->fd_barrier;
+    a.xl = m->xl;
+    return launch_decode_fused(st, a);
+}
 
 // Brackets the kernels launched in its scope with an event pair of `kind`
 // (n kernels counted) while profiling is enabled.
@@ -525,7 +548,8 @@ void model_release(n550_model *m) {
     for (cudaEvent_t e : m->prof.pool) cudaEventDestroy(e);
     void *ptrs[] = {m->blob, m->fused_qkv, m->kc, m->vc, m->x, m->qkv, m->qf, m->logits, m->xb,
                     m->qb, m->attn, m->h, m->xl, m->tmp_a, m->tmp_b, m->tok_pos, m->tok_seq,
-                    m->next, m->host_tok, m->zero_seq, m->part_m, m->part_l, m->part_o, m->rope, m->ws};
+                    m->next, m->host_tok, m->zero_seq, m->part_m, m->part_l, m->part_o, m->rope, m->ws,
+                    m->fd_layers, m->fd_counters, m->fd_barrier};
     for (void *p : ptrs) if (p) cudaFree(p);
     delete m;
 }
@@ -586,11 +610,22 @@ int model_setup(n550_model *m) {
     m->ws_bytes = (size_t)8 * std::min<size_t>(T, 1023) * 2 * INTER * 4;
     ALLOC(m->ws, m->ws_bytes);
     ALLOC(m->step_counter, 4);
+    ALLOC(m->fd_layers, NLAYER * sizeof(FusedLayer));
+    ALLOC(m->fd_counters, FD_MAX_TOKENS * NKVH * sizeof(int));
+    ALLOC(m->fd_barrier, sizeof(unsigned));
     N550_CUDA_TRY(cudaStreamCreateWithFlags(&m->cap_stream, cudaStreamNonBlocking));
     N550_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming));
     N550_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_out, cudaEventDisableTiming));
 #undef ALLOC
     N550_CUDA_TRY(cudaMemset(m->zero_seq, 0, 4));
+    N550_CUDA_TRY(cudaMemset(m->fd_counters, 0, FD_MAX_TOKENS * NKVH * sizeof(int)));
+    {
+        FusedLayer fl[NLAYER];
+        for (int l = 0; l < NLAYER; l++)
+            fl[l] = FusedLayer{W(m, l, 0), m->wqkv[l], W(m, l, 4), W(m, l, 5), W(m, l, 6),
+                               W(m, l, 7), W(m, l, 8), W(m, l, 9), W(m, l, 10)};
+        N550_CUDA_TRY(cudaMemcpy(m->fd_layers, fl, sizeof fl, cudaMemcpyHostToDevice));
+    }
     N550_CUDA_TRY(cudaMemset(m->kc, 0, kv * 2));
     N550_CUDA_TRY(cudaMemset(m->vc, 0, kv * 2));
     int rc = ensure_rope_table();
@@ -793,6 +828,14 @@ int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t
     int rc = N550_OK;
     *xl_ready = false;
     const bool exact = c.gemm_mode == N550_MODE_EXACT;
+    // A decode step of a few sequences: all 28 layers in one persistent kernel
+    if (!exact && decode && g_fused_decode && T <= FD_MAX_TOKENS && c.max_len <= FD_MAX_LEN &&
+        T <= c.max_seqs && fused_decode_grid() > 0) {
+        ProfScope ps(m, st, N550_PROF_GEMM_QKV, 1);
+        if ((rc = run_layers_fused(m, st, T, seq_ids, pos))) return rc;
+        *xl_ready = true;
+        return N550_OK;
+    }
     // From 4 tokens on the skinny GEMMs (7 kernels per layer) beat the GEMV
     // path (10); below, the GEMV's shorter launches win. Measured on B200,
     // graph-replayed decode steps with the lm_head routed alike: 1, 2, 4, 8
@@ -1125,6 +1168,11 @@ int n550_qwen3_decode_steps(n550_model_t *m, void *stream, int32_t *tokens, cons
     N550_CUDA_TRY(cudaEventRecord(m->ev_out, cs));
     N550_CUDA_TRY(cudaStreamWaitEvent(st, m->ev_out, 0));
     return rc;
+}
+
+int n550_qwen3_fused_decode(int on) {
+    g_fused_decode = on != 0;
+    return N550_OK;
 }
 
 int n550_qwen3_split_rows(int rows) {
