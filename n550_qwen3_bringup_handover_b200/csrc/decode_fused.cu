@@ -51,7 +51,7 @@ struct Smem {
     float *ored;           // [WARPS][256] partial P.V sums
     float *hv;             // [4][128] q(2g), q(2g+1), k, v of an attention unit
     float *red;            // [64] block reductions
-    uint64_t *bar;         // [2] weight-buffer mbarriers
+    uint64_t *bar;         // [3] weight-buffer mbarriers, K rows of an attention unit
     int *flag;             // barrier/abort flag
 };
 
@@ -128,10 +128,9 @@ __device__ void issue_rows(const Smem &s, int buf, const uint16_t *W, const uint
     const uint32_t row = (uint32_t)K * 2, nrow = (uint32_t)(c1 - c0);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     mbar_arrive_expect_tx(&s.bar[buf], row * nrow * (W2 ? 2 : 1));
-    for (uint32_t r = 0; r < nrow; r++) {
-        bulk_load(s.wbuf[buf] + r * row, W + (size_t)(c0 + r) * K, row, &s.bar[buf]);
-        if (W2) bulk_load(s.wbuf[buf] + (nrow + r) * row, W2 + (size_t)(c0 + r) * K, row, &s.bar[buf]);
-    }
+    // rows [c0, c1) of a row-major [N][K] matrix are one contiguous range
+    bulk_load(s.wbuf[buf], W + (size_t)c0 * K, row * nrow, &s.bar[buf]);
+    if (W2) bulk_load(s.wbuf[buf] + nrow * row, W2 + (size_t)c0 * K, row * nrow, &s.bar[buf]);
 }
 
 // Dot products of one weight row (shared memory, K BF16) with the T rows of
@@ -217,16 +216,24 @@ __device__ void load_act(uint16_t *act, const uint16_t *src, int T, int K) {
         ((uint4 *)act)[i] = __ldcg((const uint4 *)src + i);
 }
 
-// Splits of the attention over positions [0, pos]: at most 256 positions per
-// unit (the V rows a warp holds in registers), few units while the context is
-// short.
+// Rows of K a unit copies into shared memory (the activation buffer, free
+// during the attention phase): 96 x 256 bytes.
+constexpr int KSM_ROWS = ACT / (HD * 2);
+
+// Splits of the attention over positions [0, pos]: up to 96 positions per
+// unit while that takes at most FD_MAX_SPLITS units per (token, KV head), so
+// that a unit's K rows arrive by one bulk copy; longer contexts take 32 units
+// of up to 256 positions (the V rows a warp holds in registers) and read K
+// directly.
 __device__ __forceinline__ int attn_splits(int pos) {
-    return (pos + 1 + 255) / 256;
+    const int s = (pos + 1 + KSM_ROWS - 1) / KSM_ROWS;
+    return s < FD_MAX_SPLITS ? s : FD_MAX_SPLITS;
 }
 
 // One attention unit: token t, KV head g, split sp of S (qwen3.c:287-292,
 // 374-436 and 498-511 for that head pair).
-__device__ void attn_unit(const FusedDecodeArgs &a, const Smem &s, int l, int t, int g, int sp, int S) {
+__device__ void attn_unit(const FusedDecodeArgs &a, const Smem &s, int l, int t, int g, int sp, int S,
+                          uint32_t &kphase) {
     const int pos = a.pos[t], seq = a.seq_ids[t];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const FusedLayer &L = a.layers[l];
@@ -234,6 +241,14 @@ __device__ void attn_unit(const FusedDecodeArgs &a, const Smem &s, int l, int t,
     const int p0 = (int)((long long)n * sp / S), p1 = (int)((long long)n * (sp + 1) / S);
     const uint16_t *kbase = a.kc + ((size_t)(seq * NL + l) * NKV + g) * a.max_len * HD;
     const uint16_t *vbase = a.vc + ((size_t)(seq * NL + l) * NKV + g) * a.max_len * HD;
+    // K rows [p0, p1) are contiguous in the cache: one bulk copy into shared
+    // memory (the row at pos is not written yet; its scores use the new k)
+    const bool k_smem = p1 - p0 <= KSM_ROWS;
+    if (k_smem && threadIdx.x == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive_expect_tx(&s.bar[2], (uint32_t)(p1 - p0) * HD * 2);
+        bulk_load(s.act, kbase + (size_t)p0 * HD, (uint32_t)(p1 - p0) * HD * 2, &s.bar[2]);
+    }
     // V rows of this warp's positions (at most 16: a unit spans <= 256) are
     // requested first, so that their latency overlaps the head vectors and scores
     constexpr int VP = 256 / WARPS;
@@ -280,6 +295,10 @@ __device__ void attn_unit(const FusedDecodeArgs &a, const Smem &s, int l, int t,
         for (int j = 0; j < 4; j++) s.hv[warp * HD + lane + 32 * j] = v[j];
     }
     __syncthreads();
+    if (k_smem) {
+        mbar_wait(&s.bar[2], kphase);       // on expiry the status is set; the copy still lands here
+        kphase ^= 1;
+    }
     // scores, one position per thread
     float m0 = -INFINITY, m1 = -INFINITY;
     for (int p = p0 + (int)threadIdx.x; p < p1; p += THREADS) {
@@ -291,9 +310,12 @@ __device__ void attn_unit(const FusedDecodeArgs &a, const Smem &s, int l, int t,
                 d1 = fmaf(s.hv[HD + d], k, d1);
             }
         } else {
-            const uint4 *kr = (const uint4 *)(kbase + (size_t)p * HD);
+            const uint4 *kr = k_smem ? (const uint4 *)(s.act + (size_t)(p - p0) * HD)
+                                     : (const uint4 *)(kbase + (size_t)p * HD);
+            const int rot = k_smem ? (lane & 7) : 0;     // spreads the rows of 8 lanes over the banks
 #pragma unroll 4
-            for (int c = 0; c < 16; c++) {
+            for (int cc = 0; cc < 16; cc++) {
+                const int c = (cc + rot) & 15;
                 const uint4 q = kr[c];
                 const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
@@ -413,15 +435,16 @@ __global__ void __launch_bounds__(THREADS, 1) decode_fused_kernel(FusedDecodeArg
     s.hv = s.ored + WARPS * 256;
     s.red = s.hv + 4 * HD;
     s.bar = (uint64_t *)(s.red + 64);
-    s.flag = (int *)(s.bar + 2);
+    s.flag = (int *)(s.bar + 3);
     const int T = a.T;
     if (threadIdx.x == 0) {
         mbar_init(&s.bar[0], 1);
         mbar_init(&s.bar[1], 1);
+        mbar_init(&s.bar[2], 1);
         fence_mbar_init();
     }
     __syncthreads();
-    uint32_t phase[2] = {0, 0};
+    uint32_t phase[2] = {0, 0}, kphase = 0;
     int pending[2] = {0, 0};            // copies issued into a buffer and not yet waited for
     unsigned target = 0;
     const unsigned G = gridDim.x;
@@ -472,7 +495,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_fused_kernel(FusedDecodeArg
             int t = 0, r = u;
             while (r >= NKV * attn_splits(a.pos[t])) { r -= NKV * attn_splits(a.pos[t]); t++; }
             const int S = attn_splits(a.pos[t]);
-            attn_unit(a, s, l, t, r / S, r % S, S);
+            attn_unit(a, s, l, t, r / S, r % S, S, kphase);
         }
         if (!sync()) return;
         // ---- C: o projection + residual ----
