@@ -27,7 +27,6 @@ __device__ int g_device_status = 0;
 
 namespace {
 
-constexpr int TILE = 64;       // 64 x 64 outputs per CTA, 4 x 4 per thread
 constexpr int THREADS = 256;
 constexpr int MAXKB = 32;
 
@@ -101,14 +100,14 @@ __device__ double xround_f64(long long (&L)[XLIMBS]) {
 // One block of the rule, exactly: operands are BF16 values held as FP32 in
 // shared memory (a[k*stride], b[k*stride]).
 __device__ __noinline__ float exact_block(float acc, const float *a, const float *b,
-                                          int stride, int len) {
+                                          int sa, int sb, int len) {
     bool finite = isfinite(acc);
     for (int k = 0; k < len; k++)
-        finite = finite && isfinite(a[k * stride]) && isfinite(b[k * stride]);
+        finite = finite && isfinite(a[k * sa]) && isfinite(b[k * sb]);
     if (!finite) {
         double s = (double)acc;
         for (int k = 0; k < len; k++)
-            s = __dadd_rn(s, __dmul_rn((double)a[k * stride], (double)b[k * stride]));
+            s = __dadd_rn(s, __dmul_rn((double)a[k * sa], (double)b[k * sb]));
         return __double2float_rn(s);
     }
     long long L[XLIMBS];
@@ -121,8 +120,8 @@ __device__ __noinline__ float exact_block(float acc, const float *a, const float
         xadd(L, (int)(u >> 31), m, ex ? ex - 150 : -149);
     }
     for (int k = 0; k < len; k++) {
-        const uint32_t ua = __float_as_uint(a[k * stride]) >> 16;
-        const uint32_t ub = __float_as_uint(b[k * stride]) >> 16;
+        const uint32_t ua = __float_as_uint(a[k * sa]) >> 16;
+        const uint32_t ub = __float_as_uint(b[k * sb]) >> 16;
         const int ea = (ua >> 7) & 0xFF, eb = (ub >> 7) & 0xFF;
         const unsigned long long ma = ea ? (128u + (ua & 0x7Fu)) : (ua & 0x7Fu);
         const unsigned long long mb = eb ? (128u + (ub & 0x7Fu)) : (ub & 0x7Fu);
@@ -132,64 +131,77 @@ __device__ __noinline__ float exact_block(float acc, const float *a, const float
     return __double2float_rn(xround_f64(L));
 }
 
-template <bool A_F32>
+// TM x TN outputs per CTA, RM x RN per thread (THREADS = TM/RM x TN/RN): 64 x 64
+// tiles of 4 x 4 for many rows, 16 x 16 tiles of one output per thread for
+// few rows (decode, BASELINE configs[0]'s 16 rows), so that such GEMMs spread
+// over 8x more CTAs instead of computing mostly padding rows.
+// KC: K elements staged in shared memory at a time (a multiple of 32, so whole
+// K-blocks of 16 or 32); the small tiles stage 256 so that the global loads of
+// 16 K-blocks are in flight together.
+template <bool A_F32, int TM, int TN, int RM, int RN, int KC>
 __global__ void __launch_bounds__(THREADS)
 gemm_exact_kernel(const void *__restrict__ a_ptr, int lda,
                   const uint16_t *__restrict__ b, int ldb,
                   float *__restrict__ c, int ldc, int M, int N, int K, int kblock) {
+    static_assert((TM / RM) * (TN / RN) == THREADS, "one thread per RM x RN outputs");
+    constexpr int CX = TN / RN, CY = TM / RM;
     dep_wait();
     dep_launch();
-    __shared__ float As[MAXKB][TILE];
-    __shared__ float Bs[MAXKB][TILE];
-    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-    const int m0 = blockIdx.y * TILE, n0 = blockIdx.x * TILE;
+    static_assert(KC % MAXKB == 0, "whole K-blocks per stage");
+    __shared__ float As[KC][TM];
+    __shared__ float Bs[KC][TN];
+    const int tx = threadIdx.x % CX, ty = threadIdx.x / CX;
+    const int m0 = blockIdx.y * TM, n0 = blockIdx.x * TN;
 
-    float acc[4][4];
+    float acc[RM][RN];
 #pragma unroll
-    for (int i = 0; i < 4; i++)
+    for (int i = 0; i < RM; i++)
 #pragma unroll
-        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+        for (int j = 0; j < RN; j++) acc[i][j] = 0.0f;
 
-    for (int k0 = 0; k0 < K; k0 += kblock) {
-        const int len = min(kblock, K - k0);
-        // Stage the block: rows m0..m0+63 of A, n0..n0+63 of B, k0..k0+kblock.
-        for (int e = threadIdx.x; e < TILE * kblock; e += THREADS) {
-            const int r = e / kblock, kk = e - r * kblock;
-            const int k = k0 + kk;
-            float av = 0.0f, bv = 0.0f;
-            if (kk < len) {
-                if (m0 + r < M) {
-                    if (A_F32) {
-                        const float *ar = (const float *)a_ptr + (size_t)(m0 + r) * lda;
-                        av = bf16_bits_to_f32(f32_to_bf16_rne(ar[k]));
-                    } else {
-                        const uint16_t *ar = (const uint16_t *)a_ptr + (size_t)(m0 + r) * lda;
-                        av = bf16_bits_to_f32(ar[k]);
-                    }
+    for (int kc0 = 0; kc0 < K; kc0 += KC) {
+        const int clen = min(KC, K - kc0);
+        // Stage K elements [kc0, kc0 + clen) of rows m0.. of A and n0.. of B.
+        for (int e = threadIdx.x; e < TM * KC; e += THREADS) {
+            const int r = e / KC, kk = e - r * KC;
+            float av = 0.0f;
+            if (kk < clen && m0 + r < M) {
+                if (A_F32) {
+                    const float *ar = (const float *)a_ptr + (size_t)(m0 + r) * lda;
+                    av = bf16_bits_to_f32(f32_to_bf16_rne(ar[kc0 + kk]));
+                } else {
+                    const uint16_t *ar = (const uint16_t *)a_ptr + (size_t)(m0 + r) * lda;
+                    av = bf16_bits_to_f32(ar[kc0 + kk]);
                 }
-                if (n0 + r < N) bv = bf16_bits_to_f32(b[(size_t)(n0 + r) * ldb + k]);
             }
             As[kk][r] = av;
+        }
+        for (int e = threadIdx.x; e < TN * KC; e += THREADS) {
+            const int r = e / KC, kk = e - r * KC;
+            float bv = 0.0f;
+            if (kk < clen && n0 + r < N) bv = bf16_bits_to_f32(b[(size_t)(n0 + r) * ldb + kc0 + kk]);
             Bs[kk][r] = bv;
         }
         __syncthreads();
+      for (int kb0 = 0; kb0 < clen; kb0 += kblock) {
+        const int len = min(kblock, clen - kb0);
 
-        double s[4][4], e[4][4];
+        double s[RM][RN], e[RM][RN];
 #pragma unroll
-        for (int i = 0; i < 4; i++)
+        for (int i = 0; i < RM; i++)
 #pragma unroll
-            for (int j = 0; j < 4; j++) { s[i][j] = (double)acc[i][j]; e[i][j] = 0.0; }
+            for (int j = 0; j < RN; j++) { s[i][j] = (double)acc[i][j]; e[i][j] = 0.0; }
 
         for (int kk = 0; kk < len; kk++) {
-            double av[4], bv[4];
+            double av[RM], bv[RN];
 #pragma unroll
-            for (int i = 0; i < 4; i++) av[i] = (double)As[kk][ty + 16 * i];
+            for (int i = 0; i < RM; i++) av[i] = (double)As[kb0 + kk][ty + CY * i];
 #pragma unroll
-            for (int j = 0; j < 4; j++) bv[j] = (double)Bs[kk][tx + 16 * j];
+            for (int j = 0; j < RN; j++) bv[j] = (double)Bs[kb0 + kk][tx + CX * j];
 #pragma unroll
-            for (int i = 0; i < 4; i++)
+            for (int i = 0; i < RM; i++)
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
+                for (int j = 0; j < RN; j++) {
                     const double p = __dmul_rn(av[i], bv[j]);          // exact
                     const double t = __dadd_rn(s[i][j], p);
                     const double bp = __dsub_rn(t, s[i][j]);
@@ -200,26 +212,27 @@ gemm_exact_kernel(const void *__restrict__ a_ptr, int lda,
                 }
         }
 #pragma unroll
-        for (int i = 0; i < 4; i++)
+        for (int i = 0; i < RM; i++)
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
+            for (int j = 0; j < RN; j++) {
                 if (e[i][j] == 0.0 && isfinite(s[i][j])) {
                     acc[i][j] = (s[i][j] == 0.0) ? 0.0f : __double2float_rn(s[i][j]);
                 } else {
-                    acc[i][j] = exact_block(acc[i][j], &As[0][ty + 16 * i],
-                                            &Bs[0][tx + 16 * j], TILE, len);
+                    acc[i][j] = exact_block(acc[i][j], &As[kb0][ty + CY * i],
+                                            &Bs[kb0][tx + CX * j], TM, TN, len);
                 }
             }
+      }
         __syncthreads();
     }
 
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int m = m0 + ty + 16 * i;
+    for (int i = 0; i < RM; i++) {
+        const int m = m0 + ty + CY * i;
         if (m >= M) continue;
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int n = n0 + tx + 16 * j;
+        for (int j = 0; j < RN; j++) {
+            const int n = n0 + tx + CX * j;
             if (n < N) c[(size_t)m * ldc + n] = acc[i][j];
         }
     }
@@ -235,12 +248,16 @@ int launch_gemm_exact(cudaStream_t st, const void *a, int a_type, int lda,
     if (M == 0 || N == 0) return N550_OK;
     if (lda < K || ldb < K || ldc < N) return N550_ERR_ARG;
     if (!c || (K && (!a || !b))) return N550_ERR_ARG;
-    const long long gy = (M + TILE - 1) / TILE, gx = (N + TILE - 1) / TILE;
+    if (a_type != N550_F32 && a_type != N550_BF16) return N550_ERR_ARG;
+    const bool few = M <= 16;
+    const int tm = few ? 16 : 64, tn = few ? 16 : 64;
+    const long long gy = (M + tm - 1) / tm, gx = (N + tn - 1) / tn;
     if (gy > 65535 || gx > 0x7FFFFFFF) return N550_ERR_UNSUPPORTED;
     dim3 grid((unsigned)gx, (unsigned)gy);
-    if (a_type != N550_F32 && a_type != N550_BF16) return N550_ERR_ARG;
-    N550_CUDA_TRY(launch_k(a_type == N550_F32 ? gemm_exact_kernel<true> : gemm_exact_kernel<false>, grid,
-                           THREADS, 0, st, a, lda, b, ldb, c, ldc, M, N, K, kblock));
+    const bool f32 = a_type == N550_F32;
+    auto kern = few ? (f32 ? gemm_exact_kernel<true, 16, 16, 1, 1, 256> : gemm_exact_kernel<false, 16, 16, 1, 1, 256>)
+                    : (f32 ? gemm_exact_kernel<true, 64, 64, 4, 4, MAXKB> : gemm_exact_kernel<false, 64, 64, 4, 4, MAXKB>);
+    N550_CUDA_TRY(launch_k(kern, grid, THREADS, 0, st, a, lda, b, ldb, c, ldc, M, N, K, kblock));
     return N550_OK;
 }
 

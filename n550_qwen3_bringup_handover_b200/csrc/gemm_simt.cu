@@ -87,9 +87,33 @@ __device__ __forceinline__ void gv_load_step(uint4 (&q)[4], const uint16_t *row,
 }
 
 // One warp per output column n; requires K % 8 == 0 and 16-byte aligned rows.
-// The weights do not depend on the previous kernel, so the first step's loads
-// (the whole row for K <= 1024) are issued before the programmatic-launch
-// wait and overlap that kernel's tail; the activations are read after it.
+// The weights do not depend on the previous kernel, so rows of up to 3072
+// elements (every projection of the model) are requested whole -- 12 16-byte
+// loads per lane in flight -- before the programmatic-launch wait, and overlap
+// that kernel's tail; the activations are read after it. Longer rows continue
+// in steps of 4 loads per lane. The summation order does not depend on it.
+constexpr int GV_PRE = 3;           // steps of 1024 elements held in registers
+
+template <int MM>
+__device__ __forceinline__ void gv_consume(const uint4 (&q)[4], const uint16_t *__restrict__ a, int lda,
+                                           int k0, int K, float (&acc)[MM]) {
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        const int k = k0 + u * 256;
+        if (k >= K) break;
+        float bf[8];
+        bf16x8_to_f32(q[u], bf);
+#pragma unroll
+        for (int m = 0; m < MM; m++) {
+            const uint4 aq = __ldg((const uint4 *)(a + (size_t)m * lda + k));
+            float af[8];
+            bf16x8_to_f32(aq, af);
+#pragma unroll
+            for (int j = 0; j < 8; j++) acc[m] = fmaf(af[j], bf[j], acc[m]);
+        }
+    }
+}
+
 template <int MM, int EPI>
 __global__ void __launch_bounds__(GV_WARPS * 32)
 gemv_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict__ b, int ldb,
@@ -97,32 +121,22 @@ gemv_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict_
     const int lane = threadIdx.x & 31;
     const int n = blockIdx.x * GV_WARPS + (threadIdx.x >> 5);
     const uint16_t *brow = b + (size_t)(n < N ? n : 0) * ldb;
-    uint4 bq[4];
-    gv_load_step(bq, brow, n < N ? lane * 8 : K, K);
+    const int k_first = n < N ? lane * 8 : K;
+    uint4 bq[GV_PRE][4];
+#pragma unroll
+    for (int s = 0; s < GV_PRE; s++) gv_load_step(bq[s], brow, k_first + s * 1024, K);
     dep_wait();
     dep_launch();
     if (n >= N) return;
     float acc[MM];
 #pragma unroll
     for (int m = 0; m < MM; m++) acc[m] = 0.f;
-    // 4 independent 16-byte loads in flight per lane per step.
-    for (int k0 = lane * 8; k0 < K; k0 += 32 * 8 * 4) {
-        if (k0 != lane * 8) gv_load_step(bq, brow, k0, K);
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
-            const int k = k0 + u * 256;
-            if (k >= K) break;
-            float bf[8];
-            bf16x8_to_f32(bq[u], bf);
-#pragma unroll
-            for (int m = 0; m < MM; m++) {
-                const uint4 aq = __ldg((const uint4 *)(a + (size_t)m * lda + k));
-                float af[8];
-                bf16x8_to_f32(aq, af);
-#pragma unroll
-                for (int j = 0; j < 8; j++) acc[m] = fmaf(af[j], bf[j], acc[m]);
-            }
-        }
+    for (int s = 0; s < GV_PRE; s++) gv_consume<MM>(bq[s], a, lda, lane * 8 + s * 1024, K, acc);
+    for (int k0 = lane * 8 + GV_PRE * 1024; k0 < K; k0 += 1024) {
+        uint4 q[4];
+        gv_load_step(q, brow, k0, K);
+        gv_consume<MM>(q, a, lda, k0, K, acc);
     }
 #pragma unroll
     for (int m = 0; m < MM; m++) {
