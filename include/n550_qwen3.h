@@ -332,6 +332,12 @@ int n550_qwen3_forward_batch_host(n550_model_t *m, const int32_t *tokens,
  * FP32 summation order. */
 int n550_qwen3_split_rows(int rows);
 
+/* Decode steps that take the split-K or GEMV q/k/v route: the decode attention
+ * kernel applies QK-norm and RoPE to the raw q/k/v rows and writes the new K/V
+ * itself (1, default) or a separate row kernel does (0). Bit-identical
+ * results either way. */
+int n550_qwen3_fused_attention_prep(int on);
+
 /* Decode steps of 1-4 sequences as one persistent kernel (1, default) or as
  * the per-layer kernel sequence (0). The persistent kernel runs the 28 layers
  * on one CTA per SM, separated by bounded grid barriers, with the next phase's

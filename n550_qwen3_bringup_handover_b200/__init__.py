@@ -106,6 +106,7 @@ def lib() -> C.CDLL:
         "n550_qwen3_get_config": (i, [vp, C.POINTER(ModelConfig)]),
         "n550_qwen3_split_rows": (i, [i]),
         "n550_qwen3_fused_decode": (i, [i]),
+        "n550_qwen3_fused_attention_prep": (i, [i]),
         "n550_qwen3_forward_rows": (i, [vp, vp, vp, vp, i, i, vp, vp]),
         "n550_qwen3_forward_rows_host": (i, [vp, vp, i, i, vp, vp]),
         "n550_lookup_draft": (i, [vp, i, i, vp, i]),

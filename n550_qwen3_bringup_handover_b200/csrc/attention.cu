@@ -27,6 +27,7 @@ constexpr int NKV = 8;
 constexpr int NL = 28;
 constexpr float kScale = 0.08838834764831845f;     // qwen3.c:296
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kEps = 1e-6f;                      // RMSNorm epsilon (qwen3_config.h)
 
 // ---------------------------------------------------------------------------
 // decode (split-KV; q.K^T and P.V on mma.sync tensor-core fragments)
@@ -84,6 +85,7 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
     uint64_t *empty = full + DC_STAGES;
     __shared__ float wm[DC_WARPS][2], wl[DC_WARPS][2];
     __shared__ __align__(16) float wo[DC_WARPS][2][HD];
+    __shared__ __align__(16) float hv[4][HD];      // fused mode: q (2 heads), k, v of this KV head
 
     // The sequence ids and positions are inputs of the whole step (written
     // before the kernels this one depends on; read through L2), and cache
@@ -117,14 +119,67 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
         tma_load_3d(b + 3 * DC_BOX, &tmV, &full[st], 64, t0, plane);
     };
     // Tiles that end before position pos[s] are requested before waiting for
-    // the previous kernel, so their latency overlaps its tail.
+    // the previous kernel, so their latency overlaps its tail. In fused mode
+    // every tile is: the row at pos[s] is replaced in shared memory by the K/V
+    // this kernel computes.
+    const bool fused = p.qkv != nullptr;
+    const int pos = kv_len - 1;
     int pre = 0;
     if (threadIdx.x == 0)
-        while (pre < min(DC_STAGES, n_tiles) && start + (pre + 1) * DC_TP <= kv_len - 1) issue(pre++);
+        while (pre < min(DC_STAGES, n_tiles) && (fused || start + (pre + 1) * DC_TP <= pos)) issue(pre++);
     dep_wait();
     dep_launch();
     if (threadIdx.x == 0)
         for (int i = pre; i < min(DC_STAGES, n_tiles); i++) issue(i);
+    if (fused) {
+        // warp 0 / 1: query heads 2 kvh, 2 kvh + 1; warp 2: K head kvh; warp 3: V head kvh
+        const int col = warp < 2 ? (kvh * 2 + warp) * HD : (warp == 2 ? 16 * HD + kvh * HD : 24 * HD + kvh * HD);
+        const float *src = p.qkv + (size_t)s * p.qkv_ld + col + lane;
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {          // the split-K slices summed in order
+            if (p.qkv_ks <= 0) {
+                v[j] = src[32 * j];
+            } else {
+                float a[8];
+#pragma unroll
+                for (int k = 0; k < 8; k++) a[k] = k < p.qkv_ks ? src[32 * j + k * p.qkv_slice] : 0.f;
+                float acc = a[0];
+#pragma unroll
+                for (int k = 1; k < 8; k++) acc += a[k];
+                v[j] = acc;
+            }
+        }
+        if (warp < 3) {
+            const uint16_t *w = warp < 2 ? p.q_norm : p.k_norm;
+            float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+            const float sc = 1.0f / sqrtf(ss / (float)HD + kEps);
+#pragma unroll
+            for (int j = 0; j < 4; j++) v[j] = v[j] * sc * bf16_bits_to_f32(w[lane + 32 * j]);
+#pragma unroll
+            for (int j = 0; j < 2; j++) {      // rotate-half pairs (i, i + 64)
+                const float2 cs = p.rope[(size_t)pos * 64 + lane + 32 * j];
+                const float a = v[j], b = v[j + 2];
+                v[j] = a * cs.x - b * cs.y;
+                v[j + 2] = b * cs.x + a * cs.y;
+            }
+        }
+        if (warp >= 2) {                       // K and V as the cache holds them
+            uint16_t *dst = (warp == 2 ? p.kc_w : p.vc_w) + ((size_t)plane * p.max_len + pos) * HD;
+            const bool writer = start <= pos && pos < end;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const uint16_t b = f32_to_bf16_rne(v[j]);
+                if (writer) dst[lane + 32 * j] = b;
+                v[j] = bf16_bits_to_f32(b);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) hv[warp][lane + 32 * j] = v[j];
+        __syncthreads();
+    }
 
     // A fragments of q (x scale x log2 e, BF16): row g = lane / 4 is query
     // head 2 kvh + g for g < 2, zero otherwise; columns 16 kk + 2 tq (+1, +8).
@@ -135,7 +190,10 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
 #pragma unroll
         for (int h8 = 0; h8 < 2; h8++) {
             float v0 = 0.f, v1 = 0.f;
-            if (g < 2) {
+            if (g < 2 && fused) {
+                v0 = hv[g][16 * kk + 8 * h8 + 2 * tq];
+                v1 = hv[g][16 * kk + 8 * h8 + 2 * tq + 1];
+            } else if (g < 2) {
                 const size_t o = (size_t)s * p.ldq + (size_t)(kvh * 2 + g) * HD + 16 * kk + 8 * h8 + 2 * tq;
                 v0 = p.q_f32 ? p.q_f32[o] : bf16_bits_to_f32(p.q_bf16[o]);
                 v1 = p.q_f32 ? p.q_f32[o + 1] : bf16_bits_to_f32(p.q_bf16[o + 1]);
@@ -156,6 +214,18 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
         uint8_t *kt = ring + st * DC_STAGE_BYTES;
         const uint32_t kb = smem_u32(kt), vb = kb + 2 * DC_BOX;
         const int t0 = start + tile * DC_TP + p0;              // this warp's first position
+        // fused mode: the row at pos[s] (loaded stale) takes this kernel's K and V
+        if (fused && pos >= t0 && pos < t0 + DC_PPW) {
+            const int r = p0 + (pos - t0), c = lane & 15, which = lane >> 4;
+            const float *src = hv[2 + which] + 8 * c;
+            uint4 q;
+            q.x = pack_bf16x2(src[0], src[1]);
+            q.y = pack_bf16x2(src[2], src[3]);
+            q.z = pack_bf16x2(src[4], src[5]);
+            q.w = pack_bf16x2(src[6], src[7]);
+            *(uint4 *)(kt + which * 2 * DC_BOX + dc_off(r, 8 * c)) = q;
+            __syncwarp();
+        }
         // V rows past the end of the range may hold anything (stale cache):
         // zero them so that 0-weights do not meet NaN.
         if (t0 + DC_PPW > end) {

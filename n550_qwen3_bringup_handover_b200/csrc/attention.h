@@ -27,6 +27,18 @@ struct AttnDecodeArgs {
     int ldq, ldo, layer, max_len, splits;
     int kv_planes;            // slots x 28 layers x 8 KV heads in the cache
     float *part_m, *part_l, *part_o;   // split-KV partials (splits > 1)
+    // Fused q/k/v preparation (qkv != NULL; q_f32 / q_bf16 are then unused):
+    // raw q/k/v rows [s][qkv_ld] FP32, the sum of qkv_ks split-K slices
+    // qkv_slice floats apart (qkv_ks <= 0: one row); each CTA applies the
+    // per-head RMSNorm (q_norm, k_norm) and RoPE (rope table) to its two query
+    // heads and its KV head, and the CTA whose positions include pos[s] writes
+    // that position's K/V into the cache (qwen3.c:287-292, 498-511).
+    const float *qkv;
+    int qkv_ld, qkv_ks;
+    size_t qkv_slice;
+    const uint16_t *q_norm, *k_norm;
+    const float2 *rope;
+    uint16_t *kc_w, *vc_w;
 };
 
 int launch_attn_prefill(cudaStream_t st, const AttnPrefillArgs &a, int n_seqs);

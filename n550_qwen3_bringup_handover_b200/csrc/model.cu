@@ -721,8 +721,14 @@ int launch_final_norm(cudaStream_t st, uint16_t *xl, const float *x, const uint1
         if ((rc = (expr))) return rc;                 \
     } while (0)
 
+// Decode attention takes the q/k/v rows before QK-norm and RoPE and finishes
+// them itself (the K/V write included) instead of a separate row kernel
+// (n550_qwen3_fused_attention_prep).
+bool g_fused_prep = true;
+
 int run_attention(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t *seq_ids,
-                  const int32_t *pos, int Sc, int Lc, int p0, int l, bool q_in_bf16 = false) {
+                  const int32_t *pos, int Sc, int Lc, int p0, int l, bool q_in_bf16 = false,
+                  const float *raw_qkv = nullptr, int ks = 0) {
     const n550_model_config &c = m->cfg;
     int rc = N550_OK;
     if (decode) {
@@ -735,6 +741,11 @@ int run_attention(n550_model *m, cudaStream_t st, int T, bool decode, const int3
         a.kv_planes = c.max_seqs * NLAYER * NKVH;
         a.splits = attn_decode_splits(T, c.max_len, MAX_SPLITS);
         a.part_m = m->part_m; a.part_l = m->part_l; a.part_o = m->part_o;
+        if (raw_qkv) {
+            a.qkv = raw_qkv; a.qkv_ld = QKVD; a.qkv_ks = ks; a.qkv_slice = (size_t)T * QKVD;
+            a.q_norm = W(m, l, 4); a.k_norm = W(m, l, 5); a.rope = m->rope;
+            a.kc_w = m->kc; a.vc_w = m->vc;
+        }
         STEP(N550_PROF_ATTN, a.splits > 1 ? 2 : 1, launch_attn_decode(st, a, T));
     } else {
         AttnPrefillArgs a{};
@@ -759,8 +770,12 @@ int run_layers_split(n550_model *m, cudaStream_t st, int T, bool decode, const i
     STEP(N550_PROF_RMSNORM, 1, launch_norm_rows(st, m->xb, m->x, W(m, 0, 0), T));
     for (int l = 0; l < NLAYER; l++) {
         STEP(N550_PROF_GEMM_QKV, 1, partials(m, st, m->xb, H, m->wqkv[l], T, QKVD, H, &ks));
-        STEP(N550_PROF_QKNORM_ROPE, 1, launch_qknorm_rope_kv(m, st, T, l, decode, m->ws, ks));
-        if ((rc = run_attention(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, l))) return rc;
+        if (decode && g_fused_prep) {
+            if ((rc = run_attention(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, l, false, m->ws, ks))) return rc;
+        } else {
+            STEP(N550_PROF_QKNORM_ROPE, 1, launch_qknorm_rope_kv(m, st, T, l, decode, m->ws, ks));
+            if ((rc = run_attention(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, l))) return rc;
+        }
         STEP(N550_PROF_GEMM_O, 1, partials(m, st, m->attn, QD, W(m, l, 6), T, H, QD, &ks));
         STEP(N550_PROF_RMSNORM, 1, launch_resid_norm(st, m->x, m->ws, ks, T, W(m, l, 7), m->xb));
         STEP(N550_PROF_GEMM_GATEUP, gu_kernels,
@@ -863,10 +878,13 @@ int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t
         } else {
             STEP(N550_PROF_GEMM_QKV, 1,
                  mgemm(m, st, TC_EPI_F32, m->xb, H, m->wqkv[l], nullptr, m->qkv, QKVD, T, QKVD, H));
-            STEP(N550_PROF_QKNORM_ROPE, 1, launch_qknorm_rope_kv(m, st, T, l, decode));
+            if (!(decode && g_fused_prep))
+                STEP(N550_PROF_QKNORM_ROPE, 1, launch_qknorm_rope_kv(m, st, T, l, decode));
         }
-        // the fused QKV epilogue leaves BF16 queries (decode attention reads either)
-        if ((rc = run_attention(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, l, fused_qkv)))
+        // the fused QKV epilogue leaves BF16 queries (decode attention reads either);
+        // otherwise decode attention may finish the raw q/k/v rows itself
+        const float *raw = !fused_qkv && decode && g_fused_prep ? m->qkv : nullptr;
+        if ((rc = run_attention(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, l, fused_qkv, raw, 0)))
             return rc;
         STEP(N550_PROF_GEMM_O, res_kernels,
              mgemm(m, st, TC_EPI_RESID_F32, m->attn, QD, W(m, l, 6), nullptr, m->x, H, T, H, QD));
@@ -1168,6 +1186,11 @@ int n550_qwen3_decode_steps(n550_model_t *m, void *stream, int32_t *tokens, cons
     N550_CUDA_TRY(cudaEventRecord(m->ev_out, cs));
     N550_CUDA_TRY(cudaStreamWaitEvent(st, m->ev_out, 0));
     return rc;
+}
+
+int n550_qwen3_fused_attention_prep(int on) {
+    g_fused_prep = on != 0;
+    return N550_OK;
 }
 
 int n550_qwen3_fused_decode(int on) {
