@@ -345,6 +345,17 @@ int n550_qwen3_fused_attention_prep(int on);
  * positions). Results agree within FP32 summation order. */
 int n550_qwen3_fused_decode(int on);
 
+/* Per-op tensor dump (qwen3_set_dump / EMIT, qwen3.h:169-184, qwen3.c:464-575):
+ * while fn is set, n550_qwen3_forward_batch_host runs the forward op by op with
+ * every intermediate tensor materialised and calls fn(ctx, layer, name, data,
+ * n) with an FP32 host copy of each, under the reference's names and in its
+ * order ("embed_out", per layer "input_layernorm_out" ... "layer_out",
+ * "final_norm_out", "logits"; layer -1 outside the layers). A debugging route
+ * for locating numerical drift against the reference's own dump; it
+ * allocates its buffers and synchronises per tensor. NULL turns it off. */
+typedef void (*n550_dump_fn)(void *ctx, int layer, const char *name, const float *data, size_t n);
+int n550_qwen3_set_dump(n550_model_t *m, n550_dump_fn fn, void *ctx);
+
 /* The configuration a model was created with. */
 int n550_qwen3_get_config(const n550_model_t *m, n550_model_config *cfg);
 

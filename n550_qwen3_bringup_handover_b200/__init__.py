@@ -105,6 +105,7 @@ def lib() -> C.CDLL:
         "n550_synth_tokens": (i, [vp, sz, C.c_uint64, C.c_uint64, i]),
         "n550_qwen3_get_config": (i, [vp, C.POINTER(ModelConfig)]),
         "n550_qwen3_split_rows": (i, [i]),
+        "n550_qwen3_set_dump": (i, [vp, vp, vp]),
         "n550_qwen3_fused_decode": (i, [i]),
         "n550_qwen3_fused_attention_prep": (i, [i]),
         "n550_qwen3_forward_rows": (i, [vp, vp, vp, vp, i, i, vp, vp]),

@@ -284,6 +284,18 @@ qknorm_rope_kv_kernel(const float *__restrict__ qkv, int ldqkv, int ks, size_t s
     }
 }
 
+// K/V rows (FP32, after QK-norm and RoPE) of T tokens of sequence slot 0 into
+// the BF16 cache at positions pos0.. (the dump route's qwen3.c:498-511).
+__global__ void dump_kv_kernel(uint16_t *kc, uint16_t *vc, const float *__restrict__ k,
+                               const float *__restrict__ v, int layer, int max_len, int pos0) {
+    dep_wait();
+    dep_launch();
+    const int t = blockIdx.x, i = threadIdx.x, kvh = i >> 7, d = i & 127;
+    const size_t o = (((size_t)layer * NKVH + kvh) * max_len + pos0 + t) * HDIM + d;
+    kc[o] = f32_to_bf16_rne(k[(size_t)t * KVD + i]);
+    vc[o] = f32_to_bf16_rne(v[(size_t)t * KVD + i]);
+}
+
 // (cos, sin) of pos * inv_freq[i] for every position and rotation pair: the
 // RoPE factors of ops_scalar.c:21-35, computed once per model with the same
 // function the fused q/k/v GEMM epilogue evaluates in registers.
@@ -472,6 +484,8 @@ struct n550_model {
     float2 *rope = nullptr;                 // [max_len][64] (cos, sin)
     float *ws = nullptr;                    // split-K partials of skinny GEMMs
     size_t ws_bytes = 0;
+    n550_dump_fn dump = nullptr;            // per-op tensor dump (n550_qwen3_set_dump)
+    void *dump_ctx = nullptr;
     FusedLayer *fd_layers = nullptr;        // layer tensors for the persistent decode kernel
     int *fd_counters = nullptr;             // its attention-split arrivals [FD_MAX_TOKENS][8]
     unsigned *fd_barrier = nullptr;         // its grid-barrier counter
@@ -918,6 +932,108 @@ int run_head(n550_model *m, cudaStream_t st, int Sc, int Lc, float *logits, int3
     return N550_OK;
 }
 
+// The forward of T tokens of slot 0 op by op with every intermediate tensor
+// materialised in FP32 and handed to the dump callback under the reference's
+// names and in its order (qwen3.c:464-575, the EMIT points). The GEMMs take
+// BF16 inputs and give FP32 as the runtime's; norms, RoPE, SiLU . mul and the
+// residual adds are the op kernels of the C ABI; attention is the tcgen05
+// prefill attention on the BF16 cache. For locating numerical drift, not speed.
+int dump_forward(n550_model *m, cudaStream_t st, const int32_t *tokens, int T, int pos0) {
+    const n550_model_config &c = m->cfg;
+    float *q = nullptr, *k = nullptr, *v = nullptr, *g = nullptr, *u = nullptr, *o = nullptr,
+          *att = nullptr, *host = nullptr;
+    uint16_t *bf = nullptr, *attn = nullptr;
+    int rc = N550_OK;
+    auto emit = [&](int layer, const char *name, const float *d, size_t n) -> int {
+        N550_CUDA_TRY(cudaMemcpyAsync(host, d, n * 4, cudaMemcpyDeviceToHost, st));
+        N550_CUDA_TRY(cudaStreamSynchronize(st));
+        m->dump(m->dump_ctx, layer, name, host, n);
+        return N550_OK;
+    };
+    const size_t Tn = (size_t)T;
+#define DTRY(expr) do { if ((rc = (expr))) goto done; } while (0)
+#define DALLOC(p, bytes) do { if (cudaMalloc((void **)&(p), (bytes)) != cudaSuccess) { \
+        (void)cudaGetLastError(); rc = N550_ERR_OOM; goto done; } } while (0)
+    DALLOC(q, Tn * QD * 4); DALLOC(k, Tn * KVD * 4); DALLOC(v, Tn * KVD * 4);
+    DALLOC(g, Tn * INTER * 4); DALLOC(u, Tn * INTER * 4); DALLOC(o, Tn * H * 4);
+    DALLOC(att, Tn * QD * 4); DALLOC(bf, Tn * INTER * 2); DALLOC(attn, Tn * QD * 2);
+    if (cudaMallocHost((void **)&host, (size_t)VOCAB * 4 + Tn * INTER * 4) != cudaSuccess) {
+        (void)cudaGetLastError();
+        host = nullptr;
+        rc = N550_ERR_OOM;
+        goto done;
+    }
+    if (launch_k(setup_prefill_kernel, (T + 255) / 256, 256, 0, st, m->tok_pos, m->tok_seq,
+                 m->zero_seq, 1, T, pos0) != cudaSuccess ||
+        launch_k(embed_kernel, T, 128, 0, st, m->x, m->t[0], tokens, T, T, 0, nullptr, nullptr,
+                 nullptr, nullptr) != cudaSuccess) { rc = N550_ERR_CUDA; goto done; }
+    DTRY(emit(-1, "embed_out", m->x, Tn * H));
+    for (int l = 0; l < NLAYER; l++) {
+        // xb = rmsnorm(x) (FP32 dumped, BF16 into the GEMMs)
+        DTRY(launch_rmsnorm(st, o, N550_F32, m->x, W(m, l, 0), T, H, EPS));
+        DTRY(emit(l, "input_layernorm_out", o, Tn * H));
+        DTRY(launch_f32_to_bf16(st, bf, H, o, H, T, H));
+        DTRY(mgemm(m, st, TC_EPI_F32, bf, H, W(m, l, 1), nullptr, q, QD, T, QD, H));
+        DTRY(emit(l, "q_proj_out", q, Tn * QD));
+        DTRY(launch_rmsnorm(st, q, N550_F32, q, W(m, l, 4), T * NH, HDIM, EPS));
+        DTRY(emit(l, "q_norm_out", q, Tn * QD));
+        DTRY(mgemm(m, st, TC_EPI_F32, bf, H, W(m, l, 2), nullptr, k, KVD, T, KVD, H));
+        DTRY(emit(l, "k_proj_out", k, Tn * KVD));
+        DTRY(launch_rmsnorm(st, k, N550_F32, k, W(m, l, 5), T * NKVH, HDIM, EPS));
+        DTRY(emit(l, "k_norm_out", k, Tn * KVD));
+        DTRY(mgemm(m, st, TC_EPI_F32, bf, H, W(m, l, 3), nullptr, v, KVD, T, KVD, H));
+        DTRY(emit(l, "v_proj_out", v, Tn * KVD));
+        DTRY(launch_rope(st, q, T, NH, pos0));
+        DTRY(emit(l, "q_rope_out", q, Tn * QD));
+        DTRY(launch_rope(st, k, T, NKVH, pos0));
+        DTRY(emit(l, "k_rope_out", k, Tn * KVD));
+        if (launch_k(dump_kv_kernel, T, KVD, 0, st, m->kc, m->vc, (const float *)k, (const float *)v, l,
+                     c.max_len, pos0) != cudaSuccess) { rc = N550_ERR_CUDA; goto done; }
+        DTRY(launch_f32_to_bf16(st, bf, QD, q, QD, T, QD));      // BF16 queries, as the runtime's
+        {
+            AttnPrefillArgs a{};
+            a.q = bf; a.kc = m->kc; a.vc = m->vc; a.out = attn; a.seq_ids = m->zero_seq;
+            a.ldq = QD; a.ldo = QD; a.L = T; a.pos0 = pos0; a.layer = l; a.max_len = c.max_len;
+            a.kv_planes = c.max_seqs * NLAYER * NKVH;
+            DTRY(launch_attn_prefill(st, a, 1));
+        }
+        DTRY(launch_bf16_to_f32(st, att, attn, Tn * QD));
+        DTRY(emit(l, "attn_out", att, Tn * QD));
+        DTRY(mgemm(m, st, TC_EPI_F32, attn, QD, W(m, l, 6), nullptr, o, H, T, H, QD));
+        DTRY(emit(l, "o_proj_out", o, Tn * H));
+        DTRY(launch_residual_add(st, m->x, o, Tn * H));
+        DTRY(emit(l, "x_after_attn_residual", m->x, Tn * H));
+        DTRY(launch_rmsnorm(st, o, N550_F32, m->x, W(m, l, 7), T, H, EPS));
+        DTRY(emit(l, "post_attn_norm_out", o, Tn * H));
+        DTRY(launch_f32_to_bf16(st, bf, H, o, H, T, H));
+        DTRY(mgemm(m, st, TC_EPI_F32, bf, H, W(m, l, 8), nullptr, g, INTER, T, INTER, H));
+        DTRY(emit(l, "gate_proj_out", g, Tn * INTER));
+        DTRY(mgemm(m, st, TC_EPI_F32, bf, H, W(m, l, 9), nullptr, u, INTER, T, INTER, H));
+        DTRY(emit(l, "up_proj_out", u, Tn * INTER));
+        DTRY(launch_silu_mul(st, g, u, Tn * INTER));
+        DTRY(emit(l, "silu_gate_mul_up", g, Tn * INTER));
+        DTRY(launch_f32_to_bf16(st, bf, INTER, g, INTER, T, INTER));
+        DTRY(mgemm(m, st, TC_EPI_F32, bf, INTER, W(m, l, 10), nullptr, o, H, T, H, INTER));
+        DTRY(emit(l, "down_proj_out", o, Tn * H));
+        DTRY(launch_residual_add(st, m->x, o, Tn * H));
+        DTRY(emit(l, "layer_out", m->x, Tn * H));
+    }
+    DTRY(launch_rmsnorm(st, o, N550_F32, m->x, m->t[N_TENSORS - 1], T, H, EPS));
+    DTRY(emit(-1, "final_norm_out", o, Tn * H));
+    DTRY(launch_f32_to_bf16(st, bf, H, o + (Tn - 1) * H, H, 1, H));
+    DTRY(mgemm(m, st, TC_EPI_F32, bf, H, m->t[0], nullptr, m->logits, VOCAB, 1, VOCAB, H));
+    DTRY(emit(-1, "logits", m->logits, VOCAB));
+done:
+#undef DTRY
+#undef DALLOC
+    cudaStreamSynchronize(st);
+    for (void *p : {(void *)q, (void *)k, (void *)v, (void *)g, (void *)u, (void *)o, (void *)att,
+                    (void *)bf, (void *)attn})
+        if (p) cudaFree(p);
+    if (host) cudaFreeHost(host);
+    return rc;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1253,12 +1369,31 @@ int n550_qwen3_forward_rows_host(n550_model_t *m, const int32_t *tokens, int n_t
     return N550_OK;
 }
 
+int n550_qwen3_set_dump(n550_model_t *m, n550_dump_fn fn, void *ctx) {
+    if (!m) return N550_ERR_ARG;
+    m->dump = fn;
+    m->dump_ctx = ctx;
+    return N550_OK;
+}
+
 int n550_qwen3_forward_batch_host(n550_model_t *m, const int32_t *tokens, int n_token, int pos0,
                                   float *logits_host) {
     if (!m || !tokens || n_token < 1) return N550_ERR_ARG;
     if (n_token > m->cfg.max_tokens) return N550_ERR_ARG;
     cudaStream_t st = 0;
     N550_CUDA_TRY(cudaMemcpyAsync(m->host_tok, tokens, (size_t)n_token * 4, cudaMemcpyHostToDevice, st));
+    if (m->dump) {
+        if (pos0 < 0 || pos0 + n_token > m->cfg.max_len) return N550_ERR_ARG;
+        int rc = dump_forward(m, st, m->host_tok, n_token, pos0);
+        if (rc) return rc;
+        int32_t best = 0;
+        N550_CUDA_TRY(launch_argmax(st, m->logits, 1, VOCAB, VOCAB, m->next) ? cudaErrorUnknown : cudaSuccess);
+        N550_CUDA_TRY(cudaMemcpyAsync(&best, m->next, 4, cudaMemcpyDeviceToHost, st));
+        if (logits_host)
+            N550_CUDA_TRY(cudaMemcpyAsync(logits_host, m->logits, (size_t)VOCAB * 4, cudaMemcpyDeviceToHost, st));
+        N550_CUDA_TRY(cudaStreamSynchronize(st));
+        return best;
+    }
     int rc = n550_qwen3_prefill(m, st, m->host_tok, m->zero_seq, 1, n_token, pos0, m->logits, m->next);
     if (rc) return rc;
     int32_t best = 0;

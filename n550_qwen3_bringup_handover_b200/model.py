@@ -54,6 +54,23 @@ class Model:
             check(r, "n550_qwen3_forward_batch_host")
         return int(r), logits
 
+    def forward_dump(self, tokens, pos0: int):
+        """forward_batch on slot 0 with the per-op dump (n550_qwen3_set_dump):
+        (next id, [(layer, name, FP32 array), ...] in the reference's order)."""
+        out = []
+        fn_t = C.CFUNCTYPE(None, C.c_void_p, C.c_int, C.c_char_p, C.POINTER(C.c_float), C.c_size_t)
+
+        def cb(ctx, layer, name, data, n):
+            out.append((layer, name.decode(), np.ctypeslib.as_array(data, (n,)).copy()))
+
+        f = fn_t(cb)
+        check(lib().n550_qwen3_set_dump(self._h, f, None), "n550_qwen3_set_dump")
+        try:
+            nxt, _ = self.forward_batch(tokens, pos0)
+        finally:
+            lib().n550_qwen3_set_dump(self._h, fn_t(0), None)
+        return nxt, out
+
     def forward_rows(self, tokens, pos0: int, want_logits: bool = False):
         """Every row's argmax (and logits) of one call on slot 0: the
         QWEN3_SPECULATIVE qwen3_forward_batch (n550_qwen3_forward_rows_host)."""

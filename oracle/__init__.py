@@ -269,6 +269,24 @@ class RefModel:
         self.L.ref_forward_batch(_p(t), t.size, pos0)
         return np.ctypeslib.as_array(self.L.ref_logits(), (VOCAB,)).copy()
 
+    def forward_dump(self, tokens, pos0):
+        """forward_batch with the reference's per-op dump on: the list of
+        (layer, name, FP32 array) of every EMIT point, in order."""
+        out = []
+        fn_t = C.CFUNCTYPE(None, C.c_void_p, C.c_int, C.c_char_p, C.POINTER(C.c_float), C.c_size_t)
+
+        def cb(ctx, layer, name, data, n):
+            out.append((layer, name.decode(), np.ctypeslib.as_array(data, (n,)).copy()))
+
+        f = fn_t(cb)
+        self.L.ref_set_dump.argtypes = [fn_t, C.c_void_p]
+        self.L.ref_set_dump(f, None)
+        try:
+            self.forward_batch(tokens, pos0)
+        finally:
+            self.L.ref_set_dump(fn_t(0), None)
+        return out
+
     def logits_rows(self):
         """Every row of logits the last call left ([n_logits, VOCAB]); all rows
         of the call in the QWEN3_SPECULATIVE build (libref_spec.so)."""

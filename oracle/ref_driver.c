@@ -34,4 +34,8 @@ const float *ref_logits_row(int i) { return qwen3_logits_at(&g_model, i); }
 
 int ref_max_seq(void) { return QWEN3_MAX_SEQ; }
 
+/* The reference's per-op dump (qwen3_set_dump, qwen3.c:238-247): fn receives
+ * every EMIT point of the following forward calls; NULL turns it off. */
+void ref_set_dump(qwen3_dump_fn fn, void *ctx) { qwen3_set_dump(&g_model, fn, ctx); }
+
 const char *ref_kernel_name(void) { return qwen3_kernel_name(); }
