@@ -335,6 +335,36 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
             if (d == 0) { p.part_m[slot] = M; p.part_l[slot] = L; }
         }
     }
+    if (p.splits == 1 || !p.counters) return;
+    // The CTA that completes this (sequence, KV head) merges the splits of its
+    // two heads, in split order (the combine kernel's arithmetic).
+    __shared__ int last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        int *ctr = p.counters + s * NKV + kvh;
+        last = atomicAdd(ctr, 1) == p.splits - 1;
+        if (last) {
+            *ctr = 0;                              // ready for the next call
+            __threadfence();
+        }
+    }
+    __syncthreads();
+    if (!last) return;
+    for (int i = threadIdx.x; i < 2 * HD; i += DC_THREADS) {
+        const int head = kvh * 2 + (i >> 7), d = i & 127;
+        const size_t slot0 = ((size_t)s * 16 + head) * p.splits;
+        float M = -INFINITY;
+        for (int k = 0; k < p.splits; k++) M = fmaxf(M, __ldcg(p.part_m + slot0 + k));
+        float L = 0.f, O = 0.f;
+        for (int k = 0; k < p.splits; k++) {
+            const float mi = __ldcg(p.part_m + slot0 + k);
+            const float f = (mi == -INFINITY) ? 0.f : exp2f(mi - M);
+            L += __ldcg(p.part_l + slot0 + k) * f;
+            O += __ldcg(p.part_o + (slot0 + k) * HD + d) * f;
+        }
+        p.out[(size_t)s * p.ldo + head * HD + d] = f32_to_bf16_rne(O / L);
+    }
 }
 
 __global__ void attn_combine_kernel(AttnDecodeArgs p) {
@@ -394,7 +424,7 @@ int launch_attn_decode(cudaStream_t st, const AttnDecodeArgs &a, int n_seqs) {
     dim3 grid(a.splits, NKV, n_seqs);
     N550_CUDA_TRY(launch_k(attn_decode_kernel, grid, DC_THREADS, DC_SMEM, st, tk, tv, a));
     N550_LAUNCH_CHECK();
-    if (a.splits > 1) {
+    if (a.splits > 1 && !a.counters) {
         N550_CUDA_TRY(launch_k(attn_combine_kernel, dim3(16, n_seqs), HD, 0, st, a));
         N550_LAUNCH_CHECK();
     }

@@ -27,6 +27,10 @@ struct AttnDecodeArgs {
     int ldq, ldo, layer, max_len, splits;
     int kv_planes;            // slots x 28 layers x 8 KV heads in the cache
     float *part_m, *part_l, *part_o;   // split-KV partials (splits > 1)
+    // splits > 1: per (sequence, KV head) arrival counters, zero between
+    // calls; the CTA that completes a pair merges its splits (no separate
+    // combine kernel). NULL: the combine kernel runs after the splits.
+    int *counters;
     // Fused q/k/v preparation (qkv != NULL; q_f32 / q_bf16 are then unused):
     // raw q/k/v rows [s][qkv_ld] FP32, the sum of qkv_ks split-K slices
     // qkv_slice floats apart (qkv_ks <= 0: one row); each CTA applies the

@@ -151,6 +151,50 @@ gemv_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict_
     }
 }
 
+// Rows of 2048-4096 elements (the o and down projections) with the K loop
+// split over KS warps per output column, one 1024-element step each, partial
+// sums added in step order: 4x the warps of gemv_kernel in flight for the
+// same N, so that the few-row decode step's narrow projections (1024
+// outputs) are not held back by one 8-warp block per SM. Each warp's weights
+// are requested before the programmatic-launch wait.
+constexpr int GVK_COLS = 4;         // output columns per block
+
+template <int MM, int EPI, int KS>
+__global__ void __launch_bounds__(GVK_COLS * KS * 32)
+gemv_ksplit_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict__ b, int ldb,
+                   void *c, int ldc, int N, int K) {
+    __shared__ float part[GVK_COLS][KS][MM];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int col = warp / KS, kp = warp % KS;
+    const int n = blockIdx.x * GVK_COLS + col;
+    const uint16_t *brow = b + (size_t)(n < N ? n : 0) * ldb;
+    const int k0 = n < N ? kp * 1024 + lane * 8 : K;
+    uint4 q[4];
+    gv_load_step(q, brow, k0, K);
+    dep_wait();
+    dep_launch();
+    float acc[MM];
+#pragma unroll
+    for (int m = 0; m < MM; m++) acc[m] = 0.f;
+    if (n < N) gv_consume<MM>(q, a, lda, k0, K, acc);
+#pragma unroll
+    for (int m = 0; m < MM; m++) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xFFFFFFFFu, acc[m], o);
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int m = 0; m < MM; m++) part[col][kp][m] = acc[m];
+    }
+    __syncthreads();
+    if (kp == 0 && lane < MM && n < N) {
+        float v = part[col][0][lane];
+#pragma unroll
+        for (int k = 1; k < KS; k++) v += part[col][k][lane];
+        epi_store<EPI>(c, ldc, lane, n, v);
+    }
+}
+
 // Gate and up rows of output n in one warp (h = silu(x . wg[n]) * (x . wu[n])
 // as BF16, ops_scalar.c:46-51): the SwiGLU of the few-token decode step in one
 // launch instead of two GEMVs and an elementwise kernel. Same per-row loop and
@@ -238,6 +282,33 @@ __global__ void f32_to_bf16_kernel(uint16_t *out, int ldo, const float *in, int 
 template <int MM>
 int gemv_dispatch(cudaStream_t st, int epi, const uint16_t *a, int lda, const uint16_t *b,
                   int ldb, void *c, int ldc, int N, int K) {
+    // 2-4 steps of 1024 and at most 2048 columns: one warp per step
+    if (K > 1024 && K <= 4096 && N <= 2048) {
+        const int ks = (K + 1023) / 1024;
+        const int grid = (N + GVK_COLS - 1) / GVK_COLS;
+        auto go = [&](auto kernel) {
+            return launch_k(kernel, grid, GVK_COLS * ks * 32, 0, st, a, lda, b, ldb, c, ldc, N, K);
+        };
+        cudaError_t e;
+        if (ks == 2) {
+            if (epi == TC_EPI_F32) e = go(gemv_ksplit_kernel<MM, TC_EPI_F32, 2>);
+            else if (epi == TC_EPI_BF16) e = go(gemv_ksplit_kernel<MM, TC_EPI_BF16, 2>);
+            else if (epi == TC_EPI_RESID_F32) e = go(gemv_ksplit_kernel<MM, TC_EPI_RESID_F32, 2>);
+            else return N550_ERR_ARG;
+        } else if (ks == 3) {
+            if (epi == TC_EPI_F32) e = go(gemv_ksplit_kernel<MM, TC_EPI_F32, 3>);
+            else if (epi == TC_EPI_BF16) e = go(gemv_ksplit_kernel<MM, TC_EPI_BF16, 3>);
+            else if (epi == TC_EPI_RESID_F32) e = go(gemv_ksplit_kernel<MM, TC_EPI_RESID_F32, 3>);
+            else return N550_ERR_ARG;
+        } else {
+            if (epi == TC_EPI_F32) e = go(gemv_ksplit_kernel<MM, TC_EPI_F32, 4>);
+            else if (epi == TC_EPI_BF16) e = go(gemv_ksplit_kernel<MM, TC_EPI_BF16, 4>);
+            else if (epi == TC_EPI_RESID_F32) e = go(gemv_ksplit_kernel<MM, TC_EPI_RESID_F32, 4>);
+            else return N550_ERR_ARG;
+        }
+        N550_CUDA_TRY(e);
+        return N550_OK;
+    }
     const int grid = (N + GV_WARPS - 1) / GV_WARPS;
     auto go = [&](auto kernel) {
         return launch_k(kernel, grid, GV_WARPS * 32, 0, st, a, lda, b, ldb, c, ldc, N, K);

@@ -488,6 +488,7 @@ struct n550_model {
     void *dump_ctx = nullptr;
     FusedLayer *fd_layers = nullptr;        // layer tensors for the persistent decode kernel
     int *fd_counters = nullptr;             // its attention-split arrivals [FD_MAX_TOKENS][8]
+    int *attn_counters = nullptr;           // decode attention split arrivals [max_seqs][8]
     unsigned *fd_barrier = nullptr;         // its grid-barrier counter
     // captured decode step (n550_qwen3_decode_steps)
     cudaGraphExec_t graph = nullptr;
@@ -563,7 +564,7 @@ void model_release(n550_model *m) {
     void *ptrs[] = {m->blob, m->fused_qkv, m->kc, m->vc, m->x, m->qkv, m->qf, m->logits, m->xb,
                     m->qb, m->attn, m->h, m->xl, m->tmp_a, m->tmp_b, m->tok_pos, m->tok_seq,
                     m->next, m->host_tok, m->zero_seq, m->part_m, m->part_l, m->part_o, m->rope, m->ws,
-                    m->fd_layers, m->fd_counters, m->fd_barrier};
+                    m->fd_layers, m->fd_counters, m->fd_barrier, m->attn_counters};
     for (void *p : ptrs) if (p) cudaFree(p);
     delete m;
 }
@@ -627,12 +628,14 @@ int model_setup(n550_model *m) {
     ALLOC(m->fd_layers, NLAYER * sizeof(FusedLayer));
     ALLOC(m->fd_counters, FD_MAX_TOKENS * NKVH * sizeof(int));
     ALLOC(m->fd_barrier, sizeof(unsigned));
+    ALLOC(m->attn_counters, S * NKVH * sizeof(int));
     N550_CUDA_TRY(cudaStreamCreateWithFlags(&m->cap_stream, cudaStreamNonBlocking));
     N550_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming));
     N550_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_out, cudaEventDisableTiming));
 #undef ALLOC
     N550_CUDA_TRY(cudaMemset(m->zero_seq, 0, 4));
     N550_CUDA_TRY(cudaMemset(m->fd_counters, 0, FD_MAX_TOKENS * NKVH * sizeof(int)));
+    N550_CUDA_TRY(cudaMemset(m->attn_counters, 0, S * NKVH * sizeof(int)));
     {
         FusedLayer fl[NLAYER];
         for (int l = 0; l < NLAYER; l++)
@@ -755,12 +758,13 @@ int run_attention(n550_model *m, cudaStream_t st, int T, bool decode, const int3
         a.kv_planes = c.max_seqs * NLAYER * NKVH;
         a.splits = attn_decode_splits(T, c.max_len, MAX_SPLITS);
         a.part_m = m->part_m; a.part_l = m->part_l; a.part_o = m->part_o;
+        a.counters = m->attn_counters;
         if (raw_qkv) {
             a.qkv = raw_qkv; a.qkv_ld = QKVD; a.qkv_ks = ks; a.qkv_slice = (size_t)T * QKVD;
             a.q_norm = W(m, l, 4); a.k_norm = W(m, l, 5); a.rope = m->rope;
             a.kc_w = m->kc; a.vc_w = m->vc;
         }
-        STEP(N550_PROF_ATTN, a.splits > 1 ? 2 : 1, launch_attn_decode(st, a, T));
+        STEP(N550_PROF_ATTN, 1, launch_attn_decode(st, a, T));
     } else {
         AttnPrefillArgs a{};
         a.q = m->qb; a.kc = m->kc; a.vc = m->vc; a.out = m->attn; a.seq_ids = seq_ids;
