@@ -2,6 +2,7 @@
 profilers (a few hundred MB on the device; operands larger than L2).
 
     python -m n550_qwen3_bringup_handover_b200.profile_gemm --M 16384 --N 4096 --K 1024
+    python -m n550_qwen3_bringup_handover_b200.profile_gemm --M 16 --N 2048 --K 1024 --mode exact
 """
 from __future__ import annotations
 
@@ -20,6 +21,8 @@ def main():
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--out", choices=["f32", "bf16", "resid", "swiglu"], default="f32")
     ap.add_argument("--bn", type=int, default=0, help="tile width 128/256 (0 = automatic)")
+    ap.add_argument("--mode", choices=["fast", "exact"], default="fast")
+    ap.add_argument("--kblock", type=int, default=16, help="exact mode: AME K-block")
     a = ap.parse_args()
     n5.check(n5.lib().n550_gemm_tile_config(a.bn), "n550_gemm_tile_config")
     dev = torch.device("cuda:0")
@@ -38,6 +41,8 @@ def main():
             n5.gemm_residual(A, B, C)
         elif a.out == "swiglu":
             n5.gemm_swiglu(A, B, U, out=C)
+        elif a.mode == "exact":
+            n5.gemm(A, B, mode=n5.MODE_EXACT, kblock=a.kblock, out=C)
         else:
             n5.gemm(A, B, mode=n5.MODE_FAST, out=C)
         e1.record()
@@ -46,7 +51,7 @@ def main():
     n5.check(n5.device_status(), "device status")
     ms = min(times)
     flop = 2.0 * a.M * a.N * a.K * (2 if a.out == "swiglu" else 1)
-    print(f"M={a.M} N={a.N} K={a.K} out={a.out} bn={a.bn}: {ms:.4f} ms, "
+    print(f"M={a.M} N={a.N} K={a.K} out={a.out} bn={a.bn} mode={a.mode}: {ms:.4f} ms, "
           f"{flop / ms / 1e9:.1f} TFLOP/s")
 
 
