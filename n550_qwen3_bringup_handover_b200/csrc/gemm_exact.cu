@@ -131,6 +131,48 @@ __device__ __noinline__ float exact_block(float acc, const float *a, const float
     return __double2float_rn(xround_f64(L));
 }
 
+// CH consecutive K-blocks of KB products for one output (operands a[k * SA],
+// b[k * SB]), as independent TwoSum chains: the first from the accumulator, the
+// others from zero. They are then applied in order: an error-free chain is the
+// exact block sum, so one binary64 addition to the accumulator is the rule's
+// binary64_rne(acc + block); a chain with an error goes to exact_block. The
+// independent chains hide the FP64 latency of a thread's single output.
+// Returns the K elements consumed (whole groups of CH blocks within len).
+template <int CH, int KB, int SA, int SB>
+__device__ __forceinline__ int exact_chains(float &acc, const float *a, const float *b, int len) {
+    int kb0 = 0;
+    for (; kb0 + CH * KB <= len; kb0 += CH * KB) {
+        double s[CH], e[CH];
+#pragma unroll
+        for (int q = 0; q < CH; q++) { s[q] = q == 0 ? (double)acc : 0.0; e[q] = 0.0; }
+#pragma unroll
+        for (int kk = 0; kk < KB; kk++) {
+#pragma unroll
+            for (int q = 0; q < CH; q++) {
+                const int k = kb0 + q * KB + kk;
+                const double p = __dmul_rn((double)a[k * SA], (double)b[k * SB]);      // exact
+                const double t = __dadd_rn(s[q], p);
+                const double bp = __dsub_rn(t, s[q]);
+                const double err = __dadd_rn(__dsub_rn(s[q], __dsub_rn(t, bp)), __dsub_rn(p, bp));
+                s[q] = t;
+                e[q] = __dadd_rn(e[q], fabs(err));
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < CH; q++) {
+            if (e[q] != 0.0 || !isfinite(s[q])) {
+                acc = exact_block(acc, a + (kb0 + q * KB) * SA, b + (kb0 + q * KB) * SB, SA, SB, KB);
+            } else if (q == 0) {
+                acc = (s[q] == 0.0) ? 0.0f : __double2float_rn(s[q]);
+            } else {
+                const double t = __dadd_rn((double)acc, s[q]);
+                acc = (t == 0.0) ? 0.0f : __double2float_rn(t);
+            }
+        }
+    }
+    return kb0;
+}
+
 // TM x TN outputs per CTA, RM x RN per thread (THREADS = TM/RM x TN/RN): 64 x 64
 // tiles of 4 x 4 for many rows, 16 x 16 tiles of one output per thread for
 // few rows (decode, BASELINE configs[0]'s 16 rows), so that such GEMMs spread
@@ -138,7 +180,9 @@ __device__ __noinline__ float exact_block(float acc, const float *a, const float
 // KC: K elements staged in shared memory at a time (a multiple of 32, so whole
 // K-blocks of 16 or 32); the small tiles stage 256 so that the global loads of
 // 16 K-blocks are in flight together.
-template <bool A_F32, int TM, int TN, int RM, int RN, int KC>
+// CH > 1 (one output per thread only): whole groups of CH K-blocks go through
+// exact_chains, the rest of a stage block by block.
+template <bool A_F32, int TM, int TN, int RM, int RN, int KC, int CH = 1>
 __global__ void __launch_bounds__(THREADS)
 gemm_exact_kernel(const void *__restrict__ a_ptr, int lda,
                   const uint16_t *__restrict__ b, int ldb,
@@ -183,7 +227,13 @@ gemm_exact_kernel(const void *__restrict__ a_ptr, int lda,
             Bs[kk][r] = bv;
         }
         __syncthreads();
-      for (int kb0 = 0; kb0 < clen; kb0 += kblock) {
+      int kb_done = 0;                    // K elements of this stage already applied
+      if constexpr (CH > 1) {
+        static_assert(RM == 1 && RN == 1, "chains of one output per thread");
+        kb_done = kblock == 16 ? exact_chains<CH, 16, TM, TN>(acc[0][0], &As[0][ty], &Bs[0][tx], clen)
+                               : exact_chains<CH, 32, TM, TN>(acc[0][0], &As[0][ty], &Bs[0][tx], clen);
+      }
+      for (int kb0 = kb_done; kb0 < clen; kb0 += kblock) {
         const int len = min(kblock, clen - kb0);
 
         double s[RM][RN], e[RM][RN];
@@ -255,7 +305,7 @@ int launch_gemm_exact(cudaStream_t st, const void *a, int a_type, int lda,
     if (gy > 65535 || gx > 0x7FFFFFFF) return N550_ERR_UNSUPPORTED;
     dim3 grid((unsigned)gx, (unsigned)gy);
     const bool f32 = a_type == N550_F32;
-    auto kern = few ? (f32 ? gemm_exact_kernel<true, 16, 16, 1, 1, 256> : gemm_exact_kernel<false, 16, 16, 1, 1, 256>)
+    auto kern = few ? (f32 ? gemm_exact_kernel<true, 16, 16, 1, 1, 256, 4> : gemm_exact_kernel<false, 16, 16, 1, 1, 256, 4>)
                     : (f32 ? gemm_exact_kernel<true, 64, 64, 4, 4, MAXKB> : gemm_exact_kernel<false, 64, 64, 4, 4, MAXKB>);
     N550_CUDA_TRY(launch_k(kern, grid, THREADS, 0, st, a, lda, b, ldb, c, ldc, M, N, K, kblock));
     return N550_OK;

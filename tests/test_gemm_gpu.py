@@ -80,11 +80,21 @@ def test_exact_random_shapes_vs_oracle(cuda, M, N, K, kb):
     assert np.array_equal(c, c_ref)
 
 
-def test_exact_wide_dynamic_range_fallback(cuda):
-    """Blocks whose products span > 53 bits take the integer fallback."""
-    rng = np.random.default_rng(3)
-    M, N, K = 37, 41, 96
-    v = np.sign(rng.standard_normal((M + N, K))) * np.exp2(rng.uniform(-60, 60, (M + N, K)))
+@pytest.mark.parametrize("M,sparse", [(37, False), (5, False), (5, True), (16, True)])
+def test_exact_wide_dynamic_range_fallback(cuda, M, sparse):
+    """Blocks whose products span > 53 bits take the integer fallback: every
+    block, or (sparse) only the blocks holding a rare +-2^40 outlier, so that
+    exact and fallback blocks alternate in one output. 37 rows run the 64 x 64
+    tiles, 5 and 16 rows the one-output-per-thread tiles whose consecutive
+    K-blocks are summed as independent chains."""
+    rng = np.random.default_rng(3 + M)
+    N, K = 41, 200
+    if sparse:
+        v = rng.standard_normal((M + N, K))
+        hit = rng.random((M + N, K)) < 0.01
+        v[hit] = np.sign(v[hit]) * 2.0 ** 40
+    else:
+        v = np.sign(rng.standard_normal((M + N, K))) * np.exp2(rng.uniform(-60, 60, (M + N, K)))
     bits = oracle.f32_to_bf16(v.astype(np.float32))
     A, B = bits[:M], bits[M:]
     for kb in (16, 32):

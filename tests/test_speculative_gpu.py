@@ -92,3 +92,24 @@ def test_generate_lookup_is_greedy_and_accepts_drafts(cuda, ref_spec):
             m.close()
         assert list(got24) == toks
         assert (st24["rounds"], st24["drafted"], st24["accepted"]) == (rounds, drafted, accepted)
+
+
+def test_generate_lookup_stops_at_eos(cuda):
+    """The stop tokens end generation before they are emitted, in plain and in
+    speculative generation (main_baremetal.c:650-670: an accepted draft that
+    is a stop token ends the round too): with the reference's 6th greedy token
+    as the only stop token, both return the 5 tokens before it."""
+    z = np.load(GOLDEN / "greedy_ref.npz")
+    prompt, want = z["prompt"], [int(t) for t in z["scalar_tokens"]]
+    stop = want[5]
+    if stop in want[:5]:
+        pytest.skip("the stop token occurs earlier in this run")
+    m = n5.Model(seed=0, max_seqs=1, max_len=256, max_tokens=64)
+    try:
+        plain, _ = m.generate_lookup(prompt, 64, max_draft=0, eos=(stop,))
+        spec, _ = m.generate_lookup(prompt, 64, max_draft=127, eos=(stop,))
+        capped, st = m.generate_lookup(prompt, 3, max_draft=127)
+    finally:
+        m.close()
+    assert list(plain) == want[:5] and list(spec) == want[:5]
+    assert list(capped) == want[:3] and st["rounds"] + st["accepted"] == 3
