@@ -20,6 +20,8 @@ class Model:
                  max_seqs: int = 1, max_len: int = 2048, max_tokens: int = 512,
                  gemm_mode: int = MODE_FAST, kblock: int = 16):
         self.cfg = ModelConfig(max_seqs, max_len, max_tokens, gemm_mode, kblock)
+        # held for close(): at interpreter exit the module's globals may be gone
+        self._lib = lib()
         h = C.c_void_p()
         if blob is not None:
             b = np.ascontiguousarray(blob, np.uint8)
@@ -36,7 +38,7 @@ class Model:
 
     def close(self):
         if getattr(self, "_h", None):
-            lib().n550_qwen3_free(self._h)
+            self._lib.n550_qwen3_free(self._h)
             self._h = None
 
     def __del__(self):

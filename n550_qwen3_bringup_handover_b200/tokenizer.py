@@ -18,6 +18,7 @@ class Tokenizer:
         if isinstance(blob, (str, Path)):
             blob = Path(blob).read_bytes()
         buf = np.frombuffer(blob, np.uint8)
+        self._lib = lib()          # held for close() at interpreter exit
         h = C.c_void_p()
         check(lib().n550_tok_init(C.byref(h), buf.ctypes.data_as(C.c_void_p), buf.size),
               "n550_tok_init")
@@ -25,7 +26,7 @@ class Tokenizer:
 
     def close(self):
         if getattr(self, "_h", None):
-            lib().n550_tok_free(self._h)
+            self._lib.n550_tok_free(self._h)
             self._h = None
 
     def __del__(self):
