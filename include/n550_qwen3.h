@@ -133,10 +133,11 @@ int n550_gemm(void *stream, int mode, int kblock,
  * of A held in a fixed 8 MiB array that this library places in every GPU
  * that loads it (for as long as the process lives) instead of a per-call
  * allocation. Routing: up to 8 rows the GEMV, then the weight-streaming GEMM
- * (FP32 output, up to n550_gemm_skinny_rows rows), otherwise the tile GEMM in
- * one pass -- n550_gemm's split-K route for 33-1023 rows is not taken (its
- * partial sums would need a second array), so those shapes run slower here
- * than through n550_gemm. No counterpart in the reference.
+ * (FP32 output, up to 128 rows by default, n550_gemm_skinny_rows), otherwise
+ * the tile GEMM in one pass -- n550_gemm's split-K route for BF16 output and
+ * for 129-1023 rows is not taken (its partial sums would need a second
+ * array), so those shapes run slower here than through n550_gemm. No
+ * counterpart in the reference.
  *   Limit: M * round_up(K, 8) <= 4,194,304 (e.g. 4096 x 1024, 1365 x 3072);
  *   larger calls return N550_ERR_ARG and touch nothing.
  *   The first call on each device looks up the array's device address; make
@@ -160,15 +161,16 @@ int n550_gemm_tile_config(int bn);
 /* The skinny-token GEMM of the decode step: weights as the MMA's 128-row side,
  * the M rows (tokens) as its N side, K split over a thread-block cluster whose
  * partial tiles are summed on chip, the residual / SwiGLU / q-k-v epilogues
- * fused. 0 (default): fast-mode GEMMs and decoder layers with M <= 32 rows
- * (n550_gemm_skinny_rows) take it; 1-16: every M <= 512 takes it with that
- * cluster size; -1: off
+ * fused. 0 (default): decoder layers with M <= 32 rows and FP32-output GEMMs
+ * (n550_gemm, qwen3_gemm) with M <= 128 rows (n550_gemm_skinny_rows) take it;
+ * 1-16: every M <= 512 takes it with that cluster size; -1: off
  * (such GEMMs split K into FP32 partials in global memory). A tuning knob;
  * results change only by FP32 summation order. */
 int n550_gemm_skinny_config(int cs);
 
-/* Largest M (0-512, default 32) that takes the skinny-token GEMM automatically
- * (n550_gemm_skinny_config 0). A tuning knob. */
+/* Largest M (0-512) that takes the skinny-token GEMM automatically
+ * (n550_gemm_skinny_config 0): by default 32 for decoder layers and 128 for
+ * FP32-output GEMMs; a call sets both to m. A tuning knob. */
 int n550_gemm_skinny_rows(int m);
 
 /* Programmatic dependent launch (default on): every kernel of the library is

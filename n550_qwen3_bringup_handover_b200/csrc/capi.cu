@@ -93,7 +93,7 @@ int device_gemm(cudaStream_t st, int mode, int kblock, const void *a, int a_type
     int kt;
     if (M <= 8 && launch_gemv(st, epi, abf, ldab, b, ldb, c, ldc, M, N, K) == N550_OK) {
         rc = N550_OK;
-    } else if (skinny_route(M) && epi == TC_EPI_F32 &&
+    } else if (skinny_route_gemm(M) && epi == TC_EPI_F32 &&
                tc_shape_ok(abf, ldab, b, ldb, K) &&
                (rc = skinny_f32(st, abf, ldab, b, ldb, (float *)c, ldc, M, N, K)) != N550_ERR_UNSUPPORTED) {
         // weight-streaming GEMM (rc set)
@@ -393,6 +393,7 @@ int n550_gemm_skinny_config(int cs) {
 int n550_gemm_skinny_rows(int m) {
     if (m < 0 || m > SK_MAX_T) return N550_ERR_ARG;
     g_skinny_rows = m;
+    g_skinny_rows_gemm = m;
     return N550_OK;
 }
 
@@ -486,7 +487,7 @@ int n550_gemm_f32a_noalloc(void *stream, const float *a, int lda, const uint16_t
     if (!tc_shape_ok(stage, ldab, b, ldb, K))
         return launch_gemm_simt(st, epi, stage, ldab, b, ldb, c, ldc, M, N, K);
     // the weight-streaming GEMM keeps its partial tiles on chip, as in n550_gemm
-    if (skinny_route(M) && epi == TC_EPI_F32) {
+    if (skinny_route_gemm(M) && epi == TC_EPI_F32) {
         rc = skinny_f32(st, stage, ldab, b, ldb, (float *)c, ldc, M, N, K);
         if (rc != N550_ERR_UNSUPPORTED) return rc;
     }

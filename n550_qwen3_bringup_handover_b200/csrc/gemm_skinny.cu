@@ -522,6 +522,7 @@ bool sk_plan(int tn, int epi, int tiles, int num_k, int *cs, int *kt_per, int *s
 
 int g_skinny_cs = 0;
 int g_skinny_rows = SK_AUTO_T;
+int g_skinny_rows_gemm = SK_AUTO_GEMM_T;
 
 int launch_gemm_skinny(cudaStream_t st, int epi, const uint16_t *x, int ldx, const uint16_t *w,
                        const uint16_t *w2, int ldw, int T, int N, int K, const SkEpilogue &ep, int cs) {

@@ -46,9 +46,21 @@ constexpr int SK_MAX_T = 512;
 extern int g_skinny_rows;     // n550_gemm_skinny_rows: automatic limit (default SK_AUTO_T)
 constexpr int SK_AUTO_T = 32;
 
-// Whether a fast-mode GEMM / layer of M rows takes the skinny GEMM.
+// Standalone FP32-output GEMMs (n550_gemm, qwen3_gemm) have no epilogue to
+// fuse and pay for a separate reduction kernel on the split-K path: there the
+// skinny GEMM is ahead up to 128 rows (measured on B200: the seven projection
+// GEMMs of a layer at 128 rows, graph-replayed, 55.3 vs 61.7 us per layer).
+constexpr int SK_AUTO_GEMM_T = 128;
+extern int g_skinny_rows_gemm;
+
+// Whether a fast-mode decoder layer of M rows takes the skinny GEMM.
 inline bool skinny_route(int M) {
     return g_skinny_cs == 0 ? M <= g_skinny_rows : (g_skinny_cs > 0 && M <= SK_MAX_T);
+}
+
+// Whether a standalone FP32-output GEMM of M rows takes the skinny GEMM.
+inline bool skinny_route_gemm(int M) {
+    return g_skinny_cs == 0 ? M <= g_skinny_rows_gemm : (g_skinny_cs > 0 && M <= SK_MAX_T);
 }
 
 // Y = X . W^T for T <= SK_MAX_T tokens with epilogue `epi`. X BF16 [T][K]
