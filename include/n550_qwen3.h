@@ -267,6 +267,14 @@ size_t n550_attention_decode_workspace(int n_seqs, int max_len);
  * clears it (N550_OK, or N550_ERR_TIMEOUT). Synchronises the device. */
 int n550_device_status(void);
 
+/* Health check of the failure path: one warp waits `cycles` SM clock cycles
+ * (1 .. 2e9) on an mbarrier that nothing arrives on, with the library's
+ * bounded wait; the wait gives up, records N550_ERR_TIMEOUT in the device
+ * status word and the kernel returns, leaving the context usable. Enqueued
+ * on `stream`; read the result with n550_device_status(). No counterpart in
+ * the reference. */
+int n550_check_wait_expiry(void *stream, long long cycles);
+
 /* ===========================================================================
  * 3. Model runtime (qwen3.h:203-257 re-designed for HBM): weights, KV cache
  *    and activations live on one GPU; many independent sequences share it.

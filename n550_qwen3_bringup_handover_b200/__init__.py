@@ -77,6 +77,7 @@ def lib() -> C.CDLL:
         "n550_set_pdl": (i, [i]),
         "n550_gemm_skinny_config": (i, [i]),
         "n550_gemm_skinny_rows": (i, [i]),
+        "n550_check_wait_expiry": (i, [vp, C.c_longlong]),
         "n550_gemm_swiglu": (i, [vp, vp, i, vp, vp, i, vp, i, i, i, i]),
         "n550_rope": (i, [vp, vp, i, i, i]),
         "n550_silu_mul": (i, [vp, vp, vp, sz]),

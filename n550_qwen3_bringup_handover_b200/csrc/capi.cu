@@ -223,6 +223,19 @@ uint16_t *noalloc_stage() {
     return g_noalloc_ptr[dev];
 }
 
+// One warp waits on an mbarrier that nothing arrives on, for at most `cycles`:
+// the expiry path of every bounded wait in the library (status word set to
+// N550_ERR_TIMEOUT, kernel returns).
+__global__ void wait_expiry_kernel(long long cycles) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    mbar_wait(&bar, 0, cycles);
+}
+
 }  // namespace
 }  // namespace n550
 
@@ -552,6 +565,13 @@ int n550_attention_decode(void *stream, const uint16_t *q, int ldq, const uint16
         a.part_l = a.part_m + slots;
     }
     return launch_attn_decode((cudaStream_t)stream, a, n_seqs);
+}
+
+int n550_check_wait_expiry(void *stream, long long cycles) {
+    if (cycles < 1 || cycles > kWaitCycles) return N550_ERR_ARG;
+    wait_expiry_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(cycles);
+    N550_CUDA_TRY(cudaGetLastError());
+    return N550_OK;
 }
 
 int n550_device_status(void) {

@@ -147,12 +147,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 }
 
 // Bounded wait: true when the phase completed, false (and the device status
-// set to N550_ERR_TIMEOUT) after kWaitCycles.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+// set to N550_ERR_TIMEOUT) after `limit` cycles (kWaitCycles unless a health
+// check asks for less).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, long long limit = kWaitCycles) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > kWaitCycles) { report_timeout(); return false; }
+        if (clock64() - t0 > limit) { report_timeout(); return false; }
     }
     return true;
 }

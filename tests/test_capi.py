@@ -105,6 +105,9 @@ def test_device_entry_points_reject_bad_arguments():
                               2048, None, None, 64, 0) == n5.OK
     assert L.n550_rope_table(None, None, -1) == n5.ERR_ARG
     assert L.n550_rope_table(None, None, 0) == n5.OK
+    # the failure-path health check: limits outside 1 .. 2e9 cycles launch nothing
+    assert L.n550_check_wait_expiry(None, 0) == n5.ERR_ARG
+    assert L.n550_check_wait_expiry(None, 2_000_000_001) == n5.ERR_ARG
 
 
 def test_synth_normal_matches_oracle_generator():
