@@ -114,3 +114,46 @@ def test_reference_arm_prints_on_rank_zero_only():
                         "--steps", "1"], cwd=ROOT, env=env, capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.strip() == ""
+
+
+def lost_rank_main(rank: int, world: int, port: int, q) -> None:
+    """Rank 1 leaves between steps (after joining, before the gather); rank 0's
+    gather must end with an error inside the process group's timeout."""
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    sys.path.insert(0, str(ROOT))
+    from n550_qwen3_bringup_handover_b200 import dp
+    w, r, _ = dp.init_process_group("gloo", timeout_s=10.0)
+    dp.barrier()
+    if r == 1:
+        os._exit(0)                        # the lost peer: no cleanup, no more collectives
+    t0 = time.monotonic()
+    try:
+        out = torch.empty((4, 3), dtype=torch.float32)
+        dp.gather_rows(out, torch.ones((2, 3), dtype=torch.float32))
+        q.put(json.dumps({"raised": False, "s": time.monotonic() - t0}))
+    except Exception as e:                 # gloo reports the closed peer or the timeout
+        q.put(json.dumps({"raised": True, "s": time.monotonic() - t0, "what": type(e).__name__}))
+    os._exit(0)
+
+
+def test_lost_rank_ends_the_gather_with_an_error():
+    """A rank that exits between steps is detected on the host: the surviving
+    rank's next collective raises (peer closed, or the short process-group
+    timeout) instead of waiting for good."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=lost_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        res = json.loads(q.get(timeout=120))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert res["raised"], res
+    assert res["s"] < 60.0, res
