@@ -37,6 +37,7 @@ constexpr int DC_WARPS = DC_THREADS / 32;
 constexpr int DC_TP = 64;           // positions per tile
 constexpr int DC_PPW = DC_TP / DC_WARPS;       // positions of a tile per warp (16)
 constexpr int DC_STAGES = 3;        // tiles in flight per CTA
+constexpr int DC_MIN_SPLIT = 2 * DC_TP;        // positions per split at least (in-kernel merge)
 constexpr int DC_BOX = 64 * 64 * 2;            // 64 positions x 64 dims BF16, 128-byte swizzle
 constexpr int DC_STAGE_BYTES = 4 * DC_BOX;     // K dims 0-63 | K 64-127 | V 0-63 | V 64-127
 constexpr int DC_SMEM = DC_STAGES * DC_STAGE_BYTES + 1024 + 64;
@@ -95,7 +96,16 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
     const int seq = __ldcg(p.seq_ids + s);
     const int kv_len = __ldcg(p.pos + s) + 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int chunk = (kv_len + p.splits - 1) / p.splits;
+    // Splits that hold positions: with the merge in this kernel (counters set)
+    // a context of fewer than p.splits x DC_MIN_SPLIT positions takes fewer
+    // splits than the grid has, and the other CTAs of the (sequence, KV head)
+    // return at once -- a one-sequence step at a short context then runs one
+    // CTA per KV head and merges nothing, instead of merging mostly empty
+    // splits. Every CTA of the pair computes the same count from pos[s].
+    const int eff = p.counters ? max(1, min(p.splits, (kv_len + DC_MIN_SPLIT - 1) / DC_MIN_SPLIT))
+                               : p.splits;
+    if (split >= eff) return;
+    int chunk = (kv_len + eff - 1) / eff;
     chunk = (chunk + DC_TP - 1) / DC_TP * DC_TP;
     const int start = split * chunk, end = min(kv_len, start + chunk);
     const int n_tiles = end > start ? (end - start + DC_TP - 1) / DC_TP : 0;
@@ -327,7 +337,7 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
             O += wo[w][h][d] * f;
         }
         const int head = kvh * 2 + h;
-        if (p.splits == 1) {
+        if (eff == 1) {
             p.out[(size_t)s * p.ldo + head * HD + d] = f32_to_bf16_rne(O / L);
         } else {
             const size_t slot = ((size_t)s * 16 + head) * p.splits + split;
@@ -335,7 +345,7 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
             if (d == 0) { p.part_m[slot] = M; p.part_l[slot] = L; }
         }
     }
-    if (p.splits == 1 || !p.counters) return;
+    if (eff == 1 || !p.counters) return;
     // The CTA that completes this (sequence, KV head) merges the splits of its
     // two heads, in split order (the combine kernel's arithmetic).
     __shared__ int last;
@@ -343,7 +353,7 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
     if (threadIdx.x == 0) {
         __threadfence();
         int *ctr = p.counters + s * NKV + kvh;
-        last = atomicAdd(ctr, 1) == p.splits - 1;
+        last = atomicAdd(ctr, 1) == eff - 1;
         if (last) {
             *ctr = 0;                              // ready for the next call
             __threadfence();
@@ -355,9 +365,9 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
         const int head = kvh * 2 + (i >> 7), d = i & 127;
         const size_t slot0 = ((size_t)s * 16 + head) * p.splits;
         float M = -INFINITY;
-        for (int k = 0; k < p.splits; k++) M = fmaxf(M, __ldcg(p.part_m + slot0 + k));
+        for (int k = 0; k < eff; k++) M = fmaxf(M, __ldcg(p.part_m + slot0 + k));
         float L = 0.f, O = 0.f;
-        for (int k = 0; k < p.splits; k++) {
+        for (int k = 0; k < eff; k++) {
             const float mi = __ldcg(p.part_m + slot0 + k);
             const float f = (mi == -INFINITY) ? 0.f : exp2f(mi - M);
             L += __ldcg(p.part_l + slot0 + k) * f;
