@@ -37,7 +37,6 @@ constexpr int DC_WARPS = DC_THREADS / 32;
 constexpr int DC_TP = 64;           // positions per tile
 constexpr int DC_PPW = DC_TP / DC_WARPS;       // positions of a tile per warp (16)
 constexpr int DC_STAGES = 3;        // tiles in flight per CTA
-constexpr int DC_MIN_SPLIT = 2 * DC_TP;        // positions per split at least (in-kernel merge)
 constexpr int DC_BOX = 64 * 64 * 2;            // 64 positions x 64 dims BF16, 128-byte swizzle
 constexpr int DC_STAGE_BYTES = 4 * DC_BOX;     // K dims 0-63 | K 64-127 | V 0-63 | V 64-127
 constexpr int DC_SMEM = DC_STAGES * DC_STAGE_BYTES + 1024 + 64;
@@ -97,12 +96,16 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
     const int kv_len = __ldcg(p.pos + s) + 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // Splits that hold positions: with the merge in this kernel (counters set)
-    // a context of fewer than p.splits x DC_MIN_SPLIT positions takes fewer
-    // splits than the grid has, and the other CTAs of the (sequence, KV head)
-    // return at once -- a one-sequence step at a short context then runs one
-    // CTA per KV head and merges nothing, instead of merging mostly empty
-    // splits. Every CTA of the pair computes the same count from pos[s].
-    const int eff = p.counters ? max(1, min(p.splits, (kv_len + DC_MIN_SPLIT - 1) / DC_MIN_SPLIT))
+    // a context takes floor(sqrt(kv_len / 32)) splits (1 up to 127 positions,
+    // 4 at 512, 8 at 2048, 16 at 8192; at most the grid's), and the other CTAs
+    // of the (sequence, KV head) return at once. Streaming a split costs its
+    // positions, merging costs the split count: measured on B200 (graph-
+    // replayed steps of 1-4 sequences at 64-2048 positions) this beats fixed
+    // minimum split lengths of 128, 256 and 512 positions, and a one-sequence
+    // step at a short context runs one CTA per KV head instead of merging
+    // mostly empty splits (batch-1 decode 883 -> 657 us per token). Every CTA
+    // of the pair computes the same count from pos[s].
+    const int eff = p.counters ? max(1, min(p.splits, (int)sqrtf((float)kv_len * (1.0f / 32.0f))))
                                : p.splits;
     if (split >= eff) return;
     int chunk = (kv_len + eff - 1) / eff;
