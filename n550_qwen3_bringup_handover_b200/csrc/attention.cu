@@ -140,6 +140,17 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
     int pre = 0;
     if (threadIdx.x == 0)
         while (pre < min(DC_STAGES, n_tiles) && (fused || start + (pre + 1) * DC_TP <= pos)) issue(pre++);
+    // Fused mode: the QK-norm weights and the RoPE factors of position pos[s]
+    // are no output of the kernel this one depends on either.
+    float nw[4] = {0.f, 0.f, 0.f, 0.f};
+    float2 rcs[2] = {};
+    if (fused && warp < 3) {
+        const uint16_t *w = warp < 2 ? p.q_norm : p.k_norm;
+#pragma unroll
+        for (int j = 0; j < 4; j++) nw[j] = bf16_bits_to_f32(w[lane + 32 * j]);
+#pragma unroll
+        for (int j = 0; j < 2; j++) rcs[j] = p.rope[(size_t)pos * 64 + lane + 32 * j];
+    }
     dep_wait();
     dep_launch();
     if (threadIdx.x == 0)
@@ -164,16 +175,15 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
             }
         }
         if (warp < 3) {
-            const uint16_t *w = warp < 2 ? p.q_norm : p.k_norm;
             float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
             const float sc = 1.0f / sqrtf(ss / (float)HD + kEps);
 #pragma unroll
-            for (int j = 0; j < 4; j++) v[j] = v[j] * sc * bf16_bits_to_f32(w[lane + 32 * j]);
+            for (int j = 0; j < 4; j++) v[j] = v[j] * sc * nw[j];
 #pragma unroll
             for (int j = 0; j < 2; j++) {      // rotate-half pairs (i, i + 64)
-                const float2 cs = p.rope[(size_t)pos * 64 + lane + 32 * j];
+                const float2 cs = rcs[j];
                 const float a = v[j], b = v[j + 2];
                 v[j] = a * cs.x - b * cs.y;
                 v[j + 2] = b * cs.x + a * cs.y;

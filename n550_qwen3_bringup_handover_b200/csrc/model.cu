@@ -331,6 +331,10 @@ __global__ void decode_advance_kernel(const int32_t *next, int32_t *tokens, int3
 __global__ void __launch_bounds__(256)
 resid_norm_rows_kernel(float *x, const float *__restrict__ ws, int ks, size_t slice,
                        const uint16_t *__restrict__ w, uint16_t *out) {
+    // the norm weight is no kernel's output: read before the wait
+    float wv[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) wv[j] = w ? bf16_bits_to_f32(w[threadIdx.x + 256 * j]) : 0.f;
     dep_wait();
     dep_launch();
     __shared__ float red[8];
@@ -358,20 +362,30 @@ resid_norm_rows_kernel(float *x, const float *__restrict__ ws, int ks, size_t sl
 #pragma unroll
     for (int j = 0; j < 4; j++) {
         const int c = threadIdx.x + 256 * j;
-        out[(size_t)t * H + c] = f32_to_bf16_rne(xv[j] * sc * bf16_bits_to_f32(w[c]));
+        out[(size_t)t * H + c] = f32_to_bf16_rne(xv[j] * sc * wv[j]);
     }
 }
 
 // out[t] = bf16(rmsnorm(x[t]) * w) for rows of 1024 (qwen3.c:471/527, the
 // normalised GEMM input): one warp per row, eight 16-byte loads per lane held
-// in registers, warp-shuffle sum of squares, 8-byte stores.
+// in registers, warp-shuffle sum of squares, 8-byte stores. PRE_W (the few
+// rows of a decode step, where the kernel is latency-bound): the norm weight,
+// no kernel's output, is read before the programmatic-launch wait; a
+// prefill's many rows keep the registers for loads in flight instead.
+template <bool PRE_W>
 __global__ void __launch_bounds__(256)
 norm_rows_bf16_kernel(uint16_t *__restrict__ out, const float *__restrict__ x,
                       const uint16_t *__restrict__ w, int T) {
-    dep_wait();
-    dep_launch();
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
+    const uint2 *wr = (const uint2 *)w;
+    uint2 wv[8];
+    if (PRE_W) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) wv[i] = __ldg(wr + lane + 32 * i);
+    }
+    dep_wait();
+    dep_launch();
     if (row >= T) return;
     const float4 *xr = (const float4 *)(x + (size_t)row * H);
     float4 v[8];
@@ -387,16 +401,15 @@ norm_rows_bf16_kernel(uint16_t *__restrict__ out, const float *__restrict__ x,
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
     const float sc = 1.0f / sqrtf(ss / (float)H + EPS);
-    const uint2 *wr = (const uint2 *)w;
     uint2 *orow = (uint2 *)(out + (size_t)row * H);
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-        const uint2 wv = __ldg(wr + lane + 32 * i);
+        if (!PRE_W) wv[i] = __ldg(wr + lane + 32 * i);
         uint2 o;
-        o.x = pack_bf16x2(v[i].x * sc * __uint_as_float(wv.x << 16),
-                          v[i].y * sc * __uint_as_float(wv.x & 0xFFFF0000u));
-        o.y = pack_bf16x2(v[i].z * sc * __uint_as_float(wv.y << 16),
-                          v[i].w * sc * __uint_as_float(wv.y & 0xFFFF0000u));
+        o.x = pack_bf16x2(v[i].x * sc * __uint_as_float(wv[i].x << 16),
+                          v[i].y * sc * __uint_as_float(wv[i].x & 0xFFFF0000u));
+        o.y = pack_bf16x2(v[i].z * sc * __uint_as_float(wv[i].y << 16),
+                          v[i].w * sc * __uint_as_float(wv[i].y & 0xFFFF0000u));
         orow[lane + 32 * i] = o;
     }
 }
@@ -405,12 +418,21 @@ norm_rows_bf16_kernel(uint16_t *__restrict__ out, const float *__restrict__ x,
 // needs row NT-1): xl[i] = rmsnorm(x[i*Lc + Lc - 1]) in BF16.
 __global__ void __launch_bounds__(256)
 final_norm_kernel(uint16_t *xl, const float *__restrict__ x, const uint16_t *__restrict__ w, int Lc) {
+    // the norm weight is no kernel's output: read before the wait
+    float wv[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) wv[j] = bf16_bits_to_f32(w[threadIdx.x + 256 * j]);
     dep_wait();
     dep_launch();
     __shared__ float red[8];
     const float *xr = x + ((size_t)blockIdx.x * Lc + Lc - 1) * H;
+    float xv[4];
     float ss = 0.f;
-    for (int i = threadIdx.x; i < H; i += 256) ss = fmaf(xr[i], xr[i], ss);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        xv[j] = xr[threadIdx.x + 256 * j];
+        ss = fmaf(xv[j], xv[j], ss);
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
@@ -419,8 +441,9 @@ final_norm_kernel(uint16_t *xl, const float *__restrict__ x, const uint16_t *__r
 #pragma unroll
     for (int i = 0; i < 8; i++) ss += red[i];
     const float sc = 1.0f / sqrtf(ss / (float)H + EPS);
-    for (int i = threadIdx.x; i < H; i += 256)
-        xl[(size_t)blockIdx.x * H + i] = f32_to_bf16_rne(xr[i] * sc * bf16_bits_to_f32(w[i]));
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+        xl[(size_t)blockIdx.x * H + threadIdx.x + 256 * j] = f32_to_bf16_rne(xv[j] * sc * wv[j]);
 }
 
 // h = silu(g) * u in BF16 (the unfused SwiGLU for the GEMV / exact paths).
@@ -719,7 +742,10 @@ int partials(n550_model *m, cudaStream_t st, const uint16_t *a, int lda, const u
 
 int launch_norm_rows(cudaStream_t st, uint16_t *out, const float *x, const uint16_t *w, int T) {
     if (T <= 0) return N550_OK;
-    N550_CUDA_TRY(launch_k(norm_rows_bf16_kernel, (T + 7) / 8, 256, 0, st, out, x, w, T));
+    if (T <= 64)
+        N550_CUDA_TRY(launch_k(norm_rows_bf16_kernel<true>, (T + 7) / 8, 256, 0, st, out, x, w, T));
+    else
+        N550_CUDA_TRY(launch_k(norm_rows_bf16_kernel<false>, (T + 7) / 8, 256, 0, st, out, x, w, T));
     N550_LAUNCH_CHECK();
     return N550_OK;
 }
