@@ -156,13 +156,17 @@ gemv_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict_
 // sums added in step order: 4x the warps of gemv_kernel in flight for the
 // same N, so that the few-row decode step's narrow projections (1024
 // outputs) are not held back by one 8-warp block per SM. Each warp's weights
-// are requested before the programmatic-launch wait.
+// are requested before the programmatic-launch wait; with x_ready (the
+// caller's guarantee that no kernel still in flight writes c: in the decode
+// layer the residual rows were last written two or more kernels back, which
+// completed before the previous kernel passed its own wait) so are the
+// residual rows of the RESID epilogue, through L2.
 constexpr int GVK_COLS = 4;         // output columns per block
 
 template <int MM, int EPI, int KS>
 __global__ void __launch_bounds__(GVK_COLS * KS * 32)
 gemv_ksplit_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict__ b, int ldb,
-                   void *c, int ldc, int N, int K) {
+                   void *c, int ldc, int N, int K, int x_ready) {
     __shared__ float part[GVK_COLS][KS][MM];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int col = warp / KS, kp = warp % KS;
@@ -171,6 +175,9 @@ gemv_ksplit_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__re
     const int k0 = n < N ? kp * 1024 + lane * 8 : K;
     uint4 q[4];
     gv_load_step(q, brow, k0, K);
+    const bool pre_x = EPI == TC_EPI_RESID_F32 && x_ready && kp == 0 && lane < MM && n < N;
+    float xo = 0.f;
+    if (pre_x) xo = __ldcg((const float *)c + (size_t)lane * ldc + n);
     dep_wait();
     dep_launch();
     float acc[MM];
@@ -191,7 +198,8 @@ gemv_ksplit_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__re
         float v = part[col][0][lane];
 #pragma unroll
         for (int k = 1; k < KS; k++) v += part[col][k][lane];
-        epi_store<EPI>(c, ldc, lane, n, v);
+        if (pre_x) ((float *)c)[(size_t)lane * ldc + n] = xo + v;
+        else epi_store<EPI>(c, ldc, lane, n, v);
     }
 }
 
@@ -281,13 +289,14 @@ __global__ void f32_to_bf16_kernel(uint16_t *out, int ldo, const float *in, int 
 
 template <int MM>
 int gemv_dispatch(cudaStream_t st, int epi, const uint16_t *a, int lda, const uint16_t *b,
-                  int ldb, void *c, int ldc, int N, int K) {
+                  int ldb, void *c, int ldc, int N, int K, bool x_ready) {
     // 2-4 steps of 1024 and at most 2048 columns: one warp per step
     if (K > 1024 && K <= 4096 && N <= 2048) {
         const int ks = (K + 1023) / 1024;
         const int grid = (N + GVK_COLS - 1) / GVK_COLS;
         auto go = [&](auto kernel) {
-            return launch_k(kernel, grid, GVK_COLS * ks * 32, 0, st, a, lda, b, ldb, c, ldc, N, K);
+            return launch_k(kernel, grid, GVK_COLS * ks * 32, 0, st, a, lda, b, ldb, c, ldc, N, K,
+                            x_ready ? 1 : 0);
         };
         cudaError_t e;
         if (ks == 2) {
@@ -343,20 +352,20 @@ int launch_gemm_simt(cudaStream_t st, int epi, const uint16_t *a, int lda,
 }
 
 int launch_gemv(cudaStream_t st, int epi, const uint16_t *a, int lda,
-                const uint16_t *b, int ldb, void *c, int ldc, int M, int N, int K) {
+                const uint16_t *b, int ldb, void *c, int ldc, int M, int N, int K, bool x_ready) {
     if (M <= 0 || N <= 0) return N550_OK;
     if (M > GV_MAXM || (K % 8) || (lda % 8) || (ldb % 8) || (((uintptr_t)a) & 15) ||
         (((uintptr_t)b) & 15))
         return N550_ERR_UNSUPPORTED;
     switch (M) {
-    case 1: return gemv_dispatch<1>(st, epi, a, lda, b, ldb, c, ldc, N, K);
-    case 2: return gemv_dispatch<2>(st, epi, a, lda, b, ldb, c, ldc, N, K);
-    case 3: return gemv_dispatch<3>(st, epi, a, lda, b, ldb, c, ldc, N, K);
-    case 4: return gemv_dispatch<4>(st, epi, a, lda, b, ldb, c, ldc, N, K);
-    case 5: return gemv_dispatch<5>(st, epi, a, lda, b, ldb, c, ldc, N, K);
-    case 6: return gemv_dispatch<6>(st, epi, a, lda, b, ldb, c, ldc, N, K);
-    case 7: return gemv_dispatch<7>(st, epi, a, lda, b, ldb, c, ldc, N, K);
-    default: return gemv_dispatch<8>(st, epi, a, lda, b, ldb, c, ldc, N, K);
+    case 1: return gemv_dispatch<1>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready);
+    case 2: return gemv_dispatch<2>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready);
+    case 3: return gemv_dispatch<3>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready);
+    case 4: return gemv_dispatch<4>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready);
+    case 5: return gemv_dispatch<5>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready);
+    case 6: return gemv_dispatch<6>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready);
+    case 7: return gemv_dispatch<7>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready);
+    default: return gemv_dispatch<8>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready);
     }
 }
 

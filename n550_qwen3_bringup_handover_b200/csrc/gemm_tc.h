@@ -102,9 +102,12 @@ int launch_gemm_exact(cudaStream_t st, const void *a, int a_type, int lda,
 int launch_gemm_simt(cudaStream_t st, int epi, const uint16_t *a, int lda,
                      const uint16_t *b, int ldb, void *c, int ldc, int M, int N, int K);
 
-// Skinny-M GEMV (M <= 8): streams B once with 16-byte loads.
+// Skinny-M GEMV (M <= 8): streams B once with 16-byte loads. x_ready (the
+// RESID epilogue): no kernel still in flight writes c, so the K-split GEMV
+// reads its residual rows before waiting for the previous kernel.
 int launch_gemv(cudaStream_t st, int epi, const uint16_t *a, int lda,
-                const uint16_t *b, int ldb, void *c, int ldc, int M, int N, int K);
+                const uint16_t *b, int ldb, void *c, int ldc, int M, int N, int K,
+                bool x_ready = false);
 // h[m][n] = bf16(silu(a[m] . wg[n]) * (a[m] . wu[n])) for M <= 8 rows, one launch.
 int launch_gemv_swiglu(cudaStream_t st, const uint16_t *a, int lda, const uint16_t *wg,
                        const uint16_t *wu, int ldb, uint16_t *h, int ldh, int M, int N, int K);

@@ -684,8 +684,9 @@ int check_cfg(const n550_model_config *c) {
 }
 
 // A [M,K] BF16 . W[N,K]^T with epilogue `epi` into c (ldc). SILU takes W2.
+// x_ready: see launch_gemv (the decoder layer's o and down projections).
 int mgemm(n550_model *m, cudaStream_t st, int epi, const uint16_t *a, int lda, const uint16_t *w,
-          const uint16_t *w2, void *c, int ldc, int M, int N, int K) {
+          const uint16_t *w2, void *c, int ldc, int M, int N, int K, bool x_ready = false) {
     if (m->cfg.gemm_mode == N550_MODE_EXACT) {
         if (epi == TC_EPI_F32)
             return launch_gemm_exact(st, a, N550_BF16, lda, w, K, (float *)c, ldc, M, N, K, m->cfg.kblock);
@@ -706,7 +707,7 @@ int mgemm(n550_model *m, cudaStream_t st, int epi, const uint16_t *a, int lda, c
         return N550_ERR_ARG;
     }
     if (M <= 8) {
-        if (epi != TC_EPI_SILU_BF16) return launch_gemv(st, epi, a, lda, w, K, c, ldc, M, N, K);
+        if (epi != TC_EPI_SILU_BF16) return launch_gemv(st, epi, a, lda, w, K, c, ldc, M, N, K, x_ready);
         // gate, up and SiLU . mul in one GEMV launch
         return launch_gemv_swiglu(st, a, lda, w, w2, K, (uint16_t *)c, ldc, M, N, K);
     }
@@ -930,13 +931,16 @@ int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t
         const float *raw = !fused_qkv && decode && g_fused_prep ? m->qkv : nullptr;
         if ((rc = run_attention(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, l, fused_qkv, raw, 0)))
             return rc;
+        // o and down: the residual rows x were last written two or more kernels
+        // back (the embedding or the previous residual GEMM), never by the
+        // attention or the gate/up GEMM that precede them
         STEP(N550_PROF_GEMM_O, res_kernels,
-             mgemm(m, st, TC_EPI_RESID_F32, m->attn, QD, W(m, l, 6), nullptr, m->x, H, T, H, QD));
+             mgemm(m, st, TC_EPI_RESID_F32, m->attn, QD, W(m, l, 6), nullptr, m->x, H, T, H, QD, true));
         STEP(N550_PROF_RMSNORM, 1, launch_norm_rows(st, m->xb, m->x, W(m, l, 7), T));
         STEP(N550_PROF_GEMM_GATEUP, gu_kernels,
              mgemm(m, st, TC_EPI_SILU_BF16, m->xb, H, W(m, l, 8), W(m, l, 9), m->h, INTER, T, INTER, H));
         STEP(N550_PROF_GEMM_DOWN, res_kernels,
-             mgemm(m, st, TC_EPI_RESID_F32, m->h, INTER, W(m, l, 10), nullptr, m->x, H, T, H, INTER));
+             mgemm(m, st, TC_EPI_RESID_F32, m->h, INTER, W(m, l, 10), nullptr, m->x, H, T, H, INTER, true));
     }
     return N550_OK;
 }

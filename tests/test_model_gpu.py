@@ -437,6 +437,49 @@ def test_dependent_launch_on_off_bit_identical(cuda):
         assert np.array_equal(a, b)
 
 
+@pytest.mark.parametrize("S", [1, 3])
+def test_dependent_launch_on_off_bit_identical_gemv_route(cuda, S):
+    """The few-row decode route (GEMVs, row kernels, context-sized attention
+    splits) reads constants and the residual rows before waiting for the
+    previous kernel: with programmatic dependent launch on and off the prefill
+    and decode logits and the graph-replayed ids are bit-identical, at short
+    and (one sequence at 700 positions) split-attention contexts."""
+    import torch
+    steps = 8
+    lens = [40, 700, 9][:S] if S > 1 else [700]
+    L = max(lens)
+    runs = []
+    try:
+        for on in (1, 0):
+            n5.check(n5.lib().n550_set_pdl(on))
+            m = n5.Model(seed=2, max_seqs=S, max_len=L + steps + 8, max_tokens=max(L, 64))
+            toks = oracle.synth_tokens(S * L, 61 + S, 0x544F4B).reshape(S, L)
+            seq = torch.arange(S, dtype=torch.int32, device="cuda")
+            nx = torch.empty(S, dtype=torch.int32, device="cuda")
+            out = []
+            for s in range(S):
+                t = torch.from_numpy(np.ascontiguousarray(toks[s, :lens[s]]).reshape(1, -1)).cuda()
+                m.prefill(t, seq[s:s + 1], 0, None, nx[s:s + 1])
+            tok = nx.clone()
+            pos = torch.tensor(lens, dtype=torch.int32, device="cuda")
+            for _ in range(2):
+                lg = torch.empty((S, 151936), dtype=torch.float32, device="cuda")
+                m.decode(tok, seq, pos, lg, nx)
+                out.append(lg)
+                tok = nx.clone()
+                pos = pos + 1
+            ids = torch.zeros((steps, S), dtype=torch.int32, device="cuda")
+            m.decode_steps(tok, seq, pos, steps, ids, use_graph=True)
+            torch.cuda.synchronize()
+            runs.append([x.cpu().numpy() for x in out + [ids]])
+            m.close()
+    finally:
+        n5.lib().n550_set_pdl(1)
+    assert n5.device_status() == n5.OK
+    for a, b in zip(*runs):
+        assert np.array_equal(a, b)
+
+
 @pytest.mark.parametrize("S,cfg", [(16, 0), (32, 0), (48, 4), (128, 8)])
 def test_skinny_decode_matches_split_path(cuda, S, cfg):
     """Decode steps of up to 32 sequences (up to 128 with a forced cluster
