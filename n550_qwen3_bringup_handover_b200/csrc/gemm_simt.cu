@@ -94,9 +94,81 @@ __device__ __forceinline__ void gv_load_step(uint4 (&q)[4], const uint16_t *row,
 // in steps of 4 loads per lane. The summation order does not depend on it.
 constexpr int GV_PRE = 3;           // steps of 1024 elements held in registers
 
+// Input RMSNorm fused into the GEMV (NORM; rows of K = 1024): the block
+// normalises the FP32 rows nx[m] into shared memory before its dot products,
+// rounded to BF16 -- one warp per row with the loads, sum order and
+// arithmetic of norm_rows_bf16_kernel (the model's rmsnorm, qwen3.c:471/527,
+// ops_scalar.c:11-15) -- so the products see exactly the activations that
+// kernel would write, and the few-row decode layer needs no norm launches.
+// The norm weight, no kernel's output, is copied to shared memory before the
+// programmatic-launch wait, like the weight rows.
+constexpr int GV_NORM_K = 1024;
+constexpr int GV_NORM_MAXM = 4;     // rows (the decode step's GEMV route takes up to 3)
+constexpr float GV_NORM_EPS = 1e-6f;
+
+__device__ __forceinline__ float bf16_round_f32(float v) { return bf16_bits_to_f32(f32_to_bf16_rne(v)); }
+
+__device__ __forceinline__ void gv_norm_weight(uint16_t *nws, const uint16_t *__restrict__ nw) {
+    if (threadIdx.x < GV_NORM_K / 8) ((uint4 *)nws)[threadIdx.x] = __ldg((const uint4 *)nw + threadIdx.x);
+}
+
+// Warp m < MM normalises row m (after the wait). The row is read twice, the
+// second time from L1, so that it is not held in registers beside the weight
+// rows prefetched before the wait.
 template <int MM>
+__device__ __forceinline__ void gv_norm_rows(float (*xs)[GV_NORM_K], const float *__restrict__ nx,
+                                             const uint16_t *nws) {
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();                         // nws complete
+    if (w < MM) {
+        const float4 *xr = (const float4 *)(nx + (size_t)w * GV_NORM_K);
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float4 v = __ldg(xr + lane + 32 * i);
+            ss = fmaf(v.x, v.x, ss);
+            ss = fmaf(v.y, v.y, ss);
+            ss = fmaf(v.z, v.z, ss);
+            ss = fmaf(v.w, v.w, ss);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+        const float sc = 1.0f / sqrtf(ss / (float)GV_NORM_K + GV_NORM_EPS);
+        const uint2 *wr = (const uint2 *)nws;
+        float4 *dst = (float4 *)xs[w];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float4 v = __ldg(xr + lane + 32 * i);
+            const uint2 wv = wr[lane + 32 * i];
+            float4 o;
+            o.x = bf16_round_f32(v.x * sc * __uint_as_float(wv.x << 16));
+            o.y = bf16_round_f32(v.y * sc * __uint_as_float(wv.x & 0xFFFF0000u));
+            o.z = bf16_round_f32(v.z * sc * __uint_as_float(wv.y << 16));
+            o.w = bf16_round_f32(v.w * sc * __uint_as_float(wv.y & 0xFFFF0000u));
+            dst[lane + 32 * i] = o;
+        }
+    }
+    __syncthreads();
+}
+
+// Eight activations a[m][k .. k + 8) as FP32: BF16 rows in global memory, or
+// (NORM) the block's normalised rows in shared memory.
+template <bool NORM>
+__device__ __forceinline__ void gv_a8(float (&af)[8], const uint16_t *__restrict__ a, int lda,
+                                      const float (*xs)[GV_NORM_K], int m, int k) {
+    if constexpr (NORM) {
+        const float4 lo = *(const float4 *)&xs[m][k], hi = *(const float4 *)&xs[m][k + 4];
+        af[0] = lo.x; af[1] = lo.y; af[2] = lo.z; af[3] = lo.w;
+        af[4] = hi.x; af[5] = hi.y; af[6] = hi.z; af[7] = hi.w;
+    } else {
+        bf16x8_to_f32(__ldg((const uint4 *)(a + (size_t)m * lda + k)), af);
+    }
+}
+
+template <int MM, bool NORM = false>
 __device__ __forceinline__ void gv_consume(const uint4 (&q)[4], const uint16_t *__restrict__ a, int lda,
-                                           int k0, int K, float (&acc)[MM]) {
+                                           int k0, int K, float (&acc)[MM],
+                                           const float (*xs)[GV_NORM_K] = nullptr) {
 #pragma unroll
     for (int u = 0; u < 4; u++) {
         const int k = k0 + u * 256;
@@ -105,38 +177,44 @@ __device__ __forceinline__ void gv_consume(const uint4 (&q)[4], const uint16_t *
         bf16x8_to_f32(q[u], bf);
 #pragma unroll
         for (int m = 0; m < MM; m++) {
-            const uint4 aq = __ldg((const uint4 *)(a + (size_t)m * lda + k));
             float af[8];
-            bf16x8_to_f32(aq, af);
+            gv_a8<NORM>(af, a, lda, xs, m, k);
 #pragma unroll
             for (int j = 0; j < 8; j++) acc[m] = fmaf(af[j], bf[j], acc[m]);
         }
     }
 }
 
-template <int MM, int EPI>
-__global__ void __launch_bounds__(GV_WARPS * 32)
+// NORM (K = 1024, one step): 4 blocks per SM (64 registers) hold the 512
+// blocks of the q/k/v projection in one wave.
+template <int MM, int EPI, bool NORM = false>
+__global__ void __launch_bounds__(GV_WARPS * 32, NORM ? 4 : 1)
 gemv_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict__ b, int ldb,
-            void *c, int ldc, int N, int K) {
+            void *c, int ldc, int N, int K, const float *__restrict__ nx, const uint16_t *__restrict__ nw) {
+    __shared__ __align__(16) float xs[NORM ? MM : 1][GV_NORM_K];
+    __shared__ __align__(16) uint16_t nws[NORM ? GV_NORM_K : 8];
     const int lane = threadIdx.x & 31;
     const int n = blockIdx.x * GV_WARPS + (threadIdx.x >> 5);
     const uint16_t *brow = b + (size_t)(n < N ? n : 0) * ldb;
     const int k_first = n < N ? lane * 8 : K;
-    uint4 bq[GV_PRE][4];
+    constexpr int PRE = NORM ? 1 : GV_PRE;
+    uint4 bq[PRE][4];
 #pragma unroll
-    for (int s = 0; s < GV_PRE; s++) gv_load_step(bq[s], brow, k_first + s * 1024, K);
+    for (int s = 0; s < PRE; s++) gv_load_step(bq[s], brow, k_first + s * 1024, K);
+    if constexpr (NORM) gv_norm_weight(nws, nw);
     dep_wait();
     dep_launch();
+    if constexpr (NORM) gv_norm_rows<MM>(xs, nx, nws);
     if (n >= N) return;
     float acc[MM];
 #pragma unroll
     for (int m = 0; m < MM; m++) acc[m] = 0.f;
 #pragma unroll
-    for (int s = 0; s < GV_PRE; s++) gv_consume<MM>(bq[s], a, lda, lane * 8 + s * 1024, K, acc);
-    for (int k0 = lane * 8 + GV_PRE * 1024; k0 < K; k0 += 1024) {
+    for (int s = 0; s < PRE; s++) gv_consume<MM, NORM>(bq[s], a, lda, lane * 8 + s * 1024, K, acc, xs);
+    for (int k0 = lane * 8 + PRE * 1024; k0 < K; k0 += 1024) {
         uint4 q[4];
         gv_load_step(q, brow, k0, K);
-        gv_consume<MM>(q, a, lda, k0, K, acc);
+        gv_consume<MM, NORM>(q, a, lda, k0, K, acc, xs);
     }
 #pragma unroll
     for (int m = 0; m < MM; m++) {
@@ -207,10 +285,15 @@ gemv_ksplit_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__re
 // as BF16, ops_scalar.c:46-51): the SwiGLU of the few-token decode step in one
 // launch instead of two GEMVs and an elementwise kernel. Same per-row loop and
 // reduction order as gemv_kernel, so g and u are the values those GEMVs give.
-template <int MM>
-__global__ void __launch_bounds__(GV_WARPS * 32)
+// NORM: 3 blocks per SM (85 registers) hold the 384 blocks of the model's
+// gate/up projection in one wave.
+template <int MM, bool NORM = false>
+__global__ void __launch_bounds__(GV_WARPS * 32, NORM ? 3 : 1)
 gemv_swiglu_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict__ wg,
-                   const uint16_t *__restrict__ wu, int ldb, uint16_t *h, int ldh, int N, int K) {
+                   const uint16_t *__restrict__ wu, int ldb, uint16_t *h, int ldh, int N, int K,
+                   const float *__restrict__ nx, const uint16_t *__restrict__ nw) {
+    __shared__ __align__(16) float xs[NORM ? MM : 1][GV_NORM_K];
+    __shared__ __align__(16) uint16_t nws[NORM ? GV_NORM_K : 8];
     const int lane = threadIdx.x & 31;
     const int n = blockIdx.x * GV_WARPS + (threadIdx.x >> 5);
     const size_t row = (size_t)(n < N ? n : 0) * ldb;
@@ -219,8 +302,10 @@ gemv_swiglu_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__re
     uint4 gq[4], uq[4];
     gv_load_step(gq, grow, n < N ? lane * 8 : K, K);
     gv_load_step(uq, urow, n < N ? lane * 8 : K, K);
+    if constexpr (NORM) gv_norm_weight(nws, nw);
     dep_wait();
     dep_launch();
+    if constexpr (NORM) gv_norm_rows<MM>(xs, nx, nws);
     if (n >= N) return;
     float ag[MM], au[MM];
 #pragma unroll
@@ -239,9 +324,8 @@ gemv_swiglu_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__re
             bf16x8_to_f32(uq[u], uf);
 #pragma unroll
             for (int m = 0; m < MM; m++) {
-                const uint4 aq = __ldg((const uint4 *)(a + (size_t)m * lda + k));
                 float af[8];
-                bf16x8_to_f32(aq, af);
+                gv_a8<NORM>(af, a, lda, xs, m, k);
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
                     ag[m] = fmaf(af[j], gf[j], ag[m]);
@@ -269,9 +353,18 @@ gemv_swiglu_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__re
 
 template <int MM>
 int gemv_swiglu_dispatch(cudaStream_t st, const uint16_t *a, int lda, const uint16_t *wg,
-                         const uint16_t *wu, int ldb, uint16_t *h, int ldh, int N, int K) {
-    N550_CUDA_TRY(launch_k(gemv_swiglu_kernel<MM>, (N + GV_WARPS - 1) / GV_WARPS, GV_WARPS * 32, 0, st,
-                           a, lda, wg, wu, ldb, h, ldh, N, K));
+                         const uint16_t *wu, int ldb, uint16_t *h, int ldh, int N, int K,
+                         const float *nx, const uint16_t *nw) {
+    const int grid = (N + GV_WARPS - 1) / GV_WARPS;
+    if (nx) {
+        if constexpr (MM <= GV_NORM_MAXM)
+            N550_CUDA_TRY(launch_k(gemv_swiglu_kernel<MM, true>, grid, GV_WARPS * 32, 0, st, a, lda, wg, wu,
+                                   ldb, h, ldh, N, K, nx, nw));
+        else
+            return N550_ERR_UNSUPPORTED;
+    } else
+        N550_CUDA_TRY(launch_k(gemv_swiglu_kernel<MM, false>, grid, GV_WARPS * 32, 0, st, a, lda, wg, wu, ldb,
+                               h, ldh, N, K, nx, nw));
     return N550_OK;
 }
 
@@ -289,7 +382,18 @@ __global__ void f32_to_bf16_kernel(uint16_t *out, int ldo, const float *in, int 
 
 template <int MM>
 int gemv_dispatch(cudaStream_t st, int epi, const uint16_t *a, int lda, const uint16_t *b,
-                  int ldb, void *c, int ldc, int N, int K, bool x_ready) {
+                  int ldb, void *c, int ldc, int N, int K, bool x_ready, const float *nx,
+                  const uint16_t *nw) {
+    if (nx) {               // fused input norm: K = 1024, FP32 output, up to 4 rows
+        if constexpr (MM <= GV_NORM_MAXM) {
+            if (epi != TC_EPI_F32) return N550_ERR_UNSUPPORTED;
+            N550_CUDA_TRY(launch_k(gemv_kernel<MM, TC_EPI_F32, true>, (N + GV_WARPS - 1) / GV_WARPS,
+                                   GV_WARPS * 32, 0, st, a, lda, b, ldb, c, ldc, N, K, nx, nw));
+            return N550_OK;
+        } else {
+            return N550_ERR_UNSUPPORTED;
+        }
+    }
     // 2-4 steps of 1024 and at most 2048 columns: one warp per step
     if (K > 1024 && K <= 4096 && N <= 2048) {
         const int ks = (K + 1023) / 1024;
@@ -320,7 +424,8 @@ int gemv_dispatch(cudaStream_t st, int epi, const uint16_t *a, int lda, const ui
     }
     const int grid = (N + GV_WARPS - 1) / GV_WARPS;
     auto go = [&](auto kernel) {
-        return launch_k(kernel, grid, GV_WARPS * 32, 0, st, a, lda, b, ldb, c, ldc, N, K);
+        return launch_k(kernel, grid, GV_WARPS * 32, 0, st, a, lda, b, ldb, c, ldc, N, K,
+                        (const float *)nullptr, (const uint16_t *)nullptr);
     };
     cudaError_t e;
     if (epi == TC_EPI_F32) e = go(gemv_kernel<MM, TC_EPI_F32>);
@@ -351,39 +456,46 @@ int launch_gemm_simt(cudaStream_t st, int epi, const uint16_t *a, int lda,
     return N550_OK;
 }
 
+// The fused input norm's requirements: rows of K = 1024, 16-byte aligned
+// rows and norm weight.
+bool gv_norm_ok(int K, const float *nx, const uint16_t *nw) {
+    return K == GV_NORM_K && nw && !(((uintptr_t)nx) & 15) && !(((uintptr_t)nw) & 15);
+}
+
 int launch_gemv(cudaStream_t st, int epi, const uint16_t *a, int lda,
-                const uint16_t *b, int ldb, void *c, int ldc, int M, int N, int K, bool x_ready) {
+                const uint16_t *b, int ldb, void *c, int ldc, int M, int N, int K, bool x_ready,
+                const float *nx, const uint16_t *nw) {
     if (M <= 0 || N <= 0) return N550_OK;
-    if (M > GV_MAXM || (K % 8) || (lda % 8) || (ldb % 8) || (((uintptr_t)a) & 15) ||
-        (((uintptr_t)b) & 15))
-        return N550_ERR_UNSUPPORTED;
+    if (M > GV_MAXM || (K % 8) || (ldb % 8) || (((uintptr_t)b) & 15)) return N550_ERR_UNSUPPORTED;
+    if (nx ? !gv_norm_ok(K, nx, nw) : ((lda % 8) || (((uintptr_t)a) & 15))) return N550_ERR_UNSUPPORTED;
     switch (M) {
-    case 1: return gemv_dispatch<1>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready);
-    case 2: return gemv_dispatch<2>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready);
-    case 3: return gemv_dispatch<3>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready);
-    case 4: return gemv_dispatch<4>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready);
-    case 5: return gemv_dispatch<5>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready);
-    case 6: return gemv_dispatch<6>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready);
-    case 7: return gemv_dispatch<7>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready);
-    default: return gemv_dispatch<8>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready);
+    case 1: return gemv_dispatch<1>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready, nx, nw);
+    case 2: return gemv_dispatch<2>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready, nx, nw);
+    case 3: return gemv_dispatch<3>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready, nx, nw);
+    case 4: return gemv_dispatch<4>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready, nx, nw);
+    case 5: return gemv_dispatch<5>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready, nx, nw);
+    case 6: return gemv_dispatch<6>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready, nx, nw);
+    case 7: return gemv_dispatch<7>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready, nx, nw);
+    default: return gemv_dispatch<8>(st, epi, a, lda, b, ldb, c, ldc, N, K, x_ready, nx, nw);
     }
 }
 
 int launch_gemv_swiglu(cudaStream_t st, const uint16_t *a, int lda, const uint16_t *wg,
-                       const uint16_t *wu, int ldb, uint16_t *h, int ldh, int M, int N, int K) {
+                       const uint16_t *wu, int ldb, uint16_t *h, int ldh, int M, int N, int K,
+                       const float *nx, const uint16_t *nw) {
     if (M <= 0 || N <= 0) return N550_OK;
-    if (M > GV_MAXM || (K % 8) || (lda % 8) || (ldb % 8) || (((uintptr_t)a) & 15) ||
-        (((uintptr_t)wg) & 15) || (((uintptr_t)wu) & 15) || !h)
+    if (M > GV_MAXM || (K % 8) || (ldb % 8) || (((uintptr_t)wg) & 15) || (((uintptr_t)wu) & 15) || !h)
         return N550_ERR_UNSUPPORTED;
+    if (nx ? !gv_norm_ok(K, nx, nw) : ((lda % 8) || (((uintptr_t)a) & 15))) return N550_ERR_UNSUPPORTED;
     switch (M) {
-    case 1: return gemv_swiglu_dispatch<1>(st, a, lda, wg, wu, ldb, h, ldh, N, K);
-    case 2: return gemv_swiglu_dispatch<2>(st, a, lda, wg, wu, ldb, h, ldh, N, K);
-    case 3: return gemv_swiglu_dispatch<3>(st, a, lda, wg, wu, ldb, h, ldh, N, K);
-    case 4: return gemv_swiglu_dispatch<4>(st, a, lda, wg, wu, ldb, h, ldh, N, K);
-    case 5: return gemv_swiglu_dispatch<5>(st, a, lda, wg, wu, ldb, h, ldh, N, K);
-    case 6: return gemv_swiglu_dispatch<6>(st, a, lda, wg, wu, ldb, h, ldh, N, K);
-    case 7: return gemv_swiglu_dispatch<7>(st, a, lda, wg, wu, ldb, h, ldh, N, K);
-    default: return gemv_swiglu_dispatch<8>(st, a, lda, wg, wu, ldb, h, ldh, N, K);
+    case 1: return gemv_swiglu_dispatch<1>(st, a, lda, wg, wu, ldb, h, ldh, N, K, nx, nw);
+    case 2: return gemv_swiglu_dispatch<2>(st, a, lda, wg, wu, ldb, h, ldh, N, K, nx, nw);
+    case 3: return gemv_swiglu_dispatch<3>(st, a, lda, wg, wu, ldb, h, ldh, N, K, nx, nw);
+    case 4: return gemv_swiglu_dispatch<4>(st, a, lda, wg, wu, ldb, h, ldh, N, K, nx, nw);
+    case 5: return gemv_swiglu_dispatch<5>(st, a, lda, wg, wu, ldb, h, ldh, N, K, nx, nw);
+    case 6: return gemv_swiglu_dispatch<6>(st, a, lda, wg, wu, ldb, h, ldh, N, K, nx, nw);
+    case 7: return gemv_swiglu_dispatch<7>(st, a, lda, wg, wu, ldb, h, ldh, N, K, nx, nw);
+    default: return gemv_swiglu_dispatch<8>(st, a, lda, wg, wu, ldb, h, ldh, N, K, nx, nw);
     }
 }
 

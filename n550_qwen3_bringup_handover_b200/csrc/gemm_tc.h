@@ -104,13 +104,18 @@ int launch_gemm_simt(cudaStream_t st, int epi, const uint16_t *a, int lda,
 
 // Skinny-M GEMV (M <= 8): streams B once with 16-byte loads. x_ready (the
 // RESID epilogue): no kernel still in flight writes c, so the K-split GEMV
-// reads its residual rows before waiting for the previous kernel.
+// reads its residual rows before waiting for the previous kernel. nx != NULL
+// (K = 1024, FP32 output): the A rows are bf16(rmsnorm(nx[m]) * nw), computed
+// in the kernel exactly as the model's norm kernel computes them; a / lda are
+// unused.
 int launch_gemv(cudaStream_t st, int epi, const uint16_t *a, int lda,
                 const uint16_t *b, int ldb, void *c, int ldc, int M, int N, int K,
-                bool x_ready = false);
-// h[m][n] = bf16(silu(a[m] . wg[n]) * (a[m] . wu[n])) for M <= 8 rows, one launch.
+                bool x_ready = false, const float *nx = nullptr, const uint16_t *nw = nullptr);
+// h[m][n] = bf16(silu(a[m] . wg[n]) * (a[m] . wu[n])) for M <= 8 rows, one
+// launch; nx / nw as in launch_gemv.
 int launch_gemv_swiglu(cudaStream_t st, const uint16_t *a, int lda, const uint16_t *wg,
-                       const uint16_t *wu, int ldb, uint16_t *h, int ldh, int M, int N, int K);
+                       const uint16_t *wu, int ldb, uint16_t *h, int ldh, int M, int N, int K,
+                       const float *nx = nullptr, const uint16_t *nw = nullptr);
 
 // FP32 -> BF16 RNE staging copy of a row-major [rows, cols] matrix.
 int launch_f32_to_bf16(cudaStream_t st, uint16_t *out, int ldo, const float *in, int ldi,

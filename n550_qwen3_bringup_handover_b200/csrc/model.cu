@@ -906,11 +906,20 @@ int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t
     if (!exact && T > 8 && T < g_split_rows)
         return run_layers_split(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, xl_ready);
     const bool fused_qkv = !exact && T >= g_split_rows;
+    // the GEMV route of up to 4 rows normalises its input rows inside the q/k/v
+    // and gate/up GEMVs (no norm launches)
+    const bool gv_norm = !exact && T <= 4;
     const int gu_kernels = exact ? 3 : 1;
     const int res_kernels = exact ? 2 : 1;
     for (int l = 0; l < NLAYER; l++) {
-        STEP(N550_PROF_RMSNORM, 1, launch_norm_rows(st, m->xb, m->x, W(m, l, 0), T));
-        if (fused_qkv) {
+        if (!gv_norm) STEP(N550_PROF_RMSNORM, 1, launch_norm_rows(st, m->xb, m->x, W(m, l, 0), T));
+        if (gv_norm) {
+            STEP(N550_PROF_GEMM_QKV, 1,
+                 launch_gemv(st, TC_EPI_F32, nullptr, 0, m->wqkv[l], H, m->qkv, QKVD, T, QKVD, H, false, m->x,
+                             W(m, l, 0)));
+            if (!(decode && g_fused_prep))
+                STEP(N550_PROF_QKNORM_ROPE, 1, launch_qknorm_rope_kv(m, st, T, l, decode));
+        } else if (fused_qkv) {
             // One tcgen05 GEMM with QK-norm, RoPE and the K/V cache write in its epilogue.
             TcQkv q{};
             q.q_bf16 = m->qb;
@@ -936,9 +945,15 @@ int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t
         // attention or the gate/up GEMM that precede them
         STEP(N550_PROF_GEMM_O, res_kernels,
              mgemm(m, st, TC_EPI_RESID_F32, m->attn, QD, W(m, l, 6), nullptr, m->x, H, T, H, QD, true));
-        STEP(N550_PROF_RMSNORM, 1, launch_norm_rows(st, m->xb, m->x, W(m, l, 7), T));
-        STEP(N550_PROF_GEMM_GATEUP, gu_kernels,
-             mgemm(m, st, TC_EPI_SILU_BF16, m->xb, H, W(m, l, 8), W(m, l, 9), m->h, INTER, T, INTER, H));
+        if (gv_norm) {
+            STEP(N550_PROF_GEMM_GATEUP, 1,
+                 launch_gemv_swiglu(st, nullptr, 0, W(m, l, 8), W(m, l, 9), H, m->h, INTER, T, INTER, H, m->x,
+                                    W(m, l, 7)));
+        } else {
+            STEP(N550_PROF_RMSNORM, 1, launch_norm_rows(st, m->xb, m->x, W(m, l, 7), T));
+            STEP(N550_PROF_GEMM_GATEUP, gu_kernels,
+                 mgemm(m, st, TC_EPI_SILU_BF16, m->xb, H, W(m, l, 8), W(m, l, 9), m->h, INTER, T, INTER, H));
+        }
         STEP(N550_PROF_GEMM_DOWN, res_kernels,
              mgemm(m, st, TC_EPI_RESID_F32, m->h, INTER, W(m, l, 10), nullptr, m->x, H, T, H, INTER, true));
     }
