@@ -152,7 +152,21 @@ argmax_kernel(const float *__restrict__ v, int n, int ld, int32_t *idx) {
     const float *r = v + (size_t)blockIdx.x * ld;
     float bv = -INFINITY;
     int bi = 0x7FFFFFFF;
-    for (int i = threadIdx.x; i < n; i += AM_THREADS) argmax_merge(bv, bi, r[i], i);
+    // 8 independent loads per thread in flight, merged in increasing index
+    // order: the one-block row scan is bound by load latency, not bandwidth
+    for (int i0 = threadIdx.x; i0 < n; i0 += 8 * AM_THREADS) {
+        float x[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i = i0 + u * AM_THREADS;
+            x[u] = i < n ? r[i] : -INFINITY;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i = i0 + u * AM_THREADS;
+            if (i < n) argmax_merge(bv, bi, x[u], i);
+        }
+    }
     warp_argmax(bv, bi);
     if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
     __syncthreads();
