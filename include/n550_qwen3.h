@@ -161,8 +161,9 @@ int n550_gemm_tile_config(int bn);
 /* The skinny-token GEMM of the decode step: weights as the MMA's 128-row side,
  * the M rows (tokens) as its N side, K split over a thread-block cluster whose
  * partial tiles are summed on chip, the residual / SwiGLU / q-k-v epilogues
- * fused. 0 (default): decoder layers with M <= 32 rows and FP32-output GEMMs
- * (n550_gemm, qwen3_gemm) with M <= 128 rows (n550_gemm_skinny_rows) take it;
+ * fused. 0 (default): decoder layers with 9 <= M <= 32 rows (up to 8 take the
+ * GEMVs) and FP32-output GEMMs (n550_gemm, qwen3_gemm) with M <= 128 rows
+ * (n550_gemm_skinny_rows) take it;
  * 1-16: every M <= 512 takes it with that cluster size; -1: off
  * (such GEMMs split K into FP32 partials in global memory). A tuning knob;
  * results change only by FP32 summation order. */

@@ -896,12 +896,13 @@ int run_layers(n550_model *m, cudaStream_t st, int T, bool decode, const int32_t
         *xl_ready = true;
         return N550_OK;
     }
-    // From 4 tokens on the skinny GEMMs (7 kernels per layer) beat the GEMV
-    // path (10); below, the GEMV's shorter launches win. Measured on B200,
-    // graph-replayed decode steps with the lm_head routed alike: 1, 2, 4, 8
-    // sequences 886 / 986 / 1132 / 1563 us (GEMV) vs 1065 / 1081 / 1082 /
-    // 1189 us (skinny) per step.
-    if (!exact && T >= 4 && skinny_route(T))
+    // Up to 8 tokens the GEMV path (5 kernels per layer up to 4 tokens, 7
+    // from 5: the norms then run as their own kernels) is ahead of the skinny
+    // GEMMs (7 kernels with their cluster exchanges). Measured on B200,
+    // graph-replayed decode steps at a 1024-token context: 2, 3, 4, 6, 8
+    // sequences 836 / 935 / 1029 / 1130 / 1424 us (GEMV) vs 839 / 932 / 1235 /
+    // 1263 / 1445 us (skinny) per step.
+    if (!exact && T > 8 && skinny_route(T))
         return run_layers_skinny(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, xl_ready);
     if (!exact && T > 8 && T < g_split_rows)
         return run_layers_split(m, st, T, decode, seq_ids, pos, Sc, Lc, p0, xl_ready);
