@@ -834,8 +834,8 @@ int run_layers_split(n550_model *m, cudaStream_t st, int T, bool decode, const i
     return N550_OK;
 }
 
-// Token counts that skinny_route() gives to the weight-streaming GEMM (the
-// decode step of up to 32 sequences by default): every projection is one GEMM
+// Token counts above 8 that skinny_route() gives to the weight-streaming GEMM
+// (the decode step of 9-32 sequences by default): every projection is one GEMM
 // whose epilogue finishes the op -- QKV with QK-norm, RoPE and the K/V write;
 // o and down with the residual add; gate/up with SwiGLU -- so a layer is 4
 // GEMMs, attention and 2 RMSNorms.
@@ -1501,8 +1501,8 @@ int n550_rope_table(void *stream, float *table, int max_len) {
 
 // The decoder layer's q/k/v step on the route the runtime takes for M rows
 // (run_layers): tile GEMM with the fused epilogue from 1024 rows (BF16
-// queries), the weight-streaming GEMM with the fused epilogue where
-// skinny_route(M), else FP32 q/k/v rows (GEMV up to 8 rows, split-K partials
+// queries), the weight-streaming GEMM with the fused epilogue for 9 rows on
+// where skinny_route(M), else FP32 q/k/v rows (GEMV up to 8 rows, split-K partials
 // otherwise, in a stream-ordered workspace) finished by qknorm_rope_kv_kernel.
 int n550_qkv_rope_kv(void *stream, const uint16_t *x, int ldx, const uint16_t *wqkv,
                      const uint16_t *q_norm, const uint16_t *k_norm, const float *rope_table,
@@ -1528,7 +1528,7 @@ int n550_qkv_rope_kv(void *stream, const uint16_t *x, int ldx, const uint16_t *w
         q.q_norm = q_norm; q.k_norm = k_norm; q.rope = rope; q.eps = EPS;
         return launch_gemm_tc_qkv(st, x, ldx, wqkv, q, M, H, 0);
     }
-    if (M >= 4 && skinny_route(M) && tc_shape_ok(x, ldx, wqkv, H, H)) {
+    if (M > 8 && skinny_route(M) && tc_shape_ok(x, ldx, wqkv, H, H)) {
         SkEpilogue q{};
         q.q_f32 = qf; q.q_bf16 = qb; q.ldq = ldq;
         q.kc = k_cache; q.vc = v_cache; q.layer = layer; q.max_len = max_len;

@@ -2,7 +2,7 @@
 the K/V write, qwen3.c:287-292 and 498-511, inside the attention kernel;
 n550_qwen3_fused_attention_prep, default on) against the separate row kernel it
 replaces: bit-identical logits, ids and KV-cache effects (a second decode step
-reads the K/V the first one wrote) on the GEMV route (1-3 sequences, with
+reads the K/V the first one wrote) on the GEMV route (1-8 sequences, with
 split-KV at long contexts), the split-K route (33-1023 sequences), in eager
 steps and in the CUDA-graph loop."""
 import numpy as np

@@ -1,8 +1,8 @@
 """Tensor-level parity of the fused q/k/v step of a decoder layer
 (n550_qkv_rope_kv): qkv = x . [Wq;Wk;Wv]^T, per-head QK-norm (qwen3.c:287-292),
 RoPE at each row's position (ops_scalar.c:21-35) and the BF16 K/V cache write
-(qwen3.c:498-511), on every route the runtime takes -- the GEMV (1-3 rows),
-the weight-streaming GEMM (4-32 rows), split-K partials with the row kernel
+(qwen3.c:498-511), on every route the runtime takes -- the GEMV (1-8 rows),
+the weight-streaming GEMM (9-32 rows), split-K partials with the row kernel
 (33-1023 rows) and the tcgen05 tile GEMM with the fused epilogue (1024 rows
 on; single-CTA 128- and 256-wide tiles and 256 x 256 CTA-pair tiles) -- at
 positions up to 2047.
@@ -68,7 +68,7 @@ def bf16_close(got_bits, ref):
 
 
 @pytest.mark.parametrize("M,q_type,tile", [
-    (2, "f32", 0), (3, "bf16", 0),              # GEMV + row kernel
+    (2, "f32", 0), (3, "bf16", 0), (7, "f32", 0),   # GEMV + row kernel
     (16, "f32", 0), (32, "bf16", 0),            # weight-streaming GEMM, fused epilogue
     (100, "bf16", 0), (256, "f32", 0),          # split-K partials + row kernel
     (2048, "bf16", 128),                        # tile GEMM, 128-wide single-CTA tiles
