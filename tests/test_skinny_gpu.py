@@ -45,15 +45,17 @@ def skinny_cs():
 @pytest.mark.parametrize("M", [9, 16, 17, 32, 33, 64, 100, 128])
 @pytest.mark.parametrize("N,K", SHAPES)
 def test_skinny_gemm_f32(skinny_cs, M, N, K):
-    """M <= 32 takes the skinny GEMM by default; larger M (up to 128, 64- and
-    128-column token tiles) with a forced cluster size."""
-    if M > 32:
-        skinny_cs(4)
+    """FP32-output GEMMs of 9-128 rows take the skinny GEMM by default (from 33
+    rows in 64- and 128-column token tiles); above 32 rows also with the
+    cluster size forced to 4."""
     a, b = operands(M, N, K, 100 + M + N + K)
-    c = n5.gemm(a, b)
-    torch.cuda.synchronize()
-    assert n5.device_status() == n5.OK
-    close_f32(c, a.float() @ b.float().T)
+    ref = a.float() @ b.float().T
+    for cs in ((0, 4) if M > 32 else (0,)):
+        skinny_cs(cs)
+        c = n5.gemm(a, b)
+        torch.cuda.synchronize()
+        assert n5.device_status() == n5.OK
+        close_f32(c, ref)
 
 
 @pytest.mark.parametrize("cs,K", [(1, 512), (2, 1024), (3, 1024), (5, 576), (8, 3072), (16, 3072)])
