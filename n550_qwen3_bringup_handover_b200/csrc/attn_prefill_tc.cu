@@ -10,7 +10,11 @@
 //   warp 0      TMA producer: Q of both heads per item, then K and V blocks
 //               into a 2-stage ring (128-byte swizzle; V is consumed as the
 //               MN-major B operand).
-//   warp 1      allocates TMEM (512 columns); one thread issues the MMAs:
+//   warp 1      allocates TMEM (512 columns) and issues the MMAs: the whole
+//               warp walks the issue loop and one elected lane (elect.sync)
+//               executes each tcgen05.mma, which keeps addresses and
+//               descriptors warp-uniform (measured: 8 MMAs issued in ~460-700
+//               cycles instead of ~740-850 from a lone lane-0 thread):
 //               S_h = Q_h K^T (A and B in shared memory) and O_h += P_h V
 //               (A = P read from TMEM, B = V from shared memory), in the order
 //               S0 S1 | PV0(j) S0(j+1) PV1(j) S1(j+1) | ... so the tensor core
@@ -215,7 +219,9 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
-        if (lane == 0) {
+        // The whole warp walks the loop and waits; one elected lane issues
+        // each MMA and commit, so addresses and descriptors stay warp-uniform.
+        {
             constexpr uint32_t id_s = umma_idesc_bf16(128, 128);
             constexpr uint32_t id_o = umma_idesc_bf16(128, 128) | (1u << 16);   // V MN-major
             const uint32_t aQ = smem_u32(sQ), aKV = smem_u32(sKV);
@@ -225,10 +231,12 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
 #pragma unroll
                 for (int kk = 0; kk < 8; kk++) {
                     const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
-                    umma_bf16(tmem + t * 128, umma_desc_sw128(q + off), umma_desc_sw128(k + off),
-                              id_s, kk > 0 ? 1u : 0u);
+                    if (elect_one_sync())
+                        umma_bf16(tmem + t * 128, umma_desc_sw128(q + off), umma_desc_sw128(k + off),
+                                  id_s, kk > 0 ? 1u : 0u);
                 }
-                umma_commit(&s_full[t]);
+                if (elect_one_sync()) umma_commit(&s_full[t]);
+                __syncwarp();
             };
             int kv_iter = 0, item_i = 0, bj = 0;
             bool ok = true;
@@ -236,47 +244,52 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                 const Item it = decode_item(p, k);
                 // S columns are free: the previous item's P.V MMAs, which read
                 // P there, were issued earlier and execute in order.
-                if (!(ok = mbar_wait(q_full, item_i & 1) && mbar_wait(&k_full[kv_iter & 1],
-                                                                        (kv_iter >> 1) & 1)))
+                if (!(ok = warp_wait(q_full, item_i & 1) && warp_wait(&k_full[kv_iter & 1], (kv_iter >> 1) & 1)))
                     break;
                 tc_fence_after();
                 issue_s(0, kv_iter & 1);
                 issue_s(1, kv_iter & 1);
-                if (it.nblk == 1) umma_commit(q_empty);
+                if (it.nblk == 1 && elect_one_sync()) umma_commit(q_empty);
+                __syncwarp();
                 for (int j = 0; j < it.nblk && ok; j++, bj++) {
                     const int st = (kv_iter + j) & 1;
                     const uint32_t v = aKV + st * 2 * TILE_BYTES + TILE_BYTES;
                     for (int t = 0; t < 2; t++) {
-                        if (!(ok = mbar_wait(&p_full[t], bj & 1))) break;
-                        if (t == 0 && !(ok = mbar_wait(&v_full[st], ((kv_iter + j) >> 1) & 1))) break;
+                        if (!(ok = warp_wait(&p_full[t], bj & 1))) break;
+                        if (t == 0 && !(ok = warp_wait(&v_full[st], ((kv_iter + j) >> 1) & 1))) break;
                         // the first P.V of an item overwrites O: the previous
                         // item's output must have been read out of TMEM
-                        if (j == 0 && !(ok = mbar_wait(&o_free[t], (item_i & 1) ^ 1))) break;
+                        if (j == 0 && !(ok = warp_wait(&o_free[t], (item_i & 1) ^ 1))) break;
                         tc_fence_after();
                         // O_t += P_t . V over the 128 keys of the block (8 x K=16):
                         // P columns 8 kk .. 8 kk + 7, V rows 16 kk .. 16 kk + 15.
 #pragma unroll
                         for (int kk = 0; kk < 8; kk++)
-                            umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
-                                         umma_desc_sw128_mn(v + kk * 2048, HALF_BYTES), id_o,
-                                         (j > 0 || kk > 0) ? 1u : 0u);
-                        if (t == 1) umma_commit(&kv_empty[st]);
+                            if (elect_one_sync())
+                                umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                                             umma_desc_sw128_mn(v + kk * 2048, HALF_BYTES), id_o,
+                                             (j > 0 || kk > 0) ? 1u : 0u);
+                        if (t == 1 && elect_one_sync()) umma_commit(&kv_empty[st]);
+                        __syncwarp();
                         if (j + 1 < it.nblk) {
-                            if (t == 0 && !(ok = mbar_wait(&k_full[st ^ 1], ((kv_iter + j + 1) >> 1) & 1)))
+                            if (t == 0 && !(ok = warp_wait(&k_full[st ^ 1], ((kv_iter + j + 1) >> 1) & 1)))
                                 break;
                             tc_fence_after();
                             issue_s(t, st ^ 1);
-                            if (t == 1 && j + 2 == it.nblk) umma_commit(q_empty);
+                            if (t == 1 && j + 2 == it.nblk && elect_one_sync()) umma_commit(q_empty);
+                            __syncwarp();
                         } else {
-                            umma_commit(&o_full[t]);
+                            if (elect_one_sync()) umma_commit(&o_full[t]);
+                            __syncwarp();
                         }
                     }
                 }
                 kv_iter += it.nblk;
             }
-            // Drain all MMAs of this thread before TMEM is released.
-            umma_commit(done);
-            mbar_wait(done, 0);
+            // Drain all MMAs of this warp before TMEM is released.
+            if (elect_one_sync()) umma_commit(done);
+            __syncwarp();
+            warp_wait(done, 0);
         }
     } else {
         // ---------------- softmax + output (warps 2..17) ----------------

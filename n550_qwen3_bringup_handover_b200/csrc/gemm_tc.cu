@@ -549,7 +549,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         if (++stage == STAGES) { stage = 0; phase ^= 1; }
                         continue;
                     }
-                    if (!mbar_wait(&empty[stage], phase ^ 1)) { ok = false; break; }
+                    if (!mbar_wait_sleep(&empty[stage], phase ^ 1)) { ok = false; break; }
                     if (PAIR) {
                         // both CTAs' bytes complete on the leader's barrier
                         const uint32_t cb = mapa_shared(smem_u32(&full[stage]), 0);
@@ -576,7 +576,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             long long first = issued > STAGES ? issued - STAGES : 0;
             if (!PAIR || rank == 0)
                 for (long long i = first; i < issued; i++)
-                    if (!mbar_wait(&full[i % STAGES], (uint32_t)((i / STAGES) & 1))) break;
+                    if (!mbar_wait_sleep(&full[i % STAGES], (uint32_t)((i / STAGES) & 1))) break;
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
@@ -591,12 +591,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             for (int u = u0; u < total && ok; u += ustep) {
                 const int sk = u % ksplit;
                 const int kt0 = sk * kt_per, kt1 = min(num_k, kt0 + kt_per);
-                if (!(PAIR ? mbar_wait_cluster(&tempty[ab], aphase ^ 1) : mbar_wait(&tempty[ab], aphase ^ 1)))
+                if (!(PAIR ? mbar_wait_cluster(&tempty[ab], aphase ^ 1) : mbar_wait_sleep(&tempty[ab], aphase ^ 1)))
                     break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(ab * BN);
                 for (int kt = kt0; kt < kt1; kt++) {
-                    if (!mbar_wait(&full[stage], phase)) { ok = false; break; }
+                    if (!mbar_wait_sleep(&full[stage], phase)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(base + stage * Cfg::STAGE_BYTES);
                     const uint32_t b0 = a0 + Cfg::A_BYTES;
@@ -623,7 +623,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             // Drain all MMAs of this thread before TMEM is released.
             if (PAIR) umma_commit_pair_mc(done, 1);
             else umma_commit(done);
-            mbar_wait(done, 0);
+            mbar_wait_sleep(done, 0);
         }
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
@@ -637,7 +637,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
         for (int u = u0; u < total; u += ustep) {
             const int t = u / ksplit, sk = u - t * ksplit;
             const int mb = m_fast ? t % num_m : t / num_n, nb = m_fast ? t / num_m : t % num_n;
-            if (!mbar_wait(&tfull[ab], aphase)) break;
+            if (!mbar_wait_sleep(&tfull[ab], aphase)) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
             const int row0 = mb * BMT + rank * BM + q * 32;   // first row of this warp's quarter
