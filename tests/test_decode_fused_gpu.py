@@ -1,4 +1,4 @@
-"""The persistent few-token decode kernel (n550_qwen3_fused_decode, default on)
+"""The persistent few-token decode kernel (n550_qwen3_fused_decode, default off)
 against the per-layer kernel sequence it replaces and against the reference.
 
 * 1-4 sequences at contexts from 5 to 2047 positions (one to eight attention
@@ -67,7 +67,7 @@ def test_fused_decode_matches_layer_kernels(cuda, lens):
         fused = two_steps(m, toks, lens, True)
         plain = two_steps(m, toks, lens, False)
     finally:
-        n5.lib().n550_qwen3_fused_decode(1)
+        n5.lib().n550_qwen3_fused_decode(0)
         m.close()
     assert n5.device_status() == n5.OK
     (f0, fi0), (f1, fi1) = fused
@@ -87,6 +87,7 @@ def test_fused_decode_vs_reference(cuda):
     ref = oracle.RefModel(blob, "scalar") if oracle.ref_available("scalar") else \
         oracle.OracleModel(blob, max_seq=64, gemm_kind=oracle.GEMM_SCALAR)
     rl = ref.forward_batch(prompt, 0)
+    n5.check(n5.lib().n550_qwen3_fused_decode(1))
     m = n5.Model(seed=0, max_seqs=1, max_len=64, max_tokens=64)
     try:
         nx = torch.empty(1, dtype=torch.int32, device="cuda")
@@ -105,6 +106,7 @@ def test_fused_decode_vs_reference(cuda):
             assert same_choice(int(nx.item()), want)
             tok = int(oracle.argmax(want))
     finally:
+        n5.lib().n550_qwen3_fused_decode(0)
         m.close()
     assert n5.device_status() == n5.OK
 
@@ -128,7 +130,7 @@ def test_fused_decode_graph_loop_matches_layer_kernels(cuda, S):
             ids[fused] = out.cpu().numpy()
             m.close()
     finally:
-        n5.lib().n550_qwen3_fused_decode(1)
+        n5.lib().n550_qwen3_fused_decode(0)
     assert n5.device_status() == n5.OK
     # identical unless a near tie parts the runs; then they may differ from there on
     agree = (ids[1] == ids[0]).all(axis=1)
