@@ -269,9 +269,10 @@ size_t n550_attention_decode_workspace(int n_seqs, int max_len);
 int n550_device_status(void);
 
 /* Health check of the failure path: one warp waits `cycles` SM clock cycles
- * (1 .. 2e9) on an mbarrier that nothing arrives on, with the library's
- * bounded wait; the wait gives up, records N550_ERR_TIMEOUT in the device
- * status word and the kernel returns, leaving the context usable. Enqueued
+ * (1 .. 2e9) on an mbarrier that nothing arrives on, with both of the
+ * library's bounded waits in turn (the polling one and the one whose tries
+ * sleep); each gives up, records N550_ERR_TIMEOUT in the device status word
+ * and the kernel returns, leaving the context usable. Enqueued
  * on `stream`; read the result with n550_device_status(). No counterpart in
  * the reference. */
 int n550_check_wait_expiry(void *stream, long long cycles);

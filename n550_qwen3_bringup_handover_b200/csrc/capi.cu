@@ -223,9 +223,10 @@ uint16_t *noalloc_stage() {
     return g_noalloc_ptr[dev];
 }
 
-// One warp waits on an mbarrier that nothing arrives on, for at most `cycles`:
-// the expiry path of every bounded wait in the library (status word set to
-// N550_ERR_TIMEOUT, kernel returns).
+// One warp waits on an mbarrier that nothing arrives on, for at most `cycles`,
+// first polling (mbar_wait) and then with suspended tries (mbar_wait_sleep, the
+// tensor-core GEMM's waits): the expiry path of every bounded wait in the
+// library (status word set to N550_ERR_TIMEOUT, kernel returns).
 __global__ void wait_expiry_kernel(long long cycles) {
     __shared__ __align__(8) uint64_t bar;
     if (threadIdx.x == 0) {
@@ -234,6 +235,7 @@ __global__ void wait_expiry_kernel(long long cycles) {
     }
     __syncwarp();
     mbar_wait(&bar, 0, cycles);
+    mbar_wait_sleep(&bar, 0, cycles);
 }
 
 }  // namespace

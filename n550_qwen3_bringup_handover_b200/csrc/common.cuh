@@ -176,11 +176,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, long l
 // spend issue slots and power the MMAs could use (measured on B200, 64 x 512
 // prefill step: 32.50 -> 31.84 ms median); latency-critical waits keep
 // mbar_wait.
-__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, long long limit = kWaitCycles) {
     if (mbar_try_wait_sleep(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait_sleep(bar, parity)) {
-        if (clock64() - t0 > kWaitCycles) { report_timeout(); return false; }
+        if (clock64() - t0 > limit) { report_timeout(); return false; }
     }
     return true;
 }

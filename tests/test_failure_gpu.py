@@ -15,11 +15,15 @@ pytestmark = pytest.mark.gpu
 
 
 def test_expired_wait_reports_timeout_and_context_survives(cuda):
+    import time
     import torch
     L = n5.lib()
     assert n5.device_status() == n5.OK
+    t0 = time.perf_counter()
+    # a polling and a sleeping wait, 4M cycles (~2 ms) each
     n5.check(L.n550_check_wait_expiry(n5.stream_ptr(), 4_000_000), "n550_check_wait_expiry")
     assert n5.device_status() == n5.ERR_TIMEOUT
+    assert time.perf_counter() - t0 < 0.5           # both waits gave up near their limit
     assert n5.device_status() == n5.OK              # read once, then cleared
     # the context still runs kernels correctly: a GEMM against binary64
     M, K, N = 64, 1024, 2048
