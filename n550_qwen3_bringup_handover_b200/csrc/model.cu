@@ -376,7 +376,13 @@ template <bool PRE_W>
 __global__ void __launch_bounds__(256)
 norm_rows_bf16_kernel(uint16_t *__restrict__ out, const float *__restrict__ x,
                       const uint16_t *__restrict__ w, int T) {
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    // A prefill's rows are taken last to first: the residual GEMM before this
+    // kernel wrote the last row blocks last, so those are still in L2, and
+    // the GEMM after it reads the first rows first, which this order writes
+    // last (measured on B200, 64 x 512 prefill: 2.30 -> 2.20 ms of norms per
+    // step; the same bits either way)
+    const int idx = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int row = PRE_W ? idx : (int)gridDim.x * 8 - 1 - idx;
     const int lane = threadIdx.x & 31;
     const uint2 *wr = (const uint2 *)w;
     uint2 wv[8];
