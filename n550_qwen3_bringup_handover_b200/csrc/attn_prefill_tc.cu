@@ -97,7 +97,7 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
 }
 
 // Work item k (longest first): q block n_qblocks - 1 - k / (8 n_seqs), then
-// KV head k % 8 of sequence (k % (8 n_seqs)) / 8.
+// KV head k % 8 of sequence n_seqs - 1 - (k % (8 n_seqs)) / 8.
 struct Item {
     int s, kvh, q0, nblk, plane;
 };
@@ -107,7 +107,10 @@ __device__ __forceinline__ Item decode_item(const PfParams &p, int k, bool with_
     const int per_q = NKV * p.n_seqs;
     const int qb = p.n_qblocks - 1 - k / per_q;
     const int rest = k % per_q;
-    it.s = rest / NKV;
+    // last sequences first within a query block: the q/k/v GEMM wrote their
+    // rows last, so they are still in L2 (attention 4.71 -> 4.60 ms per 64 x
+    // 512-token prefill step on B200)
+    it.s = p.n_seqs - 1 - rest / NKV;
     it.kvh = rest % NKV;
     it.q0 = qb * BQ;
     const int q_last = min(p.L, it.q0 + BQ) - 1;
