@@ -229,6 +229,52 @@ gemv_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict_
     }
 }
 
+// Wide few-row GEMV with K = 1024 (the lm_head: 151,936 columns, 311 MB of
+// weights, an HBM stream): each warp takes two adjacent columns, so 8
+// 16-byte loads per lane are in flight before the dependency wait, and the
+// block keeps a 64-register budget (4 resident blocks per SM), enough bytes
+// in flight to stream at the copy rate. Per column the loads, FMA order and
+// reduction are gemv_kernel's, so the results are the same bits.
+template <int MM, int EPI>
+__global__ void __launch_bounds__(GV_WARPS * 32, 4)
+gemv_wide_kernel(const uint16_t *__restrict__ a, int lda, const uint16_t *__restrict__ b, int ldb,
+                 void *c, int ldc, int N) {
+    constexpr int K = 1024;
+    const int lane = threadIdx.x & 31;
+    const int n0 = 2 * (blockIdx.x * GV_WARPS + (threadIdx.x >> 5));
+    uint4 bq[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const int n = n0 + j;
+        gv_load_step(bq[j], b + (size_t)(n < N ? n : 0) * ldb, n < N ? lane * 8 : K, K);
+    }
+    dep_wait();
+    dep_launch();
+    if (n0 >= N) return;
+    float acc[2][MM];
+#pragma unroll
+    for (int j = 0; j < 2; j++)
+#pragma unroll
+        for (int m = 0; m < MM; m++) acc[j][m] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 2; j++) gv_consume<MM>(bq[j], a, lda, lane * 8, K, acc[j]);
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+#pragma unroll
+        for (int m = 0; m < MM; m++) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[j][m] += __shfl_xor_sync(0xFFFFFFFFu, acc[j][m], o);
+        }
+        const int n = n0 + j;
+        if (lane < MM && n < N) {
+            float v = acc[j][0];
+#pragma unroll
+            for (int m = 1; m < MM; m++) if (lane == m) v = acc[j][m];
+            epi_store<EPI>(c, ldc, lane, n, v);
+        }
+    }
+}
+
 // Rows of 2048-4096 elements (the o and down projections) with the K loop
 // split over KS warps per output column, one 1024-element step each, partial
 // sums added in step order: 4x the warps of gemv_kernel in flight for the
@@ -419,6 +465,19 @@ int gemv_dispatch(cudaStream_t st, int epi, const uint16_t *a, int lda, const ui
             else if (epi == TC_EPI_RESID_F32) e = go(gemv_ksplit_kernel<MM, TC_EPI_RESID_F32, 4>);
             else return N550_ERR_ARG;
         }
+        N550_CUDA_TRY(e);
+        return N550_OK;
+    }
+    if (K == 1024 && N >= 65536) {          // the lm_head: an HBM stream
+        const int grid = (N + 2 * GV_WARPS - 1) / (2 * GV_WARPS);
+        auto gw = [&](auto kernel) {
+            return launch_k(kernel, grid, GV_WARPS * 32, 0, st, a, lda, b, ldb, c, ldc, N);
+        };
+        cudaError_t e;
+        if (epi == TC_EPI_F32) e = gw(gemv_wide_kernel<MM, TC_EPI_F32>);
+        else if (epi == TC_EPI_BF16) e = gw(gemv_wide_kernel<MM, TC_EPI_BF16>);
+        else if (epi == TC_EPI_RESID_F32) e = gw(gemv_wide_kernel<MM, TC_EPI_RESID_F32>);
+        else return N550_ERR_ARG;
         N550_CUDA_TRY(e);
         return N550_OK;
     }
